@@ -1,0 +1,366 @@
+"""Benchmark: decode tokens/s of the 42-layer Q4_K_M Gemma-style model on B200
+(bs1 after a 512-token prompt, and 64-sequence batched decode), plus the Q4_K GEMV's
+HBM bandwidth, against the reference's CPU stage path timed on this host.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N ... bench.py --gpus N   (one pipeline stage per GPU)
+
+One JSON line on rank 0.  `value` = bs1 greedy decode tokens/s (whole job); `bs64` = batched
+decode tokens/s; `roofline` = the Q4_K GEMV (10240 x 2560, one token, cold L2) against the
+measured HBM copy bandwidth; `e2e` = bs1 tokens/s through the stage C ABI with host buffers.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "compute-sharding_b200"))
+
+METRIC = "decode tokens/s (bs1 and bs64) 42-layer Q4_K model at 1/2/4/8 B200; GEMV HBM GB/s"
+N_LAYERS, HIDDEN, VOCAB = 42, 2560, 262144
+PROMPT = 512
+# algorithmic bytes of one Q4_K GEMV 10240 x 2560 with f32 x and y (14,745,600 + 10,240 + 40,960)
+GEMV_BYTES = 10240 * 10 * 144 + 2560 * 4 + 10240 * 4
+# algorithmic weight bytes of one decode token through all 42 layers + tied fp16 logits
+LAYER_WEIGHT_BYTES = 60_518_400
+EMBD_BYTES = VOCAB * HIDDEN * 2
+
+
+def env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
+        except Exception:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        mx = float(rows[0][2])
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- reference arm (CPU)
+def cpu_decode_sample(n_steps: int, prompt_len: int = 8):
+    """The reference's CPU stage path restated (oracle, kind 'port') on all host cores:
+    42-layer greedy decode tokens/s.  Returns (tokens/s, threads, description)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import stage_oracle as so
+    threads = os.cpu_count() or 1
+    os.environ["ORACLE_THREADS"] = str(threads)
+    spec = so.ModelSpec()
+    st = so.OracleStage(so.synth_stage(spec, 0, N_LAYERS - 1, True, True),
+                        so.Layout("synthetic-gemma", "full", 0, N_LAYERS - 1, True, True), rope_theta=10000.0)
+    prompt = so.synth_tokens(spec.seed, "bench.prompt", prompt_len, spec.vocab)
+    h = st.begin_token_ids("r", prompt)
+    tok = st.sample_tail(h[-1])[0]
+    t0 = time.perf_counter()
+    for _ in range(n_steps):
+        h = st.begin_token_ids("r", [tok])
+        tok = st.sample_tail(h[-1])[0]
+    dt = time.perf_counter() - t0
+    desc = (f"{n_steps} greedy decode steps of the 42-layer model (d_model 2560, vocab 262144) after a "
+            f"{prompt_len}-token prompt, f32 KV, {threads} threads (row-parallel like rayon)")
+    return n_steps / dt, threads, desc
+
+
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 8))
+    # warm-up steps are part of the same sampled loop (first-touch of weights); time `steps` after it
+    tps, threads, desc = cpu_decode_sample(steps)
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "42-layer Gemma-style Q4_K_M decode, batch 1", "layers": N_LAYERS,
+                       "d_model": HIDDEN, "vocab": VOCAB},
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+def gemv_roofline(sf, torch, hbm_peak):
+    """Config-1 GEMV: Q4_K 10240 x 2560, one token, cycling > 2 x L2 of weight copies."""
+    dev = torch.device("cuda")
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size if hasattr(torch.cuda.get_device_properties(0), "L2_cache_size") else 126 << 20
+    wbytes = 10240 * 10 * 144
+    copies = int(np.ceil(2 * l2 / wbytes)) + 2
+    ws = [sf.synth_tensor(sf.Q4_K, 1, f"gemv.{i}", 10240, 2560, 0.02) for i in range(copies)]
+    x = torch.randn(1, 2560, device=dev)
+    y = torch.empty(1, 10240, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    lib = sf.lib
+
+    def run(i):
+        lib.sfc_matmul(sf.Q4_K, ws[i % copies].data_ptr(), 10240, 2560, x.data_ptr(), 1, y.data_ptr(), st)
+
+    for i in range(3 * copies):
+        run(i)
+    torch.cuda.synchronize()
+    reps = 30 * copies
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(reps):
+        run(i)
+    e1.record()
+    torch.cuda.synchronize()
+    dur_s = e0.elapsed_time(e1) / 1e3 / reps
+    achieved = GEMV_BYTES / dur_s / 1e9
+    return {"kernel": "qgemv_kernel<Q4_K,1,1> (10240x2560, 1 token, cold L2)", "bound": "hbm",
+            "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "us_per_launch": dur_s * 1e6, "bytes_per_launch": GEMV_BYTES, "traffic": None}
+
+
+def run_single(args):
+    import torch
+    import stagefwd as sf
+    torch.cuda.set_device(0)
+    hbm_peak, peak_kind = peaks()
+    shape = sf.ModelShape()  # 42 layers, Q4_K_M, vocab 262144, seed fixed
+    max_ctx = 4096
+    be = sf.CudaStageBackend(synthetic=shape, rope_theta=10000.0, max_ctx=max_ctx, max_sessions=66,
+                             max_batch_tokens=512).load_layout("synthetic-gemma", "full", 0, N_LAYERS - 1, True, True)
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, VOCAB, PROMPT).astype(np.uint32)
+
+    # ---- bs1 device-timed decode (one captured graph per token)
+    be.generate_greedy("warm", prompt, max(args.warmup, 3) + 1)
+    be.clear_decode_session("warm")
+    with ClockSampler(0) as clk:
+        toks = be.generate_greedy("bs1", prompt, args.steps + 1)
+        prof = be.last_profile()
+    be.clear_decode_session("bs1")
+    bs1_s = prof.total_us / 1e6
+    bs1_tps = args.steps / bs1_s
+    launches = int(prof.kernels)  # kernels recorded in the decode graph x graph replays
+
+    # ---- bs1 end-to-end through the stage C ABI (host buffers every step)
+    h = be.begin_token_ids("e2e", prompt)
+    tok, _ = be.sample_tail(h)
+    for _ in range(args.warmup):
+        h = be.begin_token_ids("e2e", [tok])
+        tok, _ = be.sample_tail(h)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        h = be.begin_token_ids("e2e", [tok])
+        tok, _ = be.sample_tail(h)
+    e2e_s = time.perf_counter() - t0
+    be.clear_decode_session("e2e")
+
+    # ---- bs64 batched decode, contexts 512..3584 (seeded), one token per sequence per step
+    ctx = rng.integers(512, 3585, 64)
+    names = [f"b{i}" for i in range(64)]
+    for i, n in enumerate(names):
+        be.fill_session_synthetic(n, int(ctx[i]), seed=100 + i)
+    dev = torch.device("cuda")
+    ids = torch.from_numpy(rng.integers(0, VOCAB, 64).astype(np.int32)).to(dev)
+    out = torch.empty(64, HIDDEN, device=dev)
+    tk = torch.empty(64, dtype=torch.int64, device=dev)
+    sc = torch.empty(64, dtype=torch.float32, device=dev)
+
+    def bs64_step():
+        be.forward_dev(names, [1] * 64, ids_dev=ids, out_dev=out, append=True)
+        be.sample_dev(out, tk, sc)
+        ids.copy_(tk.to(torch.int32))
+
+    for _ in range(max(args.warmup, 3)):
+        bs64_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    bsteps = max(2, args.steps // 8)
+    e0.record()
+    for _ in range(bsteps):
+        bs64_step()
+    e1.record()
+    torch.cuda.synchronize()
+    bs64_s = e0.elapsed_time(e1) / 1e3
+    bs64_tps = 64 * bsteps / bs64_s
+    be.close()
+
+    roof = gemv_roofline(sf, torch, hbm_peak)
+    roof["peak_kind"] = peak_kind
+    prof_file = ROOT / "profiles" / "qgemv_q4k_10240x2560_traffic.json"
+    if prof_file.exists():
+        try:
+            roof["traffic"] = json.loads(prof_file.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            pass
+
+    cpu_tps, cores, desc = cpu_decode_sample(3)
+    token_bytes = N_LAYERS * LAYER_WEIGHT_BYTES + EMBD_BYTES
+    line = {
+        "metric": METRIC, "value": bs1_tps, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": bs1_s * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "42-layer Gemma-style Q4_K_M greedy decode, batch 1, after a 512-token prompt",
+                   "layers": N_LAYERS, "d_model": HIDDEN, "heads": "8q/4kv x 256", "ffn": 10240, "vocab": VOCAB,
+                   "prompt": PROMPT, "parallelism": "pp1", "kv": "fp16",
+                   "l2": "inputs larger than L2 (3.9 GB of weights read per token)"},
+        "bs1_step_bandwidth_gbs": token_bytes / (bs1_s / args.steps) / 1e9,
+        "bs64": {"value": bs64_tps, "unit": "tokens/s", "steps": bsteps, "ms_per_step": bs64_s * 1e3 / bsteps,
+                 "workload": "64 sequences, contexts uniform 512..3584 (seeded synthetic KV), 1 token each per step"},
+        "gemv": {"value": roof["achieved"], "unit": "GB/s", "frac_of_hbm": roof["frac"]},
+        "e2e": {"value": args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 + HIDDEN * 4,
+                "d2h_bytes_per_step": HIDDEN * 4 + 8,
+                "path": "begin_token_ids + sample_tail through the C ABI with host buffers each token"},
+        "roofline": roof,
+        "cpu_baseline": {"value": cpu_tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_pipeline(args):
+    import torch
+    import torch.distributed as dist
+    import stagefwd as sf
+    from stagefwd.pipeline import CudaCompute, Pipeline, even_stage_split, make_groups
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    ranks = make_groups(rank, world)
+    start, end = even_stage_split(N_LAYERS, world)[rank]
+    be = sf.CudaStageBackend(synthetic=sf.ModelShape(), device=local, rope_theta=10000.0, max_ctx=4096,
+                             max_sessions=66, max_batch_tokens=512).load_layout(
+        "synthetic-gemma", f"stage-{rank}", start, end, ranks.is_head, ranks.is_tail)
+    dev = torch.device("cuda", local)
+    comp = CudaCompute(be, HIDDEN, 512, dev)
+    pipe = Pipeline(comp, ranks, HIDDEN, dev)
+    rng = np.random.default_rng(1234)
+    prompt = torch.from_numpy(rng.integers(0, VOCAB, PROMPT).astype(np.int64)).to(dev)
+
+    # bs1
+    pipe.generate("warm", prompt, max(args.warmup, 3))
+    dist.barrier()
+    torch.cuda.synchronize()
+    tok = pipe.step(["bs1"], [PROMPT], prompt, append=False)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            tok = pipe.step(["bs1"], [1], tok if tok is not None else torch.zeros(1, dtype=torch.int64, device=dev))
+        e1.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    bs1_s = float(t)
+
+    # bs64: 8 microbatches of 8 sequences
+    ctx = rng.integers(512, 3585, 64)
+    names = [f"b{i}" for i in range(64)]
+    for i, n in enumerate(names):
+        be.fill_session_synthetic(n, int(ctx[i]), seed=100 + i)
+    mbs = [names[8 * m: 8 * m + 8] for m in range(8)]
+    tokens = [torch.from_numpy(rng.integers(0, VOCAB, 8).astype(np.int64)).to(dev) for _ in range(8)]
+    pipe.decode_microbatched(mbs, tokens, max(args.warmup, 2))
+    torch.cuda.synchronize()
+    dist.barrier()
+    bsteps = max(2, args.steps // 8)
+    e0.record()
+    pipe.decode_microbatched(mbs, tokens, bsteps)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    bs64_s = float(t)
+    be.close()
+    if rank == 0:
+        line = {"metric": METRIC, "value": args.steps / bs1_s, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": bs1_s * 1e3 / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic",
+                "config": {"workload": "42-layer Gemma-style Q4_K_M greedy decode, batch 1, after a 512-token prompt",
+                           "layers": N_LAYERS, "d_model": HIDDEN, "vocab": VOCAB, "prompt": PROMPT,
+                           "parallelism": f"pp{world}", "split": even_stage_split(N_LAYERS, world),
+                           "handoff": "NCCL send/recv of f32 hidden rows", "kv": "fp16",
+                           "l2": "inputs larger than L2"},
+                "bs64": {"value": 64 * bsteps / bs64_s, "unit": "tokens/s", "steps": bsteps,
+                         "microbatches": "8 x 8 sequences"},
+                "e2e": None, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    _, world, _ = env_rank()
+    if world > 1:
+        run_pipeline(args)
+    else:
+        run_single(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,123 @@
+// kernels.h — host-side launchers for the sm_100a stage-forward kernels (internal API).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sfc {
+
+// ---- launch helpers
+inline int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// Number of kernels launched through launch_pdl by this process (graph captures count the
+// kernels they record).
+extern long long g_kernel_launches;
+
+// Launch with programmatic stream serialization so the kernel may begin (and start its
+// independent weight prefetch) while the previous kernel on the stream drains.
+template <class K, class... Args>
+cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  ++g_kernel_launches;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+unsigned *device_error_ptr();
+
+// ---- weights (gemv.cu)
+int device_row_bytes(int type, int64_t K);  // bytes per row in the device layout
+int gguf_row_bytes(int type, int64_t K);
+cudaError_t prepare_weights(int type, const void *gguf, int64_t rows, int64_t K, void *dst, cudaStream_t st);
+cudaError_t dequantize(int type, const void *w_gguf, int64_t n_rows, int64_t K, float *out, cudaStream_t st);
+// y[t*ldy + r] = sum_k W[r][k] x[t*K + k]; with w1 != null: GeGLU(W0 x, W1 x).
+cudaError_t gemv(int type, const void *w0, const void *w1, int64_t rows, int64_t K, const float *x, int64_t n_tok,
+                 float *y, int64_t ldy, cudaStream_t st);
+
+// ---- elementwise / norms / attention (ops.cu)
+// out[t] = rms_norm(x[t]) * w   (real_math.rs:30-47)
+cudaError_t rms_norm(const float *x, const float *w, int64_t n_tok, int dim, float eps, float *out, cudaStream_t st);
+// r = resid + (w_post ? rms_norm(a) * w_post : a); r *= *layer_scale (if given); resid = r;
+// if want_xn: xn = w_next ? rms_norm(r) * w_next : r.  (real_forward.rs:1690-1696, 1738-1786)
+cudaError_t add_norm(float *resid, const float *a, const float *w_post, const float *layer_scale, int want_xn,
+                     const float *w_next, float *xn, int64_t n_tok, int dim, float eps, cudaStream_t st);
+// embedding rows of an F16 / F32 / BF16 table scaled by sqrt(dim) (real_forward.rs:848-871);
+// ids are uint32 (ids64 = 0) or int64 (ids64 = 1); out-of-range ids set DEV_BAD_ARG.
+cudaError_t embed(int type, const void *table, int64_t vocab, int dim, const void *ids, int ids64, int64_t n_tok,
+                  float *out, unsigned *err, cudaStream_t st);
+
+struct AttnParams {
+  int n_heads, n_kv, head_dim;
+  int kv_f32;          // 0: fp16 cache, 1: f32 cache
+  int64_t max_ctx;     // positions per head in the cache
+  float eps;
+  float rope_theta;
+  int rotary_dim;
+  int proportional;
+  const float *rope_freqs;  // may be null: no RoPE (real_forward.rs:1616)
+  int n_freqs;
+  const float *q_norm, *k_norm;  // may be null
+  int window;          // <= 0: none
+};
+
+// One sequence of the current batch.  Its cache for a layer lives in slot `slot` of that
+// layer's KV region: K at base + slot*slot_stride, V at K + slot_stride/2, each laid out
+// [n_kv][max_ctx][head_dim] (head-major, so a head's keys are one contiguous run).
+struct SeqInfo {
+  int32_t slot;
+  int32_t pos0;   // positions already in the cache before this call
+  int32_t n_tok;  // tokens of this sequence in the current batch
+  int32_t tok0;   // first row of this sequence in the batch
+};
+struct KVLayer {
+  void *base;
+  int64_t slot_stride;  // elements per slot (K and V)
+};
+
+// q/k/v post-processing for a batch: per-head norms, RoPE, KV append (real_forward.rs:1583-1662).
+cudaError_t qkv_post(float *q, const float *k, const float *v, int q_ld, int kv_ld, KVLayer kv, const SeqInfo *seqs,
+                     const int32_t *tok_seq, int64_t n_tok, const AttnParams &p, cudaStream_t st);
+// causal GQA attention over the cache (real_math.rs:2697-2744); tree masks via parent links.
+size_t attention_scratch_bytes(int64_t n_tok, const AttnParams &p, int64_t max_keys);
+// tok_limit (nullable): per-token number of visible cache positions (default pos+1);
+// tok_mask (nullable): per-token bitmask over the batch's own positions of its sequence
+// (bit j = row tok0+j visible), used for tree-masked verification.
+cudaError_t attention(const float *q, float *out, KVLayer kv, const SeqInfo *seqs, const int32_t *tok_seq,
+                      const int32_t *tok_limit, const uint64_t *tok_mask, int64_t n_tok, int64_t max_keys,
+                      const AttnParams &p, void *scratch, size_t scratch_bytes, cudaStream_t st);
+
+// Decode-graph bookkeeping (see ops.cu).
+cudaError_t decode_advance(const int64_t *tok, int64_t *out_tokens, int32_t *step, SeqInfo *seqs, int n_seq,
+                           int64_t max_steps, cudaStream_t st);
+
+// ---- logits (logits.cu)
+// Tied / output projection + softcap + argmax (lowest index on ties) over rows of `w`.
+size_t logits_scratch_bytes(int64_t n_tok);
+cudaError_t logits_argmax(int type, const void *w, int64_t vocab, int dim, const float *h, int64_t n_tok, float cap,
+                          float *all_scores /*nullable [n_tok][vocab]*/, int64_t *argmax_idx, float *argmax_score,
+                          void *scratch, size_t scratch_bytes, cudaStream_t st);
+
+// ---- synthetic generators (synth.cu), same spec as the oracle
+cudaError_t synth_tensor(int type, uint64_t key, int64_t rows, int64_t K, float sigma, float mean, void *out,
+                         cudaStream_t st);
+uint64_t tensor_key(uint64_t seed, const char *name);
+uint64_t mix64_host(uint64_t key, uint64_t ctr);
+
+}  // namespace sfc

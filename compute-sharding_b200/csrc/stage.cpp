@@ -1,0 +1,1256 @@
+// stage.cpp — the stage backend behind the C ABI: packed-stage loading, KV sessions, the
+// Gemma-style layer loop, tail sampling and CUDA-graph greedy decode.
+//
+// Semantics follow RealGemmaBackend (crates/stage-forward-lab/src/real_forward.rs):
+//   load_layout            :2258-2363  config inference, rope_freqs, token_embd, tail tensors
+//   begin_token_sequence   :988-1121   head ingress, sessions
+//   forward_layer_seq      :1483-1793  the per-layer math (run by the kernels in *.cu)
+//   continue_forward_inner :2054-2254
+//   sample_hidden_state_with_trace :904-986
+// Packed stage files follow PackedStageIndex / StageTensorStore (crates/stage-forward-lab/src/
+// lib.rs:2908-2927, :3645-3806).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "capi_common.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sfc {
+
+// ------------------------------------------------------------------ minimal JSON reader
+struct Json {
+  enum Kind { Null, Bool, Num, Str, Arr, Obj } kind = Null;
+  double num = 0;
+  bool b = false;
+  std::string str;
+  std::vector<Json> arr;
+  std::vector<std::pair<std::string, Json>> obj;
+  const Json *get(const char *k) const {
+    for (auto &kv : obj)
+      if (kv.first == k) return &kv.second;
+    return nullptr;
+  }
+};
+
+struct JsonParser {
+  const char *p, *e;
+  bool ok = true;
+  void ws() {
+    while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
+  }
+  bool lit(const char *s) {
+    size_t n = strlen(s);
+    if (size_t(e - p) >= n && !memcmp(p, s, n)) {
+      p += n;
+      return true;
+    }
+    return false;
+  }
+  std::string string() {
+    std::string out;
+    ++p;  // opening quote
+    while (p < e && *p != '"') {
+      if (*p == '\\' && p + 1 < e) {
+        ++p;
+        switch (*p) {
+          case 'n': out += '\n'; break;
+          case 't': out += '\t'; break;
+          case 'r': out += '\r'; break;
+          case 'b': out += '\b'; break;
+          case 'f': out += '\f'; break;
+          case 'u': {  // keep ASCII, replace others
+            if (e - p >= 5) {
+              unsigned v = unsigned(strtoul(std::string(p + 1, p + 5).c_str(), nullptr, 16));
+              out += v < 128 ? char(v) : '?';
+              p += 4;
+            }
+            break;
+          }
+          default: out += *p;
+        }
+        ++p;
+      } else {
+        out += *p++;
+      }
+    }
+    if (p >= e) ok = false;
+    ++p;
+    return out;
+  }
+  Json value() {
+    Json j;
+    ws();
+    if (p >= e) {
+      ok = false;
+      return j;
+    }
+    if (*p == '{') {
+      j.kind = Json::Obj;
+      ++p;
+      ws();
+      if (p < e && *p == '}') {
+        ++p;
+        return j;
+      }
+      while (ok) {
+        ws();
+        if (p >= e || *p != '"') {
+          ok = false;
+          break;
+        }
+        std::string k = string();
+        ws();
+        if (p >= e || *p != ':') {
+          ok = false;
+          break;
+        }
+        ++p;
+        j.obj.emplace_back(k, value());
+        ws();
+        if (p < e && *p == ',') {
+          ++p;
+          continue;
+        }
+        if (p < e && *p == '}') {
+          ++p;
+          break;
+        }
+        ok = false;
+      }
+    } else if (*p == '[') {
+      j.kind = Json::Arr;
+      ++p;
+      ws();
+      if (p < e && *p == ']') {
+        ++p;
+        return j;
+      }
+      while (ok) {
+        j.arr.push_back(value());
+        ws();
+        if (p < e && *p == ',') {
+          ++p;
+          continue;
+        }
+        if (p < e && *p == ']') {
+          ++p;
+          break;
+        }
+        ok = false;
+      }
+    } else if (*p == '"') {
+      j.kind = Json::Str;
+      j.str = string();
+    } else if (lit("true")) {
+      j.kind = Json::Bool;
+      j.b = true;
+    } else if (lit("false")) {
+      j.kind = Json::Bool;
+    } else if (lit("null")) {
+      j.kind = Json::Null;
+    } else {
+      char *end = nullptr;
+      j.num = strtod(p, &end);
+      if (end == p) ok = false;
+      j.kind = Json::Num;
+      p = end;
+    }
+    return j;
+  }
+};
+
+static bool read_file(const std::string &path, std::string &out) {
+  FILE *f = fopen(path.c_str(), "rb");
+  if (!f) return false;
+  fseek(f, 0, SEEK_END);
+  long n = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  out.resize(size_t(n));
+  size_t got = n > 0 ? fread(&out[0], 1, size_t(n), f) : 0;
+  fclose(f);
+  return got == size_t(n);
+}
+
+// ------------------------------------------------------------------ stage
+struct DevTensor {
+  std::string name;
+  int type = 0;
+  std::vector<int64_t> dims;
+  int64_t in_dim = 0, rows = 1;
+  void *dev = nullptr;  // device layout
+};
+
+struct Layer {
+  int index = 0;
+  DevTensor *attn_norm = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *q_norm = nullptr, *k_norm = nullptr,
+            *o = nullptr, *post_attn = nullptr, *ffn_norm = nullptr, *gate = nullptr, *up = nullptr,
+            *down = nullptr, *post_ffw = nullptr, *scale = nullptr;
+};
+
+struct Session {
+  int slot = -1;
+  int64_t len = 0;
+};
+
+// Pinned host staging ring for per-call tables (safe reuse via events).
+struct PinnedRing {
+  static constexpr int N = 8;
+  void *buf[N] = {};
+  cudaEvent_t ev[N] = {};
+  size_t bytes = 0;
+  int next = 0;
+  int init(size_t b) {
+    bytes = b;
+    for (int i = 0; i < N; ++i) {
+      SFC_CUDA(cudaMallocHost(&buf[i], b));
+      SFC_CUDA(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+    }
+    return SFC_OK;
+  }
+  void *acquire(int *idx) {
+    int i = next;
+    next = (next + 1) % N;
+    cudaEventSynchronize(ev[i]);
+    *idx = i;
+    return buf[i];
+  }
+  void release(int i, cudaStream_t st) { cudaEventRecord(ev[i], st); }
+  void destroy() {
+    for (int i = 0; i < N; ++i) {
+      if (ev[i]) cudaEventDestroy(ev[i]);
+      if (buf[i]) cudaFreeHost(buf[i]);
+    }
+  }
+};
+
+}  // namespace sfc
+
+using namespace sfc;
+
+struct sfc_stage {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string model_id, stage_id;
+  uint32_t start_layer = 0, end_layer = 0;
+  bool is_head = false, is_tail = false;
+  // options
+  float theta = 1e6f, softcap = 30.f, eps = 1e-6f;
+  int kv_f32 = 0, max_ctx = 4096, max_sessions = 64, max_batch = 512;
+  // config
+  int hidden = 0, n_heads = 0, n_kv = 0, head_dim = 0, ffn = 0, q_dim = 0, k_dim = 0;
+  int64_t vocab = 0;
+  // weights
+  std::vector<std::unique_ptr<DevTensor>> tensors;
+  std::vector<Layer> layers;
+  DevTensor *token_embd = nullptr, *output_norm = nullptr, *logits_w = nullptr, *rope_freqs = nullptr;
+  void *weight_arena = nullptr;
+  int64_t weight_bytes = 0;
+  // KV cache: [n_layers][max_sessions][K|V][n_kv][max_ctx][head_dim]
+  void *kv_arena = nullptr;
+  int64_t kv_slot_stride = 0;  // elements
+  int64_t kv_bytes = 0;
+  // activations
+  float *resid = nullptr, *xn = nullptr, *proj = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+        *act = nullptr, *hn = nullptr, *score_dev = nullptr;
+  uint32_t *ids_dev = nullptr;
+  int64_t *tok_dev = nullptr, *gen_tokens_dev = nullptr;
+  int32_t *tok_seq_dev = nullptr, *step_dev = nullptr;
+  SeqInfo *seq_dev = nullptr;
+  void *scratch = nullptr;
+  size_t attn_scratch = 0, logit_scratch = 0;
+  int64_t gen_capacity = 0;
+  PinnedRing ring;
+  // sessions
+  std::unordered_map<std::string, Session> sessions;
+  std::vector<char> slot_used;
+  // graph for greedy decode
+  cudaGraphExec_t decode_graph = nullptr;
+  long long graph_kernels = 0;  // kernels per captured decode step
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  sfc_profile profile = {};
+};
+
+namespace {
+
+const char *type_name(int t) {
+  switch (t) {
+    case T_F32: return "F32";
+    case T_F16: return "F16";
+    case T_Q4_K: return "Q4_K";
+    case T_Q5_K: return "Q5_K";
+    case T_Q6_K: return "Q6_K";
+    case T_BF16: return "BF16";
+  }
+  return "UNKNOWN";
+}
+
+int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+// Which layer slot a tensor name fills (lib.rs:4287-4335 build_operator_view).
+DevTensor **layer_field(Layer &L, const std::string &name) {
+  struct {
+    const char *key;
+    DevTensor *Layer::*f;
+  } map[] = {{".attn_q.weight", &Layer::q},
+             {".attn_k.weight", &Layer::k},
+             {".attn_v.weight", &Layer::v},
+             {".attn_output.weight", &Layer::o},
+             {".attn_norm.weight", &Layer::attn_norm},
+             {".attn_q_norm.weight", &Layer::q_norm},
+             {".attn_k_norm.weight", &Layer::k_norm},
+             {".ffn_up.weight", &Layer::up},
+             {".ffn_down.weight", &Layer::down},
+             {".ffn_gate.weight", &Layer::gate},
+             {".ffn_norm.weight", &Layer::ffn_norm},
+             {".post_attention_norm.weight", &Layer::post_attn},
+             {".post_ffw_norm.weight", &Layer::post_ffw},
+             {".layer_output_scale.weight", &Layer::scale}};
+  for (auto &m : map)
+    if (name.find(m.key) != std::string::npos) return &(L.*(m.f));
+  return nullptr;
+}
+
+// Parse "blk.<n>." prefix; -1 when the name is not a layer tensor (lib.rs:4265-4285).
+int layer_of(const std::string &name) {
+  if (name.compare(0, 4, "blk.") != 0) return -1;
+  size_t dot = name.find('.', 4);
+  if (dot == std::string::npos || dot == 4) return -1;
+  int v = 0;
+  for (size_t i = 4; i < dot; ++i) {
+    if (name[i] < '0' || name[i] > '9') return -1;
+    v = v * 10 + (name[i] - '0');
+  }
+  return v;
+}
+
+struct HostTensor {
+  std::string name;
+  int type;
+  std::vector<int64_t> dims;
+  const uint8_t *data;  // GGUF bytes (null for synthetic)
+  int64_t bytes;
+  // synthetic generation parameters
+  uint64_t key = 0;
+  float sigma = 0, mean = 0;
+  bool synthetic = false;
+  bool ones = false;
+};
+
+int64_t gguf_tensor_bytes(int type, const std::vector<int64_t> &dims) {
+  if (dims.empty()) return -1;
+  int64_t rows = 1;
+  for (size_t i = 1; i < dims.size(); ++i) rows *= dims[i];
+  const int rb = gguf_row_bytes(type, dims[0]);
+  return rb < 0 ? -1 : rb * rows;
+}
+
+int64_t device_tensor_bytes(int type, const std::vector<int64_t> &dims) {
+  int64_t rows = 1;
+  for (size_t i = 1; i < dims.size(); ++i) rows *= dims[i];
+  const int rb = device_row_bytes(type, dims[0]);
+  return rb < 0 ? -1 : rb * rows;
+}
+
+int apply_options(sfc_stage *h, const sfc_options *o) {
+  if (o) {
+    if (o->rope_theta > 0) h->theta = o->rope_theta;
+    if (o->logit_softcap > 0) h->softcap = o->logit_softcap;
+    if (o->logit_softcap < 0) h->softcap = 0.f;
+    if (o->eps > 0) h->eps = o->eps;
+    h->kv_f32 = o->kv_f32 ? 1 : 0;
+    if (o->max_ctx > 0) h->max_ctx = o->max_ctx;
+    if (o->max_sessions > 0) h->max_sessions = o->max_sessions;
+    if (o->max_batch_tokens > 0) h->max_batch = o->max_batch_tokens;
+  }
+  SFC_REQUIRE(h->max_ctx <= (1 << 24), "max_ctx too large");
+  SFC_REQUIRE(h->max_batch <= (1 << 16), "max_batch_tokens too large");
+  return SFC_OK;
+}
+
+// Builds device tensors, infers the config, allocates caches and buffers.
+int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
+  // classification + config inference (real_forward.rs:2258-2283)
+  std::map<int, Layer> layer_map;
+  std::vector<std::pair<HostTensor *, DevTensor *>> uploads;
+  int64_t arena = 0;
+  for (auto &ht : hts) {
+    SFC_REQUIRE(!ht.dims.empty(), "tensor %s has no dimensions", ht.name.c_str());
+    const bool supported = ht.type == T_F32 || ht.type == T_F16 || ht.type == T_BF16 || ht.type == T_Q4_K ||
+                           ht.type == T_Q6_K;
+    SFC_REQUIRE(supported, "tensor %s has unsupported type %s (%d)", ht.name.c_str(), type_name(ht.type), ht.type);
+    const int64_t gb = gguf_tensor_bytes(ht.type, ht.dims);
+    SFC_REQUIRE(gb >= 0, "tensor %s: dims incompatible with %s", ht.name.c_str(), type_name(ht.type));
+    SFC_REQUIRE(ht.synthetic || ht.ones || gb == ht.bytes, "tensor %s: byte_len %lld != %lld implied by dims",
+                ht.name.c_str(), (long long)ht.bytes, (long long)gb);
+    auto dt = std::make_unique<DevTensor>();
+    dt->name = ht.name;
+    dt->type = ht.type;
+    dt->dims = ht.dims;
+    dt->in_dim = ht.dims[0];
+    dt->rows = 1;
+    for (size_t i = 1; i < ht.dims.size(); ++i) dt->rows *= ht.dims[i];
+    arena += align256(device_tensor_bytes(ht.type, ht.dims) + 16);
+    DevTensor *raw = dt.get();
+    h->tensors.push_back(std::move(dt));
+    uploads.emplace_back(&ht, raw);
+    const int li = layer_of(ht.name);
+    if (li >= 0) {
+      Layer &L = layer_map[li];
+      L.index = li;
+      DevTensor **f = layer_field(L, ht.name);
+      if (f) *f = raw;  // unknown layer tensors are ignored, as the reference does
+    } else if (ht.name == "token_embd.weight") {
+      h->token_embd = raw;
+    } else if (ht.name == "rope_freqs.weight") {
+      h->rope_freqs = raw;
+    } else if (ht.name == "output_norm.weight") {
+      h->output_norm = raw;
+    } else if (ht.name == "output.weight") {
+      h->logits_w = raw;
+    }
+  }
+  for (auto &kv : layer_map) h->layers.push_back(kv.second);
+  SFC_REQUIRE(!h->layers.empty() || h->is_tail, "stage has no layer tensors");
+  if (!h->logits_w) h->logits_w = h->token_embd;  // tied embedding (real_forward.rs:803-816)
+
+  // norms must be F32 (real_forward.rs:478-488)
+  for (auto &L : h->layers)
+    for (DevTensor *t : {L.attn_norm, L.q_norm, L.k_norm, L.post_attn, L.ffn_norm, L.post_ffw, L.scale})
+      SFC_REQUIRE(!t || t->type == T_F32, "Expected F32 tensor for %s, got type %d", t->name.c_str(), t->type);
+  if (h->rope_freqs) SFC_REQUIRE(h->rope_freqs->type == T_F32, "rope_freqs.weight must be F32");
+  if (h->output_norm) SFC_REQUIRE(h->output_norm->type == T_F32, "output_norm.weight must be F32");
+
+  if (!h->layers.empty()) {
+    const Layer &L0 = h->layers.front();
+    SFC_REQUIRE(L0.q && L0.k && L0.v && L0.o, "layer %d lacks attention projections", L0.index);
+    SFC_REQUIRE(L0.gate && L0.up && L0.down, "layer %d lacks FFN projections", L0.index);
+    h->hidden = int(L0.q->dims[0]);
+    h->q_dim = int(L0.q->rows);
+    h->k_dim = int(L0.k->rows);
+    h->ffn = int(L0.up->rows);
+    int hd = 0;
+    const DevTensor *qn = L0.q_norm ? L0.q_norm : L0.k_norm;
+    if (qn && qn->dims[0] > 0 && h->q_dim % qn->dims[0] == 0 && h->k_dim % qn->dims[0] == 0) hd = int(qn->dims[0]);
+    if (!hd) {  // GemmaLayerConfig::infer_head_dim (real_math.rs:2889-2907)
+      for (int c : {256, 128, 64})
+        if (h->q_dim % c == 0 && h->k_dim % c == 0) {
+          int nh = h->q_dim / c, nk = h->k_dim / c;
+          if (nk >= 1 && nh >= nk && nh % nk == 0) {
+            hd = c;
+            break;
+          }
+        }
+      if (!hd) {
+        int a = h->q_dim, b = h->k_dim;
+        while (b) {
+          int t = a % b;
+          a = b;
+          b = t;
+        }
+        hd = a;
+      }
+    }
+    h->head_dim = hd;
+    h->n_heads = h->q_dim / hd;
+    h->n_kv = std::max(1, h->k_dim / hd);
+    SFC_REQUIRE(h->n_heads % h->n_kv == 0 && h->n_heads / h->n_kv <= 8, "unsupported GQA grouping %d/%d",
+                h->n_heads, h->n_kv);
+    SFC_REQUIRE(hd <= 256, "head_dim %d > 256 unsupported", hd);
+    for (auto &L : h->layers) {
+      SFC_REQUIRE(L.q && L.k && L.v && L.o && L.gate && L.up && L.down, "layer %d is incomplete", L.index);
+      for (DevTensor *t : {L.q_norm, L.k_norm})
+        SFC_REQUIRE(!t || t->in_dim == hd, "%s has %lld elements but head_dim is %d", t->name.c_str(),
+                    (long long)t->in_dim, hd);
+      for (DevTensor *t : {L.attn_norm, L.post_attn, L.ffn_norm, L.post_ffw})
+        SFC_REQUIRE(!t || t->in_dim == h->hidden, "%s has %lld elements but hidden is %d", t->name.c_str(),
+                    (long long)t->in_dim, h->hidden);
+      SFC_REQUIRE(L.q->dims[0] == h->hidden && L.q->rows == h->q_dim && L.k->rows == h->k_dim &&
+                      L.v->rows == h->k_dim && L.o->dims[0] == h->q_dim && L.o->rows == h->hidden &&
+                      L.gate->dims[0] == h->hidden && L.gate->rows == h->ffn && L.up->rows == h->ffn &&
+                      L.down->dims[0] == h->ffn && L.down->rows == h->hidden,
+                  "layer %d shapes differ from layer %d", L.index, h->layers.front().index);
+      SFC_REQUIRE(L.gate->type == L.up->type, "layer %d: gate/up types differ", L.index);
+      for (DevTensor *t : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
+        SFC_REQUIRE((t->type != T_Q4_K && t->type != T_Q6_K) || t->in_dim <= 10240,
+                    "%s: K-quant rows of %lld elements exceed the GEMV limit 10240", t->name.c_str(),
+                    (long long)t->in_dim);
+    }
+  } else {
+    SFC_REQUIRE(h->logits_w && h->output_norm, "tail without layers needs logits tensors");
+    h->hidden = int(h->output_norm->dims[0]);
+  }
+  if (h->token_embd) {
+    SFC_REQUIRE(h->token_embd->dims.size() == 2 && h->token_embd->dims[0] == h->hidden,
+                "token_embd.weight dims do not match hidden %d", h->hidden);
+  }
+  if (h->is_head) SFC_REQUIRE(h->token_embd, "head stage needs token_embd.weight");
+  if (h->is_tail) {
+    SFC_REQUIRE(h->logits_w, "Tail stage has no logits tensor");
+    SFC_REQUIRE(h->logits_w->type == T_F16 || h->logits_w->type == T_F32 || h->logits_w->type == T_BF16,
+                "logits tensor type %s unsupported", type_name(h->logits_w->type));
+    // dims [hidden, vocab] (real_forward.rs:818-846)
+    if (h->logits_w->dims[0] == h->hidden)
+      h->vocab = h->logits_w->rows;
+    else
+      SFC_REQUIRE(false, "Logits tensor %s dimensions do not match hidden_dim %d", h->logits_w->name.c_str(),
+                  h->hidden);
+  }
+  if (h->token_embd && !h->vocab) h->vocab = h->token_embd->rows;
+
+  // ---- device memory
+  SFC_CUDA(cudaSetDevice(h->device));
+  SFC_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+  SFC_CUDA(cudaEventCreate(&h->ev0));
+  SFC_CUDA(cudaEventCreate(&h->ev1));
+  if (cudaMalloc(&h->weight_arena, size_t(arena)) != cudaSuccess) {
+    set_error("cannot allocate %lld bytes of weights", (long long)arena);
+    return SFC_E_NOMEM;
+  }
+  h->weight_bytes = arena;
+  int64_t off = 0;
+  void *staging = nullptr;
+  int64_t staging_bytes = 0;
+  for (auto &u : uploads) {
+    HostTensor *ht = u.first;
+    DevTensor *dt = u.second;
+    dt->dev = static_cast<char *>(h->weight_arena) + off;
+    const int64_t db = device_tensor_bytes(ht->type, ht->dims);
+    off += align256(db + 16);
+    if (ht->ones) {
+      std::vector<float> ones(size_t(dt->in_dim * dt->rows), 1.0f);
+      SFC_CUDA(cudaMemcpy(dt->dev, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice));
+      continue;
+    }
+    const bool needs_repack = ht->type == T_Q6_K;
+    if (ht->synthetic) {
+      if (!needs_repack) {
+        SFC_CUDA(synth_tensor(ht->type, ht->key, dt->rows, dt->in_dim, ht->sigma, ht->mean, dt->dev, h->stream));
+        continue;
+      }
+    }
+    const int64_t gb = gguf_tensor_bytes(ht->type, ht->dims);
+    void *src = dt->dev;
+    if (needs_repack) {
+      if (staging_bytes < gb) {
+        if (staging) cudaFree(staging);
+        SFC_CUDA(cudaMalloc(&staging, size_t(gb)));
+        staging_bytes = gb;
+      }
+      src = staging;
+    }
+    if (ht->synthetic)
+      SFC_CUDA(synth_tensor(ht->type, ht->key, dt->rows, dt->in_dim, ht->sigma, ht->mean, src, h->stream));
+    else
+      SFC_CUDA(cudaMemcpyAsync(src, ht->data, size_t(gb), cudaMemcpyHostToDevice, h->stream));
+    if (needs_repack) {
+      SFC_CUDA(prepare_weights(ht->type, src, dt->rows, dt->in_dim, dt->dev, h->stream));
+      SFC_CUDA(cudaStreamSynchronize(h->stream));  // staging reused by the next tensor
+    }
+  }
+  SFC_CUDA(cudaStreamSynchronize(h->stream));
+  if (staging) cudaFree(staging);
+
+  // KV cache
+  const int64_t elt = h->kv_f32 ? 4 : 2;
+  h->kv_slot_stride = 2 * int64_t(h->n_kv) * h->max_ctx * h->head_dim;
+  h->kv_bytes = int64_t(h->layers.size()) * h->max_sessions * h->kv_slot_stride * elt;
+  if (h->kv_bytes > 0) {
+    if (cudaMalloc(&h->kv_arena, size_t(h->kv_bytes)) != cudaSuccess) {
+      set_error("cannot allocate %lld bytes of KV cache (max_ctx %d x %d sessions)", (long long)h->kv_bytes,
+                h->max_ctx, h->max_sessions);
+      return SFC_E_NOMEM;
+    }
+  }
+  h->slot_used.assign(size_t(h->max_sessions), 0);
+
+  // activations
+  const int64_t T = h->max_batch;
+  auto alloc = [&](void **p, int64_t bytes) -> int {
+    if (cudaMalloc(p, size_t(std::max<int64_t>(bytes, 256))) != cudaSuccess) {
+      set_error("cannot allocate activation buffer of %lld bytes", (long long)bytes);
+      return SFC_E_NOMEM;
+    }
+    return SFC_OK;
+  };
+  int rc;
+  const int64_t H = h->hidden;
+  if ((rc = alloc((void **)&h->resid, T * H * 4)) || (rc = alloc((void **)&h->xn, T * H * 4)) ||
+      (rc = alloc((void **)&h->proj, T * H * 4)) || (rc = alloc((void **)&h->q, T * std::max(h->q_dim, 1) * 4)) ||
+      (rc = alloc((void **)&h->k, T * std::max(h->k_dim, 1) * 4)) ||
+      (rc = alloc((void **)&h->v, T * std::max(h->k_dim, 1) * 4)) ||
+      (rc = alloc((void **)&h->att, T * std::max(h->q_dim, 1) * 4)) ||
+      (rc = alloc((void **)&h->act, T * std::max(h->ffn, 1) * 4)) || (rc = alloc((void **)&h->hn, T * H * 4)) ||
+      (rc = alloc((void **)&h->score_dev, T * 4)) || (rc = alloc((void **)&h->ids_dev, T * 4)) ||
+      (rc = alloc((void **)&h->tok_dev, T * 8)) || (rc = alloc((void **)&h->tok_seq_dev, T * 4)) ||
+      (rc = alloc((void **)&h->step_dev, 4)) ||
+      (rc = alloc((void **)&h->seq_dev, int64_t(h->max_sessions) * sizeof(SeqInfo))))
+    return rc;
+  AttnParams ap = {};
+  ap.n_heads = std::max(h->n_heads, 1);
+  ap.n_kv = std::max(h->n_kv, 1);
+  ap.head_dim = std::max(h->head_dim, 1);
+  size_t amax = 0;
+  for (int64_t t = 1; t <= T; ++t) amax = std::max(amax, attention_scratch_bytes(t, ap, h->max_ctx));
+  h->attn_scratch = amax;
+  h->logit_scratch = logits_scratch_bytes(T);
+  if ((rc = alloc(&h->scratch, int64_t(std::max(h->attn_scratch, h->logit_scratch))))) return rc;
+  rc = h->ring.init(size_t(T) * 8 + size_t(h->max_sessions) * sizeof(SeqInfo) + 256);
+  if (rc) return rc;
+  return SFC_OK;
+}
+
+int new_stage(const sfc_layout *layout, const sfc_options *opts, int device, sfc_stage **out,
+              std::unique_ptr<sfc_stage> &h) {
+  SFC_REQUIRE(layout && out, "null argument");
+  h.reset(new sfc_stage());
+  h->device = device;
+  h->model_id = layout->model_id ? layout->model_id : "";
+  h->stage_id = layout->stage_id ? layout->stage_id : "";
+  h->start_layer = layout->start_layer;
+  h->end_layer = layout->end_layer;
+  h->is_head = layout->is_head != 0;
+  h->is_tail = layout->is_tail != 0;
+  return apply_options(h.get(), opts);
+}
+
+void destroy_stage(sfc_stage *h) {
+  if (!h) return;
+  cudaSetDevice(h->device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->decode_graph) cudaGraphExecDestroy(h->decode_graph);
+  for (void *p : {(void *)h->resid, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
+                  (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
+                  (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
+                  (void *)h->seq_dev, h->scratch, h->kv_arena, h->weight_arena})
+    if (p) cudaFree(p);
+  h->ring.destroy();
+  if (h->ev0) cudaEventDestroy(h->ev0);
+  if (h->ev1) cudaEventDestroy(h->ev1);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  delete h;
+}
+
+// ---- sessions
+int session_for(sfc_stage *h, const std::string &id, bool restart, Session **out) {
+  auto it = h->sessions.find(id);
+  if (it == h->sessions.end()) {
+    int slot = -1;
+    for (int i = 0; i < h->max_sessions; ++i)
+      if (!h->slot_used[i]) {
+        slot = i;
+        break;
+      }
+    if (slot < 0) {
+      set_error("all %d decode sessions are in use", h->max_sessions);
+      return SFC_E_NOMEM;
+    }
+    h->slot_used[slot] = 1;
+    it = h->sessions.emplace(id, Session{slot, 0}).first;
+  }
+  if (restart) it->second.len = 0;
+  *out = &it->second;
+  return SFC_OK;
+}
+
+KVLayer kv_layer(sfc_stage *h, size_t li) {
+  KVLayer kv;
+  const int64_t elt = h->kv_f32 ? 4 : 2;
+  kv.base = static_cast<char *>(h->kv_arena) + int64_t(li) * h->max_sessions * h->kv_slot_stride * elt;
+  kv.slot_stride = h->kv_slot_stride;
+  return kv;
+}
+
+AttnParams attn_params(sfc_stage *h, const Layer &L) {
+  AttnParams p = {};
+  p.n_heads = h->n_heads;
+  p.n_kv = h->n_kv;
+  p.head_dim = h->head_dim;
+  p.kv_f32 = h->kv_f32;
+  p.max_ctx = h->max_ctx;
+  p.eps = h->eps;
+  p.rope_theta = h->theta;
+  p.rotary_dim = h->head_dim;
+  p.proportional = 0;
+  p.rope_freqs = h->rope_freqs ? static_cast<const float *>(h->rope_freqs->dev) : nullptr;
+  p.n_freqs = h->rope_freqs ? int(h->rope_freqs->in_dim) : 0;
+  p.q_norm = L.q_norm ? static_cast<const float *>(L.q_norm->dev) : nullptr;
+  p.k_norm = L.k_norm ? static_cast<const float *>(L.k_norm->dev) : nullptr;
+  p.window = 0;
+  return p;
+}
+
+#define F32P(t) ((t) ? static_cast<const float *>((t)->dev) : nullptr)
+
+// All layers over the T rows in h->resid (device tables already uploaded).
+cudaError_t run_layers(sfc_stage *h, int64_t T, int64_t max_keys, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  const int H = h->hidden;
+  for (size_t li = 0; li < h->layers.size(); ++li) {
+    const Layer &L = h->layers[li];
+    if (li == 0) {
+      if (L.attn_norm)
+        e = rms_norm(h->resid, F32P(L.attn_norm), T, H, h->eps, h->xn, st);
+      else
+        e = cudaMemcpyAsync(h->xn, h->resid, size_t(T) * H * 4, cudaMemcpyDeviceToDevice, st);
+      if (e) return e;
+    }
+    if ((e = gemv(L.q->type, L.q->dev, nullptr, h->q_dim, H, h->xn, T, h->q, h->q_dim, st))) return e;
+    if ((e = gemv(L.k->type, L.k->dev, nullptr, h->k_dim, H, h->xn, T, h->k, h->k_dim, st))) return e;
+    if ((e = gemv(L.v->type, L.v->dev, nullptr, h->k_dim, H, h->xn, T, h->v, h->k_dim, st))) return e;
+    const AttnParams ap = attn_params(h, L);
+    const KVLayer kv = kv_layer(h, li);
+    if ((e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev, T, ap, st))) return e;
+    if ((e = attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, nullptr, nullptr, T, max_keys, ap, h->scratch,
+                       h->attn_scratch, st)))
+      return e;
+    if ((e = gemv(L.o->type, L.o->dev, nullptr, H, h->q_dim, h->att, T, h->proj, H, st))) return e;
+    if ((e = add_norm(h->resid, h->proj, F32P(L.post_attn), nullptr, 1, F32P(L.ffn_norm), h->xn, T, H, h->eps, st)))
+      return e;
+    if ((e = gemv(L.gate->type, L.gate->dev, L.up->dev, h->ffn, H, h->xn, T, h->act, h->ffn, st))) return e;
+    if ((e = gemv(L.down->type, L.down->dev, nullptr, H, h->ffn, h->act, T, h->proj, H, st))) return e;
+    const bool more = li + 1 < h->layers.size();
+    if ((e = add_norm(h->resid, h->proj, F32P(L.post_ffw), F32P(L.scale), more ? 1 : 0,
+                      more ? F32P(h->layers[li + 1].attn_norm) : nullptr, h->xn, T, H, h->eps, st)))
+      return e;
+  }
+  return e;
+}
+
+struct SeqReq {
+  Session *s;
+  int32_t n;
+};
+
+// One forward chunk (sum of rows <= max_batch).  ids (uint32, host or device) for the head,
+// `in_dev` rows for other stages.  Output stays in h->resid.
+int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t *ids, bool ids_on_device,
+                  const float *in_dev, cudaStream_t st) {
+  int64_t T = 0, max_keys = 1;
+  for (auto &s : seqs) {
+    SFC_REQUIRE(s.n > 0, "empty sequence in batch");
+    if (s.s->len + s.n > h->max_ctx) {
+      set_error("session needs %lld positions but max_ctx is %d", (long long)(s.s->len + s.n), h->max_ctx);
+      return SFC_E_NOMEM;
+    }
+    T += s.n;
+    max_keys = std::max<int64_t>(max_keys, s.s->len + s.n);
+  }
+  SFC_REQUIRE(T <= h->max_batch, "batch of %lld rows exceeds max_batch_tokens %d", (long long)T, h->max_batch);
+  int ri;
+  char *pin = static_cast<char *>(h->ring.acquire(&ri));
+  SeqInfo *si = reinterpret_cast<SeqInfo *>(pin);
+  int32_t *ts = reinterpret_cast<int32_t *>(pin + h->max_sessions * sizeof(SeqInfo));
+  int32_t row = 0;
+  for (size_t i = 0; i < seqs.size(); ++i) {
+    si[i] = SeqInfo{seqs[i].s->slot, int32_t(seqs[i].s->len), seqs[i].n, row};
+    for (int j = 0; j < seqs[i].n; ++j) ts[row + j] = int32_t(i);
+    row += seqs[i].n;
+  }
+  SFC_CUDA(cudaMemcpyAsync(h->seq_dev, si, seqs.size() * sizeof(SeqInfo), cudaMemcpyHostToDevice, st));
+  SFC_CUDA(cudaMemcpyAsync(h->tok_seq_dev, ts, size_t(T) * 4, cudaMemcpyHostToDevice, st));
+  if (h->is_head) {
+    const uint32_t *idd = ids;
+    if (!ids_on_device) {
+      uint32_t *idh = reinterpret_cast<uint32_t *>(ts + T);
+      SFC_REQUIRE(int64_t(h->max_sessions * sizeof(SeqInfo) + size_t(T) * 8) <= int64_t(h->ring.bytes),
+                  "staging too small");
+      for (int64_t i = 0; i < T; ++i) {
+        if (ids[i] >= h->vocab) {
+          h->ring.release(ri, st);
+          set_error("Token ID %u exceeds vocab size %lld", ids[i], (long long)h->vocab);
+          return SFC_E_INVALID;
+        }
+        idh[i] = ids[i];
+      }
+      SFC_CUDA(cudaMemcpyAsync(h->ids_dev, idh, size_t(T) * 4, cudaMemcpyHostToDevice, st));
+      idd = h->ids_dev;
+    }
+    SFC_CUDA(embed(h->token_embd->type, h->token_embd->dev, h->vocab, h->hidden, idd, 0, T, h->resid,
+                   device_error_ptr(), st));
+  } else {
+    SFC_CUDA(cudaMemcpyAsync(h->resid, in_dev, size_t(T) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
+  }
+  h->ring.release(ri, st);
+  SFC_CUDA(run_layers(h, T, max_keys, st));
+  for (auto &s : seqs) s.s->len += s.n;
+  return SFC_OK;
+}
+
+// Single-sequence forward of n rows, chunked by max_batch; rows land in out (device or host).
+int forward_single(sfc_stage *h, const char *req, const uint32_t *ids_host, const float *in_host, int64_t n,
+                   float *out_host, bool restart) {
+  SFC_REQUIRE(req, "null request id");
+  SFC_REQUIRE(n > 0, "Empty prompt");
+  SFC_CUDA(cudaSetDevice(h->device));
+  Session *s = nullptr;
+  int rc = session_for(h, req, restart, &s);
+  if (rc) return rc;
+  SFC_REQUIRE(s->len + n <= h->max_ctx, "session needs %lld positions but max_ctx is %d", (long long)(s->len + n),
+              h->max_ctx);
+  cudaStream_t st = h->stream;
+  SFC_CUDA(cudaEventRecord(h->ev0, st));
+  for (int64_t t0 = 0; t0 < n; t0 += h->max_batch) {
+    const int32_t c = int32_t(std::min<int64_t>(h->max_batch, n - t0));
+    if (!h->is_head) {
+      SFC_CUDA(cudaMemcpyAsync(h->hn, in_host + t0 * h->hidden, size_t(c) * h->hidden * 4, cudaMemcpyHostToDevice,
+                               st));
+    }
+    rc = forward_chunk(h, {SeqReq{s, c}}, ids_host ? ids_host + t0 : nullptr, false, h->hn, st);
+    if (rc) return rc;
+    if (out_host)
+      SFC_CUDA(cudaMemcpyAsync(out_host + t0 * h->hidden, h->resid, size_t(c) * h->hidden * 4,
+                               cudaMemcpyDeviceToHost, st));
+  }
+  SFC_CUDA(cudaEventRecord(h->ev1, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  float ms = 0;
+  cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+  h->profile.seq_len = n;
+  h->profile.layers = int64_t(h->layers.size());
+  h->profile.total_us = ms * 1e3;
+  unsigned derr = 0;
+  unsigned *dp = device_error_ptr();
+  if (dp) {
+    cudaMemcpy(&derr, dp, 4, cudaMemcpyDeviceToHost);
+    if (derr) {
+      unsigned z = 0;
+      cudaMemcpy(dp, &z, 4, cudaMemcpyHostToDevice);
+      set_error("device reported error code %u", derr);
+      return SFC_E_DEVICE;
+    }
+  }
+  return SFC_OK;
+}
+
+// Tail: output_norm + logits argmax on `n` device rows.
+int sample_rows(sfc_stage *h, const float *rows_dev, int64_t n, int64_t *tok_dev, float *score_dev, cudaStream_t st) {
+  SFC_REQUIRE(h->is_tail, "Only the tail stage may sample");
+  SFC_REQUIRE(n > 0 && n <= h->max_batch, "sample rows %lld out of range", (long long)n);
+  if (h->output_norm)
+    SFC_CUDA(rms_norm(rows_dev, F32P(h->output_norm), n, h->hidden, h->eps, h->hn, st));
+  else
+    SFC_CUDA(cudaMemcpyAsync(h->hn, rows_dev, size_t(n) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
+  SFC_CUDA(logits_argmax(h->logits_w->type, h->logits_w->dev, h->vocab, h->hidden, h->hn, n, h->softcap, nullptr,
+                         tok_dev, score_dev, h->scratch, std::max(h->attn_scratch, h->logit_scratch), st));
+  return SFC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sfc_stage_open(const char *index_json_path, const sfc_layout *layout, const sfc_options *opts, int device,
+                   sfc_stage **out) {
+  clear_error();
+  SFC_REQUIRE(index_json_path && out, "null argument");
+  std::unique_ptr<sfc_stage> h;
+  int rc = new_stage(layout, opts, device, out, h);
+  if (rc) return rc;
+  const std::string ip = index_json_path;
+  const std::string suffix = ".index.json";
+  if (ip.size() < suffix.size() || ip.compare(ip.size() - suffix.size(), suffix.size(), suffix) != 0) {
+    set_error("Packed stage index must end with .index.json");
+    return SFC_E_INVALID;
+  }
+  std::string js, pack;
+  if (!read_file(ip, js)) {
+    set_error("Failed to read %s", ip.c_str());
+    return SFC_E_IO;
+  }
+  JsonParser jp{js.data(), js.data() + js.size()};
+  Json idx = jp.value();
+  if (!jp.ok || idx.kind != Json::Obj) {
+    set_error("%s is not valid JSON", ip.c_str());
+    return SFC_E_IO;
+  }
+  const std::string pack_path = ip.substr(0, ip.size() - suffix.size()) + ".pack";
+  if (!read_file(pack_path, pack)) {
+    set_error("Packed stage file %s does not exist", pack_path.c_str());
+    return SFC_E_IO;
+  }
+  const Json *tb = idx.get("total_bytes");
+  const Json *ts = idx.get("tensors");
+  if (!tb || tb->kind != Json::Num || !ts || ts->kind != Json::Arr) {
+    set_error("index lacks total_bytes/tensors");
+    return SFC_E_IO;
+  }
+  if (int64_t(pack.size()) != int64_t(tb->num)) {
+    set_error("Packed stage size %lld does not match index total_bytes %lld", (long long)pack.size(),
+              (long long)tb->num);
+    return SFC_E_IO;
+  }
+  std::vector<HostTensor> hts;
+  int64_t expected = 0;
+  for (const Json &t : ts->arr) {
+    const Json *nm = t.get("name"), *po = t.get("pack_offset"), *bl = t.get("byte_len"), *dm = t.get("dimensions"),
+               *gt = t.get("ggml_type");
+    if (!nm || !po || !bl || !dm || !gt || nm->kind != Json::Str || dm->kind != Json::Arr) {
+      set_error("malformed tensor entry in index");
+      return SFC_E_IO;
+    }
+    const int64_t o = int64_t(po->num), n = int64_t(bl->num);
+    if (o != expected) {  // validate_offsets, lib.rs:3729-3750
+      set_error("Packed tensor %s has pack_offset %lld but expected %lld", nm->str.c_str(), (long long)o,
+                (long long)expected);
+      return SFC_E_IO;
+    }
+    expected += n;
+    if (expected > int64_t(pack.size())) {
+      set_error("Packed tensor %s extends past the pack", nm->str.c_str());
+      return SFC_E_IO;
+    }
+    HostTensor ht;
+    ht.name = nm->str;
+    ht.type = int(gt->num);
+    for (const Json &d : dm->arr) ht.dims.push_back(int64_t(d.num));
+    ht.data = reinterpret_cast<const uint8_t *>(pack.data()) + o;
+    ht.bytes = n;
+    hts.push_back(ht);
+  }
+  if (expected != int64_t(pack.size())) {
+    set_error("Packed tensor coverage %lld does not match total_bytes %lld", (long long)expected,
+              (long long)pack.size());
+    return SFC_E_IO;
+  }
+  rc = build_stage(h.get(), hts);
+  if (rc) {
+    destroy_stage(h.release());
+    return rc;
+  }
+  *out = h.release();
+  return SFC_OK;
+}
+
+int sfc_stage_open_synthetic(const sfc_synth_spec *spec, const sfc_layout *layout, const sfc_options *opts,
+                             int device, sfc_stage **out) {
+  clear_error();
+  SFC_REQUIRE(spec && out, "null argument");
+  std::unique_ptr<sfc_stage> h;
+  int rc = new_stage(layout, opts, device, out, h);
+  if (rc) return rc;
+  SFC_REQUIRE(spec->hidden > 0 && spec->n_heads > 0 && spec->n_kv > 0 && spec->head_dim > 0 && spec->ffn > 0 &&
+                  spec->vocab > 0,
+              "bad synthetic spec");
+  SFC_REQUIRE(h->start_layer <= h->end_layer && int(h->end_layer) < spec->n_layers_total, "bad layer range");
+  std::vector<HostTensor> hts;
+  const int64_t H = spec->hidden, Q = int64_t(spec->n_heads) * spec->head_dim,
+                K = int64_t(spec->n_kv) * spec->head_dim, F = spec->ffn, D = spec->head_dim;
+  auto add = [&](const std::string &name, int type, std::vector<int64_t> dims, float sigma, float mean, bool ones) {
+    HostTensor ht;
+    ht.name = name;
+    ht.type = type;
+    ht.dims = dims;
+    ht.data = nullptr;
+    ht.bytes = 0;
+    ht.synthetic = !ones;
+    ht.ones = ones;
+    ht.key = tensor_key(spec->seed, name.c_str());
+    ht.sigma = sigma;
+    ht.mean = mean;
+    hts.push_back(ht);
+  };
+  if (h->is_head || h->is_tail) add("token_embd.weight", spec->type_embd, {H, spec->vocab}, spec->embd_sigma, 0, false);
+  add("rope_freqs.weight", T_F32, {D / 2}, 0, 0, true);
+  for (uint32_t i = h->start_layer; i <= h->end_layer; ++i) {
+    const std::string p = "blk." + std::to_string(i);
+    add(p + ".attn_norm.weight", T_F32, {H}, spec->norm_sigma, 1.0f, false);
+    add(p + ".attn_q.weight", spec->type_q, {H, Q}, spec->w_sigma, 0, false);
+    add(p + ".attn_k.weight", spec->type_k, {H, K}, spec->w_sigma, 0, false);
+    add(p + ".attn_v.weight", spec->type_v, {H, K}, spec->w_sigma, 0, false);
+    add(p + ".attn_q_norm.weight", T_F32, {D}, spec->norm_sigma, 1.0f, false);
+    add(p + ".attn_k_norm.weight", T_F32, {D}, spec->norm_sigma, 1.0f, false);
+    add(p + ".attn_output.weight", spec->type_o, {Q, H}, spec->w_sigma, 0, false);
+    add(p + ".post_attention_norm.weight", T_F32, {H}, spec->norm_sigma, 1.0f, false);
+    add(p + ".ffn_norm.weight", T_F32, {H}, spec->norm_sigma, 1.0f, false);
+    add(p + ".ffn_gate.weight", spec->type_gate, {H, F}, spec->w_sigma, 0, false);
+    add(p + ".ffn_up.weight", spec->type_up, {H, F}, spec->w_sigma, 0, false);
+    add(p + ".ffn_down.weight", spec->type_down, {F, H}, spec->w_sigma, 0, false);
+    add(p + ".post_ffw_norm.weight", T_F32, {H}, spec->norm_sigma, 1.0f, false);
+  }
+  if (h->is_tail) add("output_norm.weight", T_F32, {H}, spec->norm_sigma, 1.0f, false);
+  rc = build_stage(h.get(), hts);
+  if (rc) {
+    destroy_stage(h.release());
+    return rc;
+  }
+  *out = h.release();
+  return SFC_OK;
+}
+
+int sfc_stage_close(sfc_stage *h) {
+  destroy_stage(h);
+  return SFC_OK;
+}
+
+int sfc_stage_get_info(sfc_stage *h, sfc_stage_info *info) {
+  SFC_REQUIRE(h && info, "null argument");
+  info->hidden = h->hidden;
+  info->n_heads = h->n_heads;
+  info->n_kv = h->n_kv;
+  info->head_dim = h->head_dim;
+  info->ffn = h->ffn;
+  info->n_layers = int(h->layers.size());
+  info->vocab = h->vocab;
+  info->is_head = h->is_head;
+  info->is_tail = h->is_tail;
+  info->weight_bytes = h->weight_bytes;
+  info->kv_bytes = h->kv_bytes;
+  return SFC_OK;
+}
+
+int sfc_begin_token_ids(sfc_stage *h, const char *request_id, const uint32_t *ids, int64_t n, float *out_hidden) {
+  clear_error();
+  SFC_REQUIRE(h && ids, "null argument");
+  SFC_REQUIRE(h->is_head, "Only the head stage may accept prompt ingress");
+  return forward_single(h, request_id, ids, nullptr, n, out_hidden, n > 1);
+}
+
+int sfc_continue_forward(sfc_stage *h, const char *request_id, const float *in_hidden, int64_t n, float *out_hidden) {
+  clear_error();
+  SFC_REQUIRE(h && in_hidden, "null argument");
+  SFC_REQUIRE(!h->is_head, "Head stage should use begin_prompt, not continue_forward");
+  return forward_single(h, request_id, nullptr, in_hidden, n, out_hidden, n > 1);
+}
+
+int sfc_sample_tail(sfc_stage *h, const float *hidden, int64_t n, uint32_t *token, float *score) {
+  clear_error();
+  SFC_REQUIRE(h && hidden && token, "null argument");
+  SFC_REQUIRE(n > 0, "Hidden-state payload is empty");
+  SFC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = h->stream;
+  SFC_CUDA(cudaMemcpyAsync(h->proj, hidden + (n - 1) * h->hidden, size_t(h->hidden) * 4, cudaMemcpyHostToDevice, st));
+  int rc = sample_rows(h, h->proj, 1, h->tok_dev, h->score_dev, st);
+  if (rc) return rc;
+  int64_t t = 0;
+  float s = 0;
+  SFC_CUDA(cudaMemcpyAsync(&t, h->tok_dev, 8, cudaMemcpyDeviceToHost, st));
+  SFC_CUDA(cudaMemcpyAsync(&s, h->score_dev, 4, cudaMemcpyDeviceToHost, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  *token = uint32_t(t);
+  if (score) *score = s;
+  return SFC_OK;
+}
+
+int sfc_forward_dev(sfc_stage *h, const char *const *request_ids, const int32_t *seq_tokens, int n_seq,
+                    const uint32_t *ids_dev, const float *in_dev, float *out_dev, int append, void *stream) {
+  clear_error();
+  SFC_REQUIRE(h && request_ids && seq_tokens && n_seq > 0 && out_dev, "null argument");
+  SFC_REQUIRE(n_seq <= h->max_sessions, "batch of %d sequences exceeds max_sessions %d", n_seq, h->max_sessions);
+  SFC_REQUIRE(h->is_head ? ids_dev != nullptr : in_dev != nullptr, "missing input");
+  SFC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  std::vector<SeqReq> seqs;
+  int64_t T = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    SFC_REQUIRE(request_ids[i], "null request id");
+    Session *s = nullptr;
+    int rc = session_for(h, request_ids[i], !append, &s);
+    if (rc) return rc;
+    for (auto &o : seqs) SFC_REQUIRE(o.s != s, "request %s appears twice in one batch", request_ids[i]);
+    seqs.push_back(SeqReq{s, seq_tokens[i]});
+    T += seq_tokens[i];
+  }
+  if (n_seq == 1 && T > h->max_batch) {  // long single sequence: chunk it
+    for (int64_t t0 = 0; t0 < T; t0 += h->max_batch) {
+      const int32_t c = int32_t(std::min<int64_t>(h->max_batch, T - t0));
+      int rc = forward_chunk(h, {SeqReq{seqs[0].s, c}}, ids_dev ? ids_dev + t0 : nullptr, true,
+                             in_dev ? in_dev + t0 * h->hidden : nullptr, st);
+      if (rc) return rc;
+      SFC_CUDA(cudaMemcpyAsync(out_dev + t0 * h->hidden, h->resid, size_t(c) * h->hidden * 4,
+                               cudaMemcpyDeviceToDevice, st));
+    }
+    return SFC_OK;
+  }
+  int rc = forward_chunk(h, seqs, ids_dev, true, in_dev, st);
+  if (rc) return rc;
+  SFC_CUDA(cudaMemcpyAsync(out_dev, h->resid, size_t(T) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
+  return SFC_OK;
+}
+
+int sfc_sample_dev(sfc_stage *h, const float *hidden_dev, int64_t n, int64_t *tokens_dev, float *scores_dev,
+                   void *stream) {
+  clear_error();
+  SFC_REQUIRE(h && hidden_dev && tokens_dev && scores_dev, "null argument");
+  SFC_CUDA(cudaSetDevice(h->device));
+  return sample_rows(h, hidden_dev, n, tokens_dev, scores_dev,
+                     stream ? static_cast<cudaStream_t>(stream) : h->stream);
+}
+
+int sfc_verify_greedy(sfc_stage *h, const float *hidden, const uint32_t *drafts, int64_t k, int64_t *accepted,
+                      uint32_t *bonus) {
+  clear_error();
+  SFC_REQUIRE(h && hidden && accepted && bonus && (k == 0 || drafts), "null argument");
+  SFC_REQUIRE(k >= 0 && k + 1 <= h->max_batch, "k out of range");
+  SFC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = h->stream;
+  SFC_CUDA(cudaMemcpyAsync(h->proj, hidden, size_t(k + 1) * h->hidden * 4, cudaMemcpyHostToDevice, st));
+  int rc = sample_rows(h, h->proj, k + 1, h->tok_dev, h->score_dev, st);
+  if (rc) return rc;
+  std::vector<int64_t> am((size_t)(k + 1));
+  SFC_CUDA(cudaMemcpyAsync(am.data(), h->tok_dev, size_t(k + 1) * 8, cudaMemcpyDeviceToHost, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  // lib.rs:2143-2164: accept while argmax at position i equals draft i; bonus = first mismatch.
+  int64_t acc = 0;
+  while (acc < k && uint32_t(am[size_t(acc)]) == drafts[acc]) ++acc;
+  *accepted = acc;
+  *bonus = uint32_t(am[size_t(acc)]);
+  return SFC_OK;
+}
+
+int sfc_clear_decode_session(sfc_stage *h, const char *request_id) {
+  SFC_REQUIRE(h && request_id, "null argument");
+  auto it = h->sessions.find(request_id);
+  if (it != h->sessions.end()) {
+    h->slot_used[size_t(it->second.slot)] = 0;
+    h->sessions.erase(it);
+  }
+  return SFC_OK;
+}
+
+int sfc_rollback_kv(sfc_stage *h, const char *request_id, int64_t keep) {
+  SFC_REQUIRE(h && request_id, "null argument");
+  auto it = h->sessions.find(request_id);
+  SFC_REQUIRE(it != h->sessions.end(), "unknown session %s", request_id);
+  SFC_REQUIRE(keep >= 0 && keep <= it->second.len, "keep_count %lld exceeds session length %lld", (long long)keep,
+              (long long)it->second.len);
+  it->second.len = keep;
+  return SFC_OK;
+}
+
+int64_t sfc_session_len(sfc_stage *h, const char *request_id) {
+  if (!h || !request_id) return SFC_E_INVALID;
+  auto it = h->sessions.find(request_id);
+  return it == h->sessions.end() ? 0 : it->second.len;
+}
+
+int sfc_session_fill_synthetic(sfc_stage *h, const char *request_id, int64_t n_pos, uint64_t seed) {
+  clear_error();
+  SFC_REQUIRE(h && request_id, "null argument");
+  SFC_REQUIRE(n_pos >= 0 && n_pos <= h->max_ctx, "n_pos %lld out of range", (long long)n_pos);
+  SFC_CUDA(cudaSetDevice(h->device));
+  Session *s = nullptr;
+  int rc = session_for(h, request_id, true, &s);
+  if (rc) return rc;
+  const int64_t elt = h->kv_f32 ? 4 : 2;
+  for (size_t li = 0; li < h->layers.size(); ++li) {
+    KVLayer kv = kv_layer(h, li);
+    for (int part = 0; part < 2; ++part)
+      for (int kh = 0; kh < h->n_kv; ++kh) {
+        char *base = static_cast<char *>(kv.base) +
+                     (int64_t(s->slot) * kv.slot_stride + part * (kv.slot_stride / 2) +
+                      int64_t(kh) * h->max_ctx * h->head_dim) *
+                         elt;
+        const std::string nm = "kv." + std::to_string(li) + "." + std::to_string(part) + "." + std::to_string(kh);
+        SFC_CUDA(synth_tensor(h->kv_f32 ? T_F32 : T_F16, tensor_key(seed, nm.c_str()), n_pos, h->head_dim, 1.0f,
+                              0.0f, base, h->stream));
+      }
+  }
+  SFC_CUDA(cudaStreamSynchronize(h->stream));
+  s->len = n_pos;
+  return SFC_OK;
+}
+
+int sfc_generate_greedy(sfc_stage *h, const char *request_id, const uint32_t *prompt, int64_t n_prompt,
+                        int64_t n_steps, uint32_t *out_tokens) {
+  clear_error();
+  SFC_REQUIRE(h && request_id && prompt && out_tokens, "null argument");
+  SFC_REQUIRE(h->is_head && h->is_tail, "greedy generation needs a whole-model stage (head and tail)");
+  SFC_REQUIRE(n_prompt > 0 && n_steps > 0, "empty prompt or no steps");
+  SFC_REQUIRE(n_prompt + n_steps <= h->max_ctx, "prompt + steps exceed max_ctx %d", h->max_ctx);
+  SFC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = h->stream;
+  int rc = forward_single(h, request_id, prompt, nullptr, n_prompt, nullptr, true);
+  if (rc) return rc;
+  Session *s = &h->sessions[request_id];
+  // first token from the last prompt row
+  const int64_t last = (n_prompt - 1) % h->max_batch;
+  rc = sample_rows(h, h->resid + last * h->hidden, 1, h->tok_dev, h->score_dev, st);
+  if (rc) return rc;
+  if (h->gen_capacity < n_steps) {
+    if (h->decode_graph) {  // the graph holds the old token buffer and step bound
+      cudaGraphExecDestroy(h->decode_graph);
+      h->decode_graph = nullptr;
+    }
+    if (h->gen_tokens_dev) cudaFree(h->gen_tokens_dev);
+    h->gen_tokens_dev = nullptr;
+    SFC_CUDA(cudaMalloc(&h->gen_tokens_dev, size_t(n_steps) * 8));
+    h->gen_capacity = n_steps;
+  }
+  SFC_CUDA(cudaMemcpyAsync(h->gen_tokens_dev, h->tok_dev, 8, cudaMemcpyDeviceToDevice, st));
+  const int32_t one = 1;
+  SeqInfo si{s->slot, int32_t(s->len), 1, 0};
+  const int32_t zero = 0;
+  SFC_CUDA(cudaMemcpyAsync(h->step_dev, &one, 4, cudaMemcpyHostToDevice, st));
+  SFC_CUDA(cudaMemcpyAsync(h->seq_dev, &si, sizeof(si), cudaMemcpyHostToDevice, st));
+  SFC_CUDA(cudaMemcpyAsync(h->tok_seq_dev, &zero, 4, cudaMemcpyHostToDevice, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  if (n_steps > 1) {
+    if (!h->decode_graph) {
+      cudaGraph_t g = nullptr;
+      const long long k0 = g_kernel_launches;
+      SFC_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      cudaError_t e = embed(h->token_embd->type, h->token_embd->dev, h->vocab, h->hidden, h->tok_dev, 1, 1, h->resid,
+                            device_error_ptr(), st);
+      if (!e) e = run_layers(h, 1, h->max_ctx, st);
+      if (!e) {
+        if (h->output_norm)
+          e = rms_norm(h->resid, F32P(h->output_norm), 1, h->hidden, h->eps, h->hn, st);
+        else
+          e = cudaMemcpyAsync(h->hn, h->resid, size_t(h->hidden) * 4, cudaMemcpyDeviceToDevice, st);
+      }
+      if (!e)
+        e = logits_argmax(h->logits_w->type, h->logits_w->dev, h->vocab, h->hidden, h->hn, 1, h->softcap, nullptr,
+                          h->tok_dev, h->score_dev, h->scratch, std::max(h->attn_scratch, h->logit_scratch), st);
+      if (!e) e = decode_advance(h->tok_dev, h->gen_tokens_dev, h->step_dev, h->seq_dev, 1, h->gen_capacity, st);
+      cudaError_t e2 = cudaStreamEndCapture(st, &g);
+      if (e) return cuda_fail(e, "decode graph capture");
+      if (e2) return cuda_fail(e2, "cudaStreamEndCapture");
+      h->graph_kernels = g_kernel_launches - k0;
+      e = cudaGraphInstantiate(&h->decode_graph, g, 0);
+      cudaGraphDestroy(g);
+      if (e) return cuda_fail(e, "cudaGraphInstantiate");
+    }
+    SFC_CUDA(cudaEventRecord(h->ev0, st));
+    for (int64_t i = 1; i < n_steps; ++i) SFC_CUDA(cudaGraphLaunch(h->decode_graph, st));
+    SFC_CUDA(cudaEventRecord(h->ev1, st));
+  }
+  std::vector<int64_t> toks((size_t)n_steps);
+  SFC_CUDA(cudaMemcpyAsync(toks.data(), h->gen_tokens_dev, size_t(n_steps) * 8, cudaMemcpyDeviceToHost, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  for (int64_t i = 0; i < n_steps; ++i) out_tokens[i] = uint32_t(toks[size_t(i)]);
+  s->len += n_steps - 1;
+  if (n_steps > 1) {
+    float ms = 0;
+    cudaEventElapsedTime(&ms, h->ev0, h->ev1);
+    h->profile.total_us = ms * 1e3;
+    h->profile.seq_len = n_steps - 1;
+    h->profile.kernels = h->graph_kernels * (n_steps - 1);
+  }
+  unsigned derr = 0;
+  unsigned *dp = device_error_ptr();
+  if (dp && cudaMemcpy(&derr, dp, 4, cudaMemcpyDeviceToHost) == cudaSuccess && derr) {
+    unsigned z = 0;
+    cudaMemcpy(dp, &z, 4, cudaMemcpyHostToDevice);
+    set_error("device reported error code %u", derr);
+    return SFC_E_DEVICE;
+  }
+  return SFC_OK;
+}
+
+int sfc_last_profile(sfc_stage *h, sfc_profile *out) {
+  SFC_REQUIRE(h && out, "null argument");
+  *out = h->profile;
+  return SFC_OK;
+}
+
+}  // extern "C"

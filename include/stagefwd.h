@@ -1,0 +1,196 @@
+/*
+ * stagefwd.h — C ABI of the B200 stage-forward backend (libstagefwd.so).
+ *
+ * Drop-in boundary for the stage workers of Compute-Network/compute-sharding: every
+ * entry point names the reference interface it replaces (paths are relative to the
+ * reference repository).  Plain pointers and sizes only; no torch types.
+ *
+ * Conventions
+ *  - Return value: 0 on success, a negative SFC_E_* code on failure.  The message of the
+ *    last failure on the calling thread is available from sfc_last_error().  Bad input
+ *    (shapes, ids, offsets, sizes) is rejected on the host before any kernel runs.
+ *  - "dev" pointers are device pointers on the handle's / current device; `stream` is a
+ *    cudaStream_t (NULL = legacy default stream).  Host-pointer entry points synchronise.
+ *  - Weight layouts are GGUF (ggml_type ids: F32=0, F16=1, Q4_K=12, Q6_K=14, BF16=30);
+ *    rows hold `in_dim` elements, tensor dims are GGUF [in_dim, out_dim].
+ *  - A stage handle is not re-entrant: one host thread drives it at a time (the reference's
+ *    "caller serializes" contract, crates/llama-stage-backend/src/lib.rs:580-588).
+ */
+#ifndef STAGEFWD_H
+#define STAGEFWD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SFC_ABI_VERSION 1
+
+enum {
+  SFC_OK = 0,
+  SFC_E_INVALID = -1,  /* bad argument, shape or state */
+  SFC_E_CUDA = -2,     /* CUDA runtime error */
+  SFC_E_IO = -3,       /* pack / index file error */
+  SFC_E_NOMEM = -4,    /* device allocation failed or a fixed capacity is exceeded */
+  SFC_E_DEVICE = -5,   /* a kernel reported a device-side error (bounded wait expired, bad id) */
+};
+
+/* ------------------------------------------------------------------ misc */
+int sfc_abi_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+const char *sfc_last_error(void);
+/* Read and clear the device-side error word of the current device (0 = none). */
+int sfc_device_error(unsigned *code);
+
+/* ------------------------------------------------------------------ kernel-level API
+ * Device pointers, caller's stream.  Weights for sfc_matmul* must be in the device layout
+ * produced by sfc_prepare_weights (identical to GGUF for F32/F16/BF16/Q4_K; Q6_K rows are
+ * re-laid out field-by-field so every field is 16-byte aligned).                        */
+
+/* Bytes of `rows` rows in the device layout. <0 on unsupported type/shape. */
+int64_t sfc_weight_device_bytes(int ggml_type, int64_t rows, int64_t in_dim);
+
+/* GGUF rows (device) -> device layout.  Replaces the pack read of
+ * StageTensorStore::read (crates/stage-forward-lab/src/lib.rs:3693-3727). */
+int sfc_prepare_weights(int ggml_type, const void *gguf_dev, int64_t rows, int64_t in_dim, void *dst_dev,
+                        void *stream);
+
+/* Bit-exact dequantization of GGUF Q4_K / Q6_K rows to f32.
+ * Replaces quants.rs:181-249 dequantize_q4_k_block / dequantize_q6_k_block. */
+int sfc_dequantize_rows(int ggml_type, const void *gguf_dev, int64_t rows, int64_t in_dim, float *out_dev,
+                        void *stream);
+
+/* y[t][r] = sum_k W[r][k] x[t][k] (token-major).  Replaces real_math.rs:398-1124
+ * matmul_quantized_many_refs_range(_token_major) and the row dots quants.rs:829-3700. */
+int sfc_matmul(int ggml_type, const void *w_dev, int64_t out_dim, int64_t in_dim, const float *x_dev, int64_t n_tok,
+               float *y_dev, void *stream);
+
+/* act[t][r] = gelu_tanh(G x)[r] * (U x)[r] in one pass over both matrices.  Replaces
+ * real_math.rs:1584-1800 (pair matmul) + real_math.rs:79-85 (GeGLU), as called at
+ * crates/stage-forward-lab/src/real_forward.rs:1716-1730. */
+int sfc_matmul_pair_geglu(int ggml_type, const void *w_gate_dev, const void *w_up_dev, int64_t out_dim,
+                          int64_t in_dim, const float *x_dev, int64_t n_tok, float *act_dev, void *stream);
+
+/* out[t] = x[t] * (1/sqrt(mean(x[t]^2) + eps)) * w.  Replaces real_math.rs:30-47. */
+int sfc_rms_norm(const float *x_dev, const float *w_dev, int64_t n_tok, int64_t dim, float eps, float *out_dev,
+                 void *stream);
+
+/* Logits over `vocab` rows of W (dims [dim, vocab]) for each of n_tok hidden vectors, softcap
+ * cap*tanh(s/cap) (cap <= 0: none), argmax with ties to the lowest index; optionally all
+ * capped scores [n_tok][vocab].  Replaces real_math.rs:2119-2488 matmul_raw_top_k. */
+int sfc_logits_argmax(int ggml_type, const void *w_dev, int64_t vocab, int64_t dim, const float *h_dev,
+                      int64_t n_tok, float cap, float *all_scores_dev, int64_t *argmax_dev, float *score_dev,
+                      void *stream);
+
+/* Seeded synthetic tensor in GGUF layout (deterministic; same bytes on every device). */
+int sfc_synth_tensor(int ggml_type, uint64_t seed, const char *name, int64_t rows, int64_t in_dim, float sigma,
+                     float mean, void *out_dev, void *stream);
+
+/* ------------------------------------------------------------------ stage-level API
+ * Implements the StageForwardBackend trait (crates/stage-forward-lab/src/lib.rs:4663-4674)
+ * with RealGemmaBackend semantics (crates/stage-forward-lab/src/real_forward.rs:112-2411).  */
+
+typedef struct sfc_stage sfc_stage;
+
+/* StageLayout, crates/stage-forward-lab/src/lib.rs:212-219 */
+typedef struct {
+  const char *model_id;
+  const char *stage_id;
+  uint32_t start_layer;
+  uint32_t end_layer;
+  int is_head;
+  int is_tail;
+} sfc_layout;
+
+typedef struct {
+  float rope_theta;    /* 0 -> 1e6, the reference's hard-coded base (real_forward.rs:2284) */
+  float logit_softcap; /* 0 -> 30 (real_forward.rs:2285); <0 -> none */
+  float eps;           /* 0 -> 1e-6 (real_math.rs:5) */
+  int kv_f32;          /* 0: fp16 KV cache (default); 1: f32 KV cache, the reference's precision */
+  int max_ctx;         /* positions per session; 0 -> 4096 */
+  int max_sessions;    /* KV slots; 0 -> 64 (real_forward.rs:23 DECODE_SESSION_LIMIT) */
+  int max_batch_tokens;/* rows per forward chunk; 0 -> 512 */
+} sfc_options;
+
+/* Synthetic Gemma-style stage: same tensor names, types and shapes as a packed stage. */
+typedef struct {
+  uint64_t seed;
+  int hidden, n_heads, n_kv, head_dim, ffn, n_layers_total;
+  int64_t vocab;
+  int type_q, type_k, type_v, type_o, type_gate, type_up, type_down, type_embd;
+  float w_sigma, embd_sigma, norm_sigma;
+} sfc_synth_spec;
+
+typedef struct {
+  int hidden, n_heads, n_kv, head_dim, ffn, n_layers;
+  int64_t vocab;
+  int is_head, is_tail;
+  int64_t weight_bytes;
+  int64_t kv_bytes;
+} sfc_stage_info;
+
+/* RealGemmaBackend::new(index_path) + load_layout (real_forward.rs:162, :2258-2363): loads a
+ * `<stage>.index.json` + `.pack` (PackedStageIndex, lib.rs:2908-2927; validation
+ * lib.rs:3645-3750) onto `device`. */
+int sfc_stage_open(const char *index_json_path, const sfc_layout *layout, const sfc_options *opts, int device,
+                   sfc_stage **out);
+/* Same, with weights generated on the device from `spec` (layers start..end of the layout). */
+int sfc_stage_open_synthetic(const sfc_synth_spec *spec, const sfc_layout *layout, const sfc_options *opts,
+                             int device, sfc_stage **out);
+int sfc_stage_close(sfc_stage *h);
+int sfc_stage_get_info(sfc_stage *h, sfc_stage_info *info);
+
+/* Head ingress: begin_token_ids (real_forward.rs:1123, :988-1121).  ids[n] -> hidden [n][H]
+ * (host).  n > 1 starts a new session for request_id; n == 1 continues its KV (or starts one). */
+int sfc_begin_token_ids(sfc_stage *h, const char *request_id, const uint32_t *ids, int64_t n, float *out_hidden);
+/* continue_forward (real_forward.rs:2376-2405, :2054-2254): hidden [n][H] -> [n][H] (host),
+ * same session rule as sfc_begin_token_ids. */
+int sfc_continue_forward(sfc_stage *h, const char *request_id, const float *in_hidden, int64_t n, float *out_hidden);
+/* sample_tail (real_forward.rs:2407-2410, :904-986): output_norm, logits, softcap, argmax of
+ * the LAST row of hidden [n][H] (host). */
+int sfc_sample_tail(sfc_stage *h, const float *hidden, int64_t n, uint32_t *token, float *score);
+
+/* Batched device path (pipelines): n_seq sessions, seq_tokens[i] rows each, concatenated.
+ * Head: ids_dev [sum] token ids; other stages: in_dev [sum][H].  out_dev [sum][H].
+ * append = 1 continues every session; append = 0 restarts them (prefill). */
+int sfc_forward_dev(sfc_stage *h, const char *const *request_ids, const int32_t *seq_tokens, int n_seq,
+                    const uint32_t *ids_dev, const float *in_dev, float *out_dev, int append, void *stream);
+/* Tail: greedy sample of rows of hidden_dev [n][H] -> tokens_dev [n] (int64), scores_dev [n]. */
+int sfc_sample_dev(sfc_stage *h, const float *hidden_dev, int64_t n, int64_t *tokens_dev, float *scores_dev,
+                   void *stream);
+
+/* Greedy speculative verification at the tail (crates/llama-stage-backend/src/lib.rs:2022-2234):
+ * hidden [k+1][H] for [last, d1..dk] already forwarded; accept while argmax_i == d_{i+1}; bonus =
+ * argmax at the first mismatch (or at k).  Returns accepted count and bonus token. */
+int sfc_verify_greedy(sfc_stage *h, const float *hidden, const uint32_t *drafts, int64_t k, int64_t *accepted,
+                      uint32_t *bonus);
+
+/* Session management (real_forward.rs:294-317; rollback lib.rs:2236-2269). */
+int sfc_clear_decode_session(sfc_stage *h, const char *request_id);
+int sfc_rollback_kv(sfc_stage *h, const char *request_id, int64_t keep);
+int64_t sfc_session_len(sfc_stage *h, const char *request_id);
+/* Fill a session's cache with `n_pos` positions of seeded N(0,1) keys/values (benchmarks:
+ * a decode step's cost does not depend on the cached values). */
+int sfc_session_fill_synthetic(sfc_stage *h, const char *request_id, int64_t n_pos, uint64_t seed);
+
+/* Single-GPU greedy generation through a whole model (head+tail in one stage):
+ * prompt ids[n_prompt] prefill, then n_steps greedy tokens into out_tokens (host).
+ * The decode step runs as one captured CUDA graph.  Mirrors the bench loop of
+ * crates/stage-forward-lab/src/bin/real_two_stage_generate_bench.rs:215-290. */
+int sfc_generate_greedy(sfc_stage *h, const char *request_id, const uint32_t *prompt, int64_t n_prompt,
+                        int64_t n_steps, uint32_t *out_tokens);
+
+/* Per-phase device times of the last forward (RealForwardProfile, real_forward.rs:28-47), us. */
+typedef struct {
+  int64_t seq_len, layers;
+  double embed_us, attn_us, ffn_us, logits_us, total_us;
+  int64_t kernels; /* kernels launched by the timed region (graph replays included) */
+} sfc_profile;
+int sfc_last_profile(sfc_stage *h, sfc_profile *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,502 @@
+"""CPU oracle for the stage-forward hot path — TEST INFRASTRUCTURE ONLY.
+
+A restatement of the reference's Rust CPU stage (`RealGemmaBackend`,
+crates/stage-forward-lab/src/real_forward.rs) on top of the C++ kernels in
+stage_oracle.cpp.  Only tests/, ``__graft_entry__.smoke()`` and bench.py's
+CPU-baseline leg import this module, and only as the checker; the product
+(`compute-sharding_b200/`) never does.
+
+Parity anchors:
+  * dequant: bit-exact against the reference's own ggml-quants.c
+    (oracle/_ref, built from the reference sources) and gguf-py numpy
+    (tests/golden fixtures) — see tests/test_oracle_golden.py;
+  * known-answer rows from quants.rs:3725-3772 and real_math.rs:3130-3191,
+    4334-4440 (tests/golden/known_answers.json);
+  * incremental decode == full rerun (real_forward.rs:3129).
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import math
+import os
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+F32, F16, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 12, 13, 14, 30
+QK_K = 256
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
+EPS = 1e-6  # real_math.rs:5
+
+
+def bytes_per_row(t: int, in_dim: int) -> int:
+    if t == F32:
+        return 4 * in_dim
+    if t in (F16, BF16):
+        return 2 * in_dim
+    if t in BLOCK_BYTES:
+        if in_dim % QK_K:
+            raise ValueError(f"in_dim {in_dim} not a multiple of {QK_K}")
+        return in_dim // QK_K * BLOCK_BYTES[t]
+    raise ValueError(f"unsupported ggml type {t}")
+
+
+def _threads() -> int:
+    return max(1, int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1)))
+
+
+class _Lib:
+    def __init__(self):
+        path = HERE / "_build" / "libstage_oracle.so"
+        if not path.exists():
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle`")
+        L = ctypes.CDLL(str(path))
+        P, I64, I, F, U64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_uint64
+        L.or_dequantize_rows.argtypes = [I, P, I64, I64, P]
+        L.or_matmul.argtypes = [I, P, I64, I64, P, I64, P, I]
+        L.or_rms_norm_inplace.argtypes = [P, I64, P, I64, F]
+        L.or_per_head_rms_norm.argtypes = [P, P, I64, I, I, F]
+        L.or_gelu_tanh_mul_inplace.argtypes = [P, P, I64]
+        L.or_rope_apply.argtypes = [P, I, I, P, I64, ctypes.c_uint32, F, I, I]
+        L.or_gqa_attention.argtypes = [P, P, P, I64, I64, I64, I, I, I, P]
+        L.or_logits_top_k.argtypes = [I, P, I64, I64, P, I, F, P, P, P, P, P, I]
+        L.or_mix64.argtypes = [U64, U64]
+        L.or_mix64.restype = U64
+        L.or_tensor_key.argtypes = [U64, ctypes.c_char_p]
+        L.or_tensor_key.restype = U64
+        L.or_synth_normal.argtypes = [U64, U64]
+        L.or_synth_normal.restype = F
+        L.or_synth_tensor.argtypes = [I, U64, I64, I64, F, F, P, I]
+        L.or_fp16_to_f32.argtypes = [ctypes.c_uint16]
+        L.or_fp16_to_f32.restype = F
+        L.or_f32_to_fp16.argtypes = [F]
+        L.or_f32_to_fp16.restype = ctypes.c_uint16
+        self.L = L
+
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        _LIB = _Lib()
+    return _LIB.L
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ---------------------------------------------------------------- kernels
+def dequantize_rows(t: int, raw: np.ndarray, n_rows: int, in_dim: int) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    out = np.empty((n_rows, in_dim), np.float32)
+    if lib().or_dequantize_rows(t, _p(raw), n_rows, in_dim, _p(out)) != 0:
+        raise ValueError("dequantize shape mismatch")
+    return out
+
+
+def matmul(t: int, raw: np.ndarray, out_dim: int, in_dim: int, x: np.ndarray) -> np.ndarray:
+    """Token-major y[T, out_dim] (real_math.rs matmul_quantized_many_refs_range_token_major)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    if x.shape[1] != in_dim:
+        raise ValueError("input width mismatch")
+    y = np.empty((x.shape[0], out_dim), np.float32)
+    if lib().or_matmul(t, _p(raw), out_dim, in_dim, _p(x), x.shape[0], _p(y), _threads()) != 0:
+        raise ValueError("matmul shape mismatch")
+    return y
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float = EPS) -> np.ndarray:
+    x = np.array(x, np.float32, copy=True, order="C")
+    w = np.ascontiguousarray(w, np.float32)
+    for row in x.reshape(-1, x.shape[-1]):
+        lib().or_rms_norm_inplace(_p(row), row.shape[0], _p(w), w.shape[0], eps)
+    return x
+
+
+def per_head_rms_norm(x: np.ndarray, w, n_heads: int, head_dim: int, eps: float = EPS) -> np.ndarray:
+    x = np.array(x, np.float32, copy=True, order="C")
+    if w is not None:
+        w = np.ascontiguousarray(w, np.float32)
+    for row in x.reshape(-1, n_heads * head_dim):
+        lib().or_per_head_rms_norm(_p(row), None if w is None else _p(w), 0 if w is None else w.shape[0],
+                                   n_heads, head_dim, eps)
+    return x
+
+
+def gelu_tanh_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g = np.array(g, np.float32, copy=True, order="C")
+    u = np.ascontiguousarray(u, np.float32)
+    lib().or_gelu_tanh_mul_inplace(_p(g), _p(u), g.size)
+    return g
+
+
+def rope(x: np.ndarray, n_heads: int, head_dim: int, freqs, position: int, theta: float,
+         rotary_dim: int | None = None, proportional: bool = False) -> np.ndarray:
+    x = np.array(x, np.float32, copy=True, order="C")
+    f = np.ascontiguousarray(freqs if freqs is not None else np.zeros(0), np.float32)
+    lib().or_rope_apply(_p(x), n_heads, head_dim, _p(f), f.shape[0], position, theta,
+                        head_dim if rotary_dim is None else rotary_dim, int(proportional))
+    return x
+
+
+def gqa_attention(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, n_heads: int, n_kv: int, head_dim: int,
+                  limit: int = -1, window: int = 0) -> np.ndarray:
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(kc, np.float32)
+    vc = np.ascontiguousarray(vc, np.float32)
+    out = np.empty(n_heads * head_dim, np.float32)
+    lib().or_gqa_attention(_p(q), _p(kc), _p(vc), kc.shape[0], limit, window, n_heads, n_kv, head_dim, _p(out))
+    return out
+
+
+def logits_top_k(t: int, raw: np.ndarray, vocab: int, hidden: int, h: np.ndarray, k: int = 0,
+                 cap: float = 30.0, want_all: bool = False):
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    h = np.ascontiguousarray(h, np.float32)
+    am = np.zeros(1, np.int64)
+    asc = np.zeros(1, np.float32)
+    ti = np.zeros(max(k, 1), np.int64)
+    ts = np.zeros(max(k, 1), np.float32)
+    allsc = np.empty(vocab, np.float32) if want_all else None
+    rc = lib().or_logits_top_k(t, _p(raw), vocab, hidden, _p(h), k, cap, _p(am), _p(asc), _p(ti), _p(ts),
+                               None if allsc is None else _p(allsc), _threads())
+    if rc != 0:
+        raise ValueError("logits shape mismatch")
+    top = [(int(i), float(s)) for i, s in zip(ti[:k], ts[:k]) if i >= 0]
+    return int(am[0]), float(asc[0]), top, allsc
+
+
+def fp16_round(a: np.ndarray) -> np.ndarray:
+    """Round f32 values to fp16 precision (used to emulate an fp16 KV cache)."""
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+
+
+# ---------------------------------------------------------------- synthetic model
+def tensor_key(seed: int, name: str) -> int:
+    return int(lib().or_tensor_key(seed & (2**64 - 1), name.encode()))
+
+
+def synth_tensor(t: int, key: int, n_rows: int, in_dim: int, sigma: float, mean: float = 0.0) -> np.ndarray:
+    out = np.empty(n_rows * bytes_per_row(t, in_dim), np.uint8)
+    if lib().or_synth_tensor(t, key, n_rows, in_dim, sigma, mean, _p(out), _threads()) != 0:
+        raise ValueError("bad synthetic tensor shape")
+    return out
+
+
+def synth_tokens(seed: int, name: str, n: int, vocab: int) -> np.ndarray:
+    key = tensor_key(seed, name)
+    return np.array([int(lib().or_mix64(key, i)) % vocab for i in range(n)], np.uint32)
+
+
+def synth_normal_f32(seed: int, name: str, n: int, sigma: float = 1.0) -> np.ndarray:
+    raw = synth_tensor(F32, tensor_key(seed, name), 1, n, sigma)
+    return raw.view(np.float32).copy()
+
+
+@dataclass
+class ModelSpec:
+    """Gemma-style decoder with GGUF tensor names (real_forward.rs:1483-1793).
+
+    Defaults are the 42-layer Q4_K_M shape of the graded configs: d_model 2560,
+    8 q heads / 4 kv heads of 256, GeGLU FFN 10240, vocab 262144, tied fp16 embedding.
+    """
+    hidden: int = 2560
+    n_heads: int = 8
+    n_kv: int = 4
+    head_dim: int = 256
+    ffn: int = 10240
+    vocab: int = 262144
+    n_layers: int = 42
+    seed: int = 0x5EED
+    rope_theta: float = 10000.0
+    w_sigma: float = 0.02        # fp16 d/dmin ~ |N(0, 0.02)|
+    embd_sigma: float = 0.02     # tied embedding ~ N(0, 0.02)
+    norm_sigma: float = 0.05     # norm weights 1 + N(0, 0.05)
+    types: dict = field(default_factory=lambda: {
+        "attn_q": Q4_K, "attn_k": Q4_K, "attn_v": Q6_K, "attn_output": Q4_K,
+        "ffn_gate": Q4_K, "ffn_up": Q4_K, "ffn_down": Q6_K, "token_embd": F16})
+
+    @property
+    def q_dim(self):
+        return self.n_heads * self.head_dim
+
+    @property
+    def k_dim(self):
+        return self.n_kv * self.head_dim
+
+    def layer_tensor_shapes(self, i: int):
+        """(name, ggml_type, dims [in, out]) for layer i, GGUF order."""
+        H, Q, K, F, D = self.hidden, self.q_dim, self.k_dim, self.ffn, self.head_dim
+        p = f"blk.{i}"
+        t = self.types
+        return [
+            (f"{p}.attn_norm.weight", F32, [H]),
+            (f"{p}.attn_q.weight", t["attn_q"], [H, Q]),
+            (f"{p}.attn_k.weight", t["attn_k"], [H, K]),
+            (f"{p}.attn_v.weight", t["attn_v"], [H, K]),
+            (f"{p}.attn_q_norm.weight", F32, [D]),
+            (f"{p}.attn_k_norm.weight", F32, [D]),
+            (f"{p}.attn_output.weight", t["attn_output"], [Q, H]),
+            (f"{p}.post_attention_norm.weight", F32, [H]),
+            (f"{p}.ffn_norm.weight", F32, [H]),
+            (f"{p}.ffn_gate.weight", t["ffn_gate"], [H, F]),
+            (f"{p}.ffn_up.weight", t["ffn_up"], [H, F]),
+            (f"{p}.ffn_down.weight", t["ffn_down"], [F, H]),
+            (f"{p}.post_ffw_norm.weight", F32, [H]),
+        ]
+
+    def stage_tensor_shapes(self, start: int, end: int, is_head: bool, is_tail: bool):
+        out = []
+        if is_head or is_tail:
+            out.append(("token_embd.weight", self.types["token_embd"], [self.hidden, self.vocab]))
+        out.append(("rope_freqs.weight", F32, [self.head_dim // 2]))
+        for i in range(start, end + 1):
+            out.extend(self.layer_tensor_shapes(i))
+        if is_tail:
+            out.append(("output_norm.weight", F32, [self.hidden]))
+        return out
+
+    def synth(self, name: str, t: int, dims) -> np.ndarray:
+        """Bytes of one synthetic tensor (same spec as the device generator)."""
+        in_dim = dims[0]
+        rows = int(np.prod(dims[1:])) if len(dims) > 1 else 1
+        key = tensor_key(self.seed, name)
+        if name == "rope_freqs.weight":
+            return np.ones(in_dim, np.float32).view(np.uint8).copy()
+        if t == F32:  # norm weights
+            return synth_tensor(F32, key, rows, in_dim, self.norm_sigma, 1.0)
+        if name == "token_embd.weight":
+            return synth_tensor(t, key, rows, in_dim, self.embd_sigma)
+        return synth_tensor(t, key, rows, in_dim, self.w_sigma)
+
+
+def synth_stage(spec: ModelSpec, start: int, end: int, is_head: bool, is_tail: bool) -> dict:
+    """name -> (ggml_type, dims, bytes)."""
+    return {n: (t, d, spec.synth(n, t, d)) for n, t, d in spec.stage_tensor_shapes(start, end, is_head, is_tail)}
+
+
+# ---------------------------------------------------------------- packed stage files
+def write_pack(directory, stage_name: str, role: str, stage_index: int, tensors: dict,
+               model_name: str = "synthetic-gemma") -> Path:
+    """Write `<stage>-required.index.json` + `.pack` (PackedStageIndex, lib.rs:2908-2927).
+    Tensors are contiguous in insertion order, as validate_offsets requires (lib.rs:3729-3750)."""
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    index_path = directory / f"{stage_name}-required.index.json"
+    pack_path = directory / f"{stage_name}-required.pack"
+    entries, off = [], 0
+    with open(pack_path, "wb") as f:
+        for name, (t, dims, data) in tensors.items():
+            b = np.ascontiguousarray(data).view(np.uint8)
+            f.write(b.tobytes())
+            entries.append({"name": name, "pack_offset": off, "byte_len": int(b.size), "source_file_offset": 0,
+                            "dimensions": [int(d) for d in dims], "ggml_type": int(t)})
+            off += int(b.size)
+    index = {"model_name": model_name, "architecture": "gemma4", "stage_index": stage_index, "role": role,
+             "total_bytes": off, "tensor_count": len(entries), "tensors": entries}
+    index_path.write_text(json.dumps(index, indent=2))
+    return index_path
+
+
+def load_pack(index_path) -> dict:
+    """PackedStageArtifact::load + validate_offsets (lib.rs:3645-3675, :3729-3750)."""
+    index_path = Path(index_path)
+    if not index_path.name.endswith(".index.json"):
+        raise ValueError("Packed stage index must end with .index.json")
+    index = json.loads(index_path.read_text())
+    pack = index_path.with_name(index_path.name[: -len(".index.json")] + ".pack")
+    if not pack.exists():
+        raise FileNotFoundError(f"Packed stage file {pack} does not exist")
+    if pack.stat().st_size != index["total_bytes"]:
+        raise ValueError("Packed stage size does not match index total_bytes")
+    mm = np.memmap(pack, np.uint8, "r")
+    out, expected = {}, 0
+    for e in index["tensors"]:
+        if e["pack_offset"] != expected:
+            raise ValueError(f"Packed tensor {e['name']} has pack_offset {e['pack_offset']} but expected {expected}")
+        expected += e["byte_len"]
+        out[e["name"]] = (e["ggml_type"], e["dimensions"], mm[e["pack_offset"]: e["pack_offset"] + e["byte_len"]])
+    if expected != index["total_bytes"]:
+        raise ValueError("Packed tensor coverage does not match total_bytes")
+    return out
+
+
+# ---------------------------------------------------------------- stage backend
+@dataclass
+class Layout:
+    """StageLayout (lib.rs:212-219)."""
+    model_id: str
+    stage_id: str
+    start_layer: int
+    end_layer: int
+    is_head: bool
+    is_tail: bool
+
+
+class OracleStage:
+    """RealGemmaBackend semantics with an explicit KV cache.
+
+    The reference drops its KV on single-token steps when the model has no PLE
+    (real_forward.rs:1006-1011, :2072-2076) and pins "incremental decode == full
+    rerun" (real_forward.rs:3129); this oracle keeps the KV explicitly, which the
+    tests check against a full rerun.  ``kv_fp16`` rounds stored K/V to fp16 to
+    mirror a device fp16 cache; False is the reference's f32 cache.
+    """
+
+    def __init__(self, tensors: dict, layout: Layout, rope_theta: float = 1e6, softcap: float = 30.0,
+                 kv_fp16: bool = False):
+        self.t = tensors
+        self.layout = layout
+        self.kv_fp16 = kv_fp16
+        self.softcap = softcap
+        self.rope_theta = rope_theta
+        layers = sorted({int(n.split(".")[1]) for n in tensors if n.startswith("blk.")})
+        self.layers = layers
+        l0 = f"blk.{layers[0]}" if layers else None
+        # config inference, real_forward.rs:2258-2283 and real_math.rs:2869-2907
+        self.hidden = tensors[f"{l0}.attn_q.weight"][1][0] if l0 else 2560
+        q_dim = tensors[f"{l0}.attn_q.weight"][1][1] if l0 else 2048
+        k_dim = tensors[f"{l0}.attn_k.weight"][1][1] if l0 else 512
+        hd = None
+        qn = tensors.get(f"{l0}.attn_q_norm.weight")
+        if qn is not None and q_dim % qn[1][0] == 0 and k_dim % qn[1][0] == 0:
+            hd = qn[1][0]
+        if hd is None:
+            hd = next((c for c in (256, 128, 64) if q_dim % c == 0 and k_dim % c == 0 and
+                       q_dim // c >= k_dim // c and (q_dim // c) % (k_dim // c) == 0), math.gcd(q_dim, k_dim))
+        self.head_dim, self.n_heads, self.n_kv = hd, q_dim // hd, max(1, k_dim // hd)
+        rf = tensors.get("rope_freqs.weight")
+        self.rope_freqs = None if rf is None else self._f32(rf)
+        self.sessions: dict[str, dict] = {}
+
+    @staticmethod
+    def _f32(entry) -> np.ndarray:
+        t, dims, raw = entry
+        if t != F32:
+            raise ValueError("Expected F32 tensor")  # real_forward.rs:478-488
+        return np.frombuffer(np.ascontiguousarray(raw).tobytes(), np.float32)
+
+    def _mm(self, name: str, x: np.ndarray) -> np.ndarray:
+        t, dims, raw = self.t[name]
+        return matmul(t, raw, dims[1], dims[0], x)
+
+    def embed(self, ids) -> np.ndarray:
+        """embed_tokens, real_forward.rs:848-871: F16 row dequant, then * sqrt(hidden)."""
+        t, dims, raw = self.t["token_embd.weight"]
+        H, V = dims
+        rb = bytes_per_row(t, H)
+        out = np.empty((len(ids), H), np.float32)
+        scale = np.float32(math.sqrt(H))
+        for i, tid in enumerate(ids):
+            if tid >= V:
+                raise ValueError(f"Token ID {tid} exceeds vocab size {V}")
+            out[i] = dequantize_rows(t, raw[int(tid) * rb:(int(tid) + 1) * rb], 1, H)[0] * scale
+        return out
+
+    def _layer(self, i: int, states: np.ndarray, pos0: int, kv: dict) -> np.ndarray:
+        """forward_layer_seq, real_forward.rs:1483-1793 (generic schedule, no PLE)."""
+        p = f"blk.{i}"
+        H, nh, nkv, hd = self.hidden, self.n_heads, self.n_kv, self.head_dim
+        T = states.shape[0]
+        x = rms_norm(states, self._f32(self.t[f"{p}.attn_norm.weight"]))
+        q_all = self._mm(f"{p}.attn_q.weight", x)
+        k_all = self._mm(f"{p}.attn_k.weight", x)
+        v_all = self._mm(f"{p}.attn_v.weight", x)
+        q_all = per_head_rms_norm(q_all, self._f32(self.t[f"{p}.attn_q_norm.weight"]), nh, hd)
+        k_all = per_head_rms_norm(k_all, self._f32(self.t[f"{p}.attn_k_norm.weight"]), nkv, hd)
+        v_all = per_head_rms_norm(v_all, None, nkv, hd)
+        kc, vc = kv.setdefault(i, ([], []))
+        att = np.empty((T, nh * hd), np.float32)
+        for t in range(T):
+            q, k = q_all[t], k_all[t]
+            if self.rope_freqs is not None:
+                q = rope(q, nh, hd, self.rope_freqs, pos0 + t, self.rope_theta)
+                k = rope(k, nkv, hd, self.rope_freqs, pos0 + t, self.rope_theta)
+            v = v_all[t]
+            if self.kv_fp16:
+                k, v = fp16_round(k), fp16_round(v)
+            kc.append(k)
+            vc.append(v)
+            att[t] = gqa_attention(q, np.stack(kc), np.stack(vc), nh, nkv, hd, limit=pos0 + t + 1)
+        o = self._mm(f"{p}.attn_output.weight", att)
+        o = rms_norm(o, self._f32(self.t[f"{p}.post_attention_norm.weight"]))
+        states = o + states
+        x = rms_norm(states, self._f32(self.t[f"{p}.ffn_norm.weight"]))
+        g = self._mm(f"{p}.ffn_gate.weight", x)
+        u = self._mm(f"{p}.ffn_up.weight", x)
+        a = gelu_tanh_mul(g, u)
+        d = self._mm(f"{p}.ffn_down.weight", a)
+        d = rms_norm(d, self._f32(self.t[f"{p}.post_ffw_norm.weight"]))
+        states = d + states
+        sc = self.t.get(f"{p}.layer_output_scale.weight")
+        if sc is not None:
+            states = states * self._f32(sc)[0]
+        return states
+
+    def run_layers(self, states: np.ndarray, pos0: int, kv: dict) -> np.ndarray:
+        for i in self.layers:
+            states = self._layer(i, states, pos0, kv)
+        return states
+
+    def _session(self, req: str, n: int, fresh: bool) -> dict:
+        s = self.sessions.get(req)
+        if fresh or s is None:
+            s = {"seq_len": 0, "kv": {}}
+            self.sessions[req] = s
+        return s
+
+    def begin_token_ids(self, req: str, ids, append: bool = False) -> np.ndarray:
+        """Head ingress (real_forward.rs:988-1121). A multi-token call starts a new
+        session; a single-token call (or append=True) continues the session's KV."""
+        if not self.layout.is_head:
+            raise ValueError("Only the head stage may accept prompt ingress")
+        if len(ids) == 0:
+            raise ValueError("Empty prompt")
+        s = self._session(req, len(ids), fresh=(len(ids) > 1 and not append))
+        out = self.run_layers(self.embed(ids), s["seq_len"], s["kv"])
+        s["seq_len"] += len(ids)
+        return out
+
+    def continue_forward(self, req: str, hidden: np.ndarray, append: bool = False) -> np.ndarray:
+        """continue_forward_inner (real_forward.rs:2054-2254), same session rule."""
+        if self.layout.is_head:
+            raise ValueError("Head stage should use begin_prompt, not continue_forward")
+        hidden = np.ascontiguousarray(np.atleast_2d(hidden), np.float32)
+        s = self._session(req, hidden.shape[0], fresh=(hidden.shape[0] > 1 and not append))
+        out = self.run_layers(hidden, s["seq_len"], s["kv"])
+        s["seq_len"] += hidden.shape[0]
+        return out
+
+    def rollback(self, req: str, keep: int):
+        s = self.sessions[req]
+        if keep > s["seq_len"]:
+            raise ValueError("keep_count exceeds session length")
+        for kc, vc in s["kv"].values():
+            del kc[keep:]
+            del vc[keep:]
+        s["seq_len"] = keep
+
+    def logits_entry(self):
+        return self.t.get("output.weight") or self.t["token_embd.weight"]  # real_forward.rs:803-816
+
+    def sample_tail(self, hidden_last: np.ndarray, top_k: int = 0, want_all: bool = False):
+        """sample_hidden_state_with_trace (real_forward.rs:904-986): output_norm, tied
+        logits with softcap 30, argmax (lowest index wins ties)."""
+        if not self.layout.is_tail:
+            raise ValueError("Only the tail stage may sample")
+        h = np.ascontiguousarray(hidden_last, np.float32).reshape(-1)
+        on = self.t.get("output_norm.weight")
+        if on is not None:
+            h = rms_norm(h, self._f32(on))
+        t, dims, raw = self.logits_entry()
+        H = self.hidden
+        vocab = dims[1] if dims[0] == H else dims[0]
+        return logits_top_k(t, raw, vocab, H, h, top_k, self.softcap, want_all)

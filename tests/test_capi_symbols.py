@@ -1,0 +1,53 @@
+"""CPU: the C-ABI library loads, exports every entry point include/stagefwd.h declares, and
+rejects bad input on the host with an error message (no GPU needed for these paths)."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "stagefwd.h"
+LIB = ROOT / "compute-sharding_b200" / "stagefwd" / "libstagefwd.so"
+
+
+def declared():
+    return sorted(set(re.findall(r"\b(sfc_[a-z0-9_]+)\s*\(", HEADER.read_text())))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for must in ("sfc_matmul", "sfc_dequantize_rows", "sfc_stage_open", "sfc_begin_token_ids",
+                 "sfc_continue_forward", "sfc_sample_tail", "sfc_rollback_kv", "sfc_verify_greedy"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    assert LIB.exists(), "build with make -C compute-sharding_b200"
+    lib = ctypes.CDLL(str(LIB))
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (sfc_[a-z0-9_]+)", out))
+    assert set(declared()) <= exported
+
+
+def test_host_validation_without_gpu():
+    import stagefwd as sf
+    assert sf.lib.sfc_abi_version() == 1
+    # unsupported type / shape: rejected before any CUDA call
+    assert sf.lib.sfc_matmul(13, None, 4, 256, None, 1, None, None) == -1
+    assert b"unsupported ggml type 13" in sf.lib.sfc_last_error()
+    assert sf.lib.sfc_matmul(12, None, 4, 100, None, 1, None, None) == -1
+    assert sf.lib.sfc_dequantize_rows(1, None, 1, 256, None, None) == -1
+    assert sf.lib.sfc_weight_device_bytes(14, 10, 2560) == 10 * 2112
+    assert sf.lib.sfc_weight_device_bytes(12, 10, 2560) == 10 * 1440
+
+
+def test_stage_open_rejects_bad_index_name(tmp_path):
+    import stagefwd as sf
+    bad = tmp_path / "stage.json"
+    bad.write_text("{}")
+    with pytest.raises(sf.StageError, match="index.json"):
+        sf.CudaStageBackend(bad).load_layout("m", "s", 0, 0, True, True)

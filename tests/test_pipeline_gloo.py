@@ -1,0 +1,126 @@
+"""CPU, world_size 2 and 3 over gloo: the pipeline driver (stagefwd/pipeline.py) splits layers
+like gguf.rs:307-329, hands hidden rows rank to rank, returns tail tokens to the head, and
+reproduces the single-process result.  The per-rank compute here is the CPU oracle."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import stage_oracle as so
+
+SPEC = dict(hidden=256, n_heads=4, n_kv=2, head_dim=64, ffn=512, vocab=200, n_layers=5, seed=31)
+
+
+class OracleCompute:
+    def __init__(self, stage):
+        self.s = stage
+
+    def forward(self, request_ids, seq_tokens, x, append=True):
+        outs, row = [], 0
+        for rid, n in zip(request_ids, seq_tokens):
+            part = x[row:row + n]
+            if self.s.layout.is_head:
+                o = self.s.begin_token_ids(rid, part.numpy().astype(np.uint32), append=append)
+            else:
+                o = self.s.continue_forward(rid, part.numpy(), append=append)
+            outs.append(torch.from_numpy(o))
+            row += n
+        return torch.cat(outs)
+
+    def sample(self, hidden):
+        return torch.tensor([self.s.sample_tail(h.numpy())[0] for h in hidden], dtype=torch.int64)
+
+
+def make_stage(start, end, head, tail):
+    spec = so.ModelSpec(**SPEC)
+    return so.OracleStage(so.synth_stage(spec, start, end, head, tail),
+                          so.Layout("m", f"s{start}", start, end, head, tail), rope_theta=10000.0)
+
+
+def run_pipeline(rank, world, port, q):
+    os.environ["ORACLE_THREADS"] = "1"
+    from stagefwd.pipeline import Pipeline, even_stage_split, make_groups
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    ranks = make_groups(rank, world)
+    start, end = even_stage_split(SPEC["n_layers"], world)[rank]
+    pipe = Pipeline(OracleCompute(make_stage(start, end, rank == 0, rank == world - 1)), ranks, SPEC["hidden"],
+                    torch.device("cpu"))
+    prompt = torch.from_numpy(so.synth_tokens(2, "p", 7, SPEC["vocab"]).astype(np.int64))
+    gen = pipe.generate("g", prompt, 6)
+    mbs = [["a", "b"], ["c", "d"]]
+    for i, rid in enumerate(["a", "b", "c", "d"]):  # short prefills so every session has context
+        pipe.step([rid], [3], torch.tensor([i + 1, i + 2, i + 3], dtype=torch.int64), append=False)
+    toks = [torch.tensor([5, 6], dtype=torch.int64), torch.tensor([7, 8], dtype=torch.int64)]
+    out = pipe.decode_microbatched(mbs, toks, 3)
+    if rank == 0:
+        q.put((gen.tolist(), [t.tolist() for t in out]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def single_process_reference():
+    st = make_stage(0, SPEC["n_layers"] - 1, True, True)
+    prompt = so.synth_tokens(2, "p", 7, SPEC["vocab"])
+    h = st.begin_token_ids("g", prompt)
+    gen = []
+    for _ in range(6):
+        t = st.sample_tail(h[-1])[0]
+        gen.append(t)
+        h = st.begin_token_ids("g", [t])
+    for i, rid in enumerate(["a", "b", "c", "d"]):
+        st.begin_token_ids(rid, [i + 1, i + 2, i + 3])
+    toks = {"a": 5, "b": 6, "c": 7, "d": 8}
+    for _ in range(3):
+        for rid in ["a", "b", "c", "d"]:
+            toks[rid] = st.sample_tail(st.begin_token_ids(rid, [toks[rid]])[-1])[0]
+    return gen, [[toks["a"], toks["b"]], [toks["c"], toks["d"]]]
+
+
+def test_even_stage_split_matches_reference_rule():
+    from stagefwd.pipeline import even_stage_split
+    assert even_stage_split(42, 2) == [(0, 20), (21, 41)]
+    assert even_stage_split(42, 4) == [(0, 10), (11, 21), (22, 31), (32, 41)]
+    assert [e - s + 1 for s, e in even_stage_split(42, 8)] == [6, 6, 5, 5, 5, 5, 5, 5]
+    with pytest.raises(ValueError):
+        even_stage_split(3, 4)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_pipeline_matches_single_process(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=run_pipeline, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    import queue
+    import time
+    got, t0 = None, time.time()
+    while got is None and time.time() - t0 < 240:
+        try:
+            got = q.get(timeout=2)
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        if got is None:
+            p.kill()
+    assert got is not None, [p.exitcode for p in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = single_process_reference()
+    assert got[0] == ref[0]
+    assert got[1] == ref[1]

@@ -1,0 +1,154 @@
+"""GPU parity of the stage-level C ABI (StageForwardBackend semantics) against the oracle."""
+import numpy as np
+import pytest
+
+import stage_oracle as so
+from gpu_util import assert_close
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def sf():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import stagefwd
+    return stagefwd
+
+
+def shape_pair(**kw):
+    """(oracle ModelSpec, stagefwd ModelShape) describing the same synthetic model."""
+    base = dict(hidden=512, n_heads=4, n_kv=2, head_dim=128, ffn=1024, vocab=4096, n_layers=4, seed=21)
+    base.update(kw)
+    spec = so.ModelSpec(**{k: v for k, v in base.items()})
+    import stagefwd
+    shape = stagefwd.ModelShape(**{k: v for k, v in base.items()})
+    return spec, shape
+
+
+def oracle_stage(spec, start, end, head, tail, kv_fp16=True):
+    return so.OracleStage(so.synth_stage(spec, start, end, head, tail),
+                          so.Layout("m", f"s{start}", start, end, head, tail), rope_theta=10000.0, kv_fp16=kv_fp16)
+
+
+def gpu_stage(sf, shape, start, end, head, tail, kv_f32=False, **kw):
+    return sf.CudaStageBackend(synthetic=shape, rope_theta=10000.0, kv_f32=kv_f32, max_ctx=1024, max_sessions=8,
+                               **kw).load_layout("m", f"s{start}", start, end, head, tail)
+
+
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_two_stage_prefill_decode_matches_oracle(sf, kv_f32):
+    spec, shape = shape_pair()
+    oh, ot = oracle_stage(spec, 0, 1, True, False, not kv_f32), oracle_stage(spec, 2, 3, False, True, not kv_f32)
+    gh, gt = gpu_stage(sf, shape, 0, 1, True, False, kv_f32), gpu_stage(sf, shape, 2, 3, False, True, kv_f32)
+    prompt = so.synth_tokens(4, "p", 37, spec.vocab)
+    h_o, h_g = oh.begin_token_ids("r", prompt), gh.begin_token_ids("r", prompt)
+    assert_close(h_g, h_o, what="head prefill")
+    t_o, t_g = ot.continue_forward("r", h_o), gt.continue_forward("r", h_o)
+    assert_close(t_g, t_o, what="tail prefill")
+    tok_o, tok_g = ot.sample_tail(t_o[-1])[0], gt.sample_tail(t_g)[0]
+    assert tok_o == tok_g
+    for step in range(6):  # incremental decode keeps KV on both sides
+        h_o, h_g = oh.begin_token_ids("r", [tok_o]), gh.begin_token_ids("r", [tok_g])
+        assert_close(h_g, h_o, what=f"head step {step}")
+        t_o, t_g = ot.continue_forward("r", h_o), gt.continue_forward("r", h_g)
+        assert_close(t_g, t_o, what=f"tail step {step}")
+        tok_o, tok_g = ot.sample_tail(t_o[-1])[0], gt.sample_tail(t_g)[0]
+        assert tok_o == tok_g
+    assert gh.session_len("r") == 37 + 6 and gt.session_len("r") == 37 + 6
+
+
+def test_pack_file_loads_and_matches(sf, tmp_path):
+    spec, shape = shape_pair(n_layers=2, vocab=1000)
+    tensors = so.synth_stage(spec, 0, 1, True, True)
+    idx = so.write_pack(tmp_path, "stage-0", "full", 0, tensors)
+    g = sf.CudaStageBackend(idx, rope_theta=10000.0, max_ctx=256, max_sessions=2).load_layout(
+        "synthetic-gemma", "stage-0", 0, 1, True, True)
+    o = so.OracleStage(so.load_pack(idx), so.Layout("m", "s", 0, 1, True, True), rope_theta=10000.0, kv_fp16=True)
+    prompt = so.synth_tokens(6, "p", 11, spec.vocab)
+    assert_close(g.begin_token_ids("a", prompt), o.begin_token_ids("a", prompt), what="pack stage")
+    # host-side validation errors (no kernel runs)
+    with pytest.raises(sf.StageError, match="exceeds vocab"):
+        g.begin_token_ids("b", [spec.vocab + 5])
+    with pytest.raises(sf.StageError, match="keep_count"):
+        g.rollback_kv("a", 1000)
+
+
+def test_pack_validation_errors(sf, tmp_path):
+    spec, _ = shape_pair(n_layers=1, vocab=500)
+    idx = so.write_pack(tmp_path, "stage-0", "full", 0, so.synth_stage(spec, 0, 0, True, True))
+    pack = idx.with_name("stage-0-required.pack")
+    data = pack.read_bytes()
+    pack.write_bytes(data[:-3])
+    with pytest.raises(sf.StageError, match="total_bytes"):
+        sf.CudaStageBackend(idx, max_ctx=64, max_sessions=1).load_layout("m", "s", 0, 0, True, True)
+    pack.write_bytes(data)
+
+
+def test_incremental_equals_full_rerun_on_gpu(sf):
+    spec, shape = shape_pair(n_layers=2)
+    g = gpu_stage(sf, shape, 0, 1, True, True)
+    prompt = so.synth_tokens(9, "p", 20, spec.vocab)
+    full = g.begin_token_ids("full", prompt)
+    g.begin_token_ids("inc", prompt[:12])
+    rows = [g.begin_token_ids("inc", [t]) for t in prompt[12:]]
+    assert_close(np.concatenate(rows), full[12:], what="incremental vs full")
+
+
+def test_rollback_then_redo(sf):
+    spec, shape = shape_pair(n_layers=2)
+    g = gpu_stage(sf, shape, 0, 1, True, True)
+    prompt = so.synth_tokens(3, "p", 10, spec.vocab)
+    g.begin_token_ids("r", prompt)
+    a = g.begin_token_ids("r", [5])
+    g.rollback_kv("r", 10)
+    b = g.begin_token_ids("r", [5])
+    assert np.array_equal(a, b)
+
+
+def test_generate_greedy_matches_oracle_64_steps(sf):
+    """Greedy stream identity for 64 steps (small model; the full-size case is below)."""
+    spec, shape = shape_pair(n_layers=3, vocab=8192)
+    g = gpu_stage(sf, shape, 0, 2, True, True)
+    o = oracle_stage(spec, 0, 2, True, True)
+    prompt = so.synth_tokens(8, "p", 16, spec.vocab)
+    got = g.generate_greedy("r", prompt, 64)
+    toks, h = [], o.begin_token_ids("r", prompt)
+    for _ in range(64):
+        t = o.sample_tail(h[-1])[0]
+        toks.append(t)
+        h = o.begin_token_ids("r", [t])
+    assert got.tolist() == toks
+
+
+def test_verify_greedy(sf):
+    spec, shape = shape_pair(n_layers=2)
+    g = gpu_stage(sf, shape, 0, 1, True, True)
+    prompt = so.synth_tokens(8, "p", 12, spec.vocab)
+    ref = g.generate_greedy("ref", prompt, 5)
+    g.begin_token_ids("v", prompt)
+    drafts = np.array([ref[1], ref[2], 7, ref[4]], np.uint32)
+    # feed [last, d1..d4] as single-token appends: rows 0..4
+    hs = [g.begin_token_ids("v", [t]) for t in np.concatenate([[ref[0]], drafts])]
+    acc, bonus = g.verify_greedy(np.concatenate(hs), drafts)
+    assert acc == 2 and bonus == ref[3]
+
+
+@pytest.mark.parametrize("kv_f32", [False])
+def test_full_size_greedy_64_steps(sf, kv_f32):
+    """The graded model shape: 42 layers, d_model 2560, vocab 262144, Q4_K_M, greedy 64 steps."""
+    spec, shape = shape_pair(hidden=2560, n_heads=8, n_kv=4, head_dim=256, ffn=10240, vocab=262144, n_layers=42,
+                             seed=0x5EED)
+    g = sf.CudaStageBackend(synthetic=shape, rope_theta=10000.0, kv_f32=kv_f32, max_ctx=512,
+                            max_sessions=2).load_layout("m", "full", 0, 41, True, True)
+    prompt = so.synth_tokens(17, "prompt", 8, spec.vocab)
+    got = g.generate_greedy("r", prompt, 64)
+    g.close()
+    o = oracle_stage(spec, 0, 41, True, True, kv_fp16=not kv_f32)
+    toks, h = [], o.begin_token_ids("r", prompt)
+    for _ in range(64):
+        t = o.sample_tail(h[-1])[0]
+        toks.append(t)
+        h = o.begin_token_ids("r", [t])
+    assert got.tolist() == toks
