@@ -41,35 +41,24 @@ struct XSlice {
   float sum[2];
 };
 
-__device__ __forceinline__ void load_xslice(const float *__restrict__ x, int blk, int j, int h, int lane,
-                                            XSlice &xs) {
-  const float *base = x + blk * QK_K + j * 64 + h * 16;
-  float v[2][16];
-#pragma unroll
-  for (int half = 0; half < 2; ++half)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float4 f = *reinterpret_cast<const float4 *>(base + half * 32 + 4 * k);
-      v[half][4 * k + 0] = f.x;
-      v[half][4 * k + 1] = f.y;
-      v[half][4 * k + 2] = f.z;
-      v[half][4 * k + 3] = f.w;
-    }
+// Split this thread's 32 activations into exact digit planes (see file header); the block
+// exponent is shared by the 8 slices (8 consecutive lanes) of one 256-element block.
+__device__ __forceinline__ void quantize_slice(const float (&v)[2][16], int lane, XSlice &xs) {
   float m = 0.f;
 #pragma unroll
   for (int half = 0; half < 2; ++half)
 #pragma unroll
     for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[half][i]));
-  // max over the 8 slices of this 256-block (8 consecutive lanes)
   const unsigned seg = 0xFFu << (lane & 24);
   m = fmaxf(m, __shfl_xor_sync(seg, m, 1));
   m = fmaxf(m, __shfl_xor_sync(seg, m, 2));
   m = fmaxf(m, __shfl_xor_sync(seg, m, 4));
-  int E = 0;
-  if (m > 0.f) frexpf(m, &E);  // m < 2^E
+  // m < 2^E with E = biased exponent - 126 (zero and subnormal maxima clamp to E = -100)
+  int E = int((__float_as_uint(m) >> 23) & 0xFF) - 126;
   if (E < -100) E = -100;
-  const int up = 22 - E;  // x * 2^up has magnitude < 2^22
-  xs.scale = ldexpf(1.0f, -up);
+  const int up = 22 - E;  // x * 2^up has magnitude < 2^22; up in [-106, 122]
+  const float pw = __uint_as_float(uint32_t(127 + up) << 23);  // 2^up, a normal float
+  xs.scale = __uint_as_float(uint32_t(127 - up) << 23);        // 2^-up
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     int isum = 0;
@@ -78,12 +67,12 @@ __device__ __forceinline__ void load_xslice(const float *__restrict__ x, int blk
       uint32_t pa = 0, pb = 0, pc = 0;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        int X = __float2int_rn(ldexpf(v[half][4 * w + k], up));
+        const int X = __float2int_rn(v[half][4 * w + k] * pw);  // exact power-of-two scaling
         isum += X;
-        int c = (X << 24) >> 24;
-        int X1 = (X - c) >> 8;
-        int b = (X1 << 24) >> 24;
-        int a = (X1 - b) >> 8;
+        const int c = (X << 24) >> 24;
+        const int X1 = (X - c) >> 8;
+        const int b = (X1 << 24) >> 24;
+        const int a = (X1 - b) >> 8;
         pa |= uint32_t(a & 0xFF) << (8 * k);
         pb |= uint32_t(b & 0xFF) << (8 * k);
         pc |= uint32_t(c & 0xFF) << (8 * k);
@@ -126,17 +115,11 @@ __device__ __forceinline__ void q4k_slice(const uint8_t *__restrict__ row, int b
     const uint32_t b0a = (s0 >> (8 * k)) & 0xFF, b1a = (s1 >> (8 * k)) & 0xFF, b2a = (s2 >> (8 * k)) & 0xFF;
     const uint32_t b0b = (s0 >> (8 * k + 8)) & 0xFF, b1b = (s1 >> (8 * k + 8)) & 0xFF,
                    b2b = (s2 >> (8 * k + 8)) & 0xFF;
-    if (j < 2) {
-      scA = b0a & 63;
-      mA = b1a & 63;
-      scB = b0b & 63;
-      mB = b1b & 63;
-    } else {
-      scA = (b2a & 15) | ((b0a >> 6) << 4);
-      mA = (b2a >> 4) | ((b1a >> 6) << 4);
-      scB = (b2b & 15) | ((b0b >> 6) << 4);
-      mB = (b2b >> 4) | ((b1b >> 6) << 4);
-    }
+    const bool lo = j < 2;  // selects, not branches: j differs across the lanes of a warp
+    scA = lo ? int(b0a & 63) : int((b2a & 15) | ((b0a >> 6) << 4));
+    mA = lo ? int(b1a & 63) : int((b2a >> 4) | ((b1a >> 6) << 4));
+    scB = lo ? int(b0b & 63) : int((b2b & 15) | ((b0b >> 6) << 4));
+    mB = lo ? int(b1b & 63) : int((b2b >> 4) | ((b1b >> 6) << 4));
   }
   uint32_t lo[4], hi[4];
   lo[0] = qv.x & 0x0F0F0F0Fu;
@@ -198,106 +181,197 @@ __device__ __forceinline__ float gelu_tanh_mul(float v, float u) {
 }
 
 // ---------------------------------------------------------------- kernel
+constexpr int MAX_SEG = 3;
+
 struct QGemvArgs {
-  const uint8_t *w[2];  // NMAT matrices, device layout
-  const float *x;       // [T][K]
-  float *y;             // [T][rows] (NMAT==1) or GeGLU act [T][rows] (NMAT==2)
-  int64_t rows;
-  int nb;               // K / 256
-  int row_bytes;        // device-layout bytes per row (multiple of 16)
-  int groups;           // row groups per CTA
-  int rows_per_stage;
+  GemvSeg seg[MAX_SEG];
+  int nseg;
+  int64_t total_rows;
+  int nb;
+  int groups;
   int nstage;
-  int ldy;              // row stride of y in floats (>= rows)
+  int stage_bytes;
+  int rps_max;
+  GemvPrologue pro;
   unsigned *err;
 };
 
-template <int TYPE, int NMAT, int T>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs a) {
+// Segments let one launch cover several matrices with the same K (q, k and v of a layer):
+// the CTAs split the concatenated row space evenly and each stage stays inside one segment.
+template <int NMAT, int T>
+__global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(const QGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float pro_red[GEMV_THREADS / 32];
   const int tid = threadIdx.x;
   const int S = a.nb * 8;
   const int g = tid / S, s = tid % S;
   const int blk = s >> 3, j = (s >> 1) & 3, h = s & 1;
   const int lane = tid & 31;
-  const bool active = g < a.groups;
+  const int K = a.nb * QK_K;
 
-  // CTA row range
-  const int64_t r_begin = a.rows * blockIdx.x / gridDim.x;
-  const int64_t r_end = a.rows * (blockIdx.x + 1) / gridDim.x;
-  const int n_rows = int(r_end - r_begin);
-  const int n_iter = (n_rows + a.rows_per_stage - 1) / a.rows_per_stage;
-  const int stage_bytes = a.rows_per_stage * a.row_bytes * NMAT;
+  const int64_t r_begin = a.total_rows * blockIdx.x / gridDim.x;
+  const int64_t r_end = a.total_rows * (blockIdx.x + 1) / gridDim.x;
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-  float *red = reinterpret_cast<float *>(smem + 128);  // [2][rows_per_stage][NMAT][T][nb]
-  const int red_stride = a.rows_per_stage * NMAT * T * a.nb;
+  float *red = reinterpret_cast<float *>(smem + 128);  // [2][rps_max][NMAT][T][nb]
+  const int red_stride = a.rps_max * NMAT * T * a.nb;
   uint8_t *stages = smem + 128 + ((2 * red_stride * 4 + 127) / 128) * 128;
 
-  auto issue = [&](int it) {
-    const int slot = it % a.nstage;
-    const int64_t r0 = r_begin + int64_t(it) * a.rows_per_stage;
-    const int nr = int(r_end - r0 < a.rows_per_stage ? r_end - r0 : a.rows_per_stage);
-    const uint32_t bytes = uint32_t(nr) * a.row_bytes;
+  // stage at global row `pos`: segment, first local row, row count
+  auto stage_at = [&](int64_t pos, int &sg, int64_t &local0, int &nr) {
+    int64_t base = 0;
+    sg = 0;
+    while (sg + 1 < a.nseg && pos >= base + a.seg[sg].rows) base += a.seg[sg++].rows;
+    local0 = pos - base;
+    int64_t n = a.seg[sg].rps;
+    if (r_end - pos < n) n = r_end - pos;
+    if (a.seg[sg].rows - local0 < n) n = a.seg[sg].rows - local0;
+    nr = int(n);
+  };
+  int64_t ppos = r_begin;  // producer cursor (thread 0 only)
+  int pit = 0;
+  auto issue_next = [&]() {
+    int sg, nr;
+    int64_t l0;
+    stage_at(ppos, sg, l0, nr);
+    const GemvSeg &G = a.seg[sg];
+    const int slot = pit % a.nstage;
+    const uint32_t bytes = uint32_t(nr) * G.row_bytes;
     mbar_arrive_expect_tx(&bars[slot], bytes * NMAT);
 #pragma unroll
     for (int m = 0; m < NMAT; ++m)
-      bulk_g2s(stages + slot * stage_bytes + m * a.rows_per_stage * a.row_bytes, a.w[m] + r0 * a.row_bytes,
-               bytes, &bars[slot]);
+      bulk_g2s(stages + slot * a.stage_bytes + m * G.rps * G.row_bytes, G.w[m] + l0 * G.row_bytes, bytes,
+               &bars[slot]);
+    ppos += nr;
+    ++pit;
   };
 
   if (tid == 0) {
     for (int i = 0; i < a.nstage; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
-    // Weights do not depend on the previous kernel: start streaming them before the
-    // dependency wait so their fetch overlaps the producer's tail.
-    for (int it = 0; it < min(a.nstage, n_iter); ++it) issue(it);
+    // Weights never depend on the previous kernel: stream them before the dependency wait so
+    // their fetch overlaps the producer's tail (programmatic dependent launch).
+    while (pit < a.nstage && ppos < r_end) issue_next();
   }
   pdl_wait();
   pdl_launch_dependents();
 
+  // ---- activations: optional fused residual add + RMSNorm, then exact digit planes
   XSlice xs[T];
-  if (active) {
+  {
+    const GemvPrologue &P = a.pro;
+    const int base = blk * QK_K + j * 64 + h * 16;
+    // sum over row group 0 (whose slices cover K exactly once), identical in every thread
+    auto block_sum = [&](float val) {
+      float x = warp_sum(g == 0 ? val : 0.f);
+      if (lane == 0) pro_red[tid >> 5] = x;
+      __syncthreads();
+      float sum = 0.f;
+      for (int w = 0; w < int(blockDim.x + 31) / 32; ++w) sum += pro_red[w];
+      __syncthreads();
+      return sum;
+    };
 #pragma unroll
-    for (int t = 0; t < T; ++t) load_xslice(a.x + int64_t(t) * a.nb * QK_K, blk, j, h, lane, xs[t]);
+    for (int t = 0; t < T; ++t) {
+      const float *src = (P.mode == 0 ? P.x : P.a) + int64_t(t) * K + base;
+      float v[2][16];
+      float ssq = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 f = *reinterpret_cast<const float4 *>(src + half * 32 + 4 * k);
+          v[half][4 * k] = f.x;
+          v[half][4 * k + 1] = f.y;
+          v[half][4 * k + 2] = f.z;
+          v[half][4 * k + 3] = f.w;
+          ssq += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
+        }
+      if (P.mode != 0) {
+        const bool norm_a = P.mode == 1 || P.w_post;
+        const float s1 = norm_a ? 1.0f / sqrtf(block_sum(ssq) / float(K) + P.eps) : 1.0f;
+        float ssr = 0.f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int idx = base + half * 32 + i;
+            float r = v[half][i];
+            if (P.mode == 1) {
+              r = r * s1;  // (x * scale) * w, real_math.rs:43
+            } else {
+              r = (P.w_post ? (r * s1) * P.w_post[idx] : r) + P.resid_in[int64_t(t) * K + idx];
+              if (P.scale) r = r * P.scale[0];
+            }
+            v[half][i] = r;
+            ssr += r * r;
+          }
+        if (P.mode == 2 && P.resid_out && blockIdx.x == 0 && g == 0) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              *reinterpret_cast<float4 *>(P.resid_out + int64_t(t) * K + base + half * 32 + 4 * k) =
+                  make_float4(v[half][4 * k], v[half][4 * k + 1], v[half][4 * k + 2], v[half][4 * k + 3]);
+        }
+        const float s2 = (P.mode == 2 && P.w_next) ? 1.0f / sqrtf(block_sum(ssr) / float(K) + P.eps) : 1.0f;
+        if (P.w_next) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[half][i] = (v[half][i] * s2) * P.w_next[base + half * 32 + i];
+        }
+      }
+      quantize_slice(v, lane, xs[t]);
+    }
   }
   __syncthreads();  // barrier inits visible to all threads
 
   const unsigned seg = 0xFFu << (lane & 24);
-  for (int it = 0; it < n_iter; ++it) {
+  int64_t pos = r_begin;
+  for (int it = 0; pos < r_end; ++it) {
+    int sg, nr;
+    int64_t l0;
+    stage_at(pos, sg, l0, nr);
+    const GemvSeg &G = a.seg[sg];
     const int slot = it % a.nstage;
-    const int64_t r0 = r_begin + int64_t(it) * a.rows_per_stage;
-    const int nr = int(r_end - r0 < a.rows_per_stage ? r_end - r0 : a.rows_per_stage);
     mbar_wait_bounded(&bars[slot], (it / a.nstage) & 1, a.err);
-    const uint8_t *st = stages + slot * stage_bytes;
+    const uint8_t *st = stages + slot * a.stage_bytes;
     float *rd = red + (it & 1) * red_stride;
-    if (active) {
-      for (int lr = g; lr < nr; lr += a.groups) {
-        float acc[NMAT][T];
+    const bool q4 = G.type == T_Q4_K;
+    for (int lr = g; lr < nr; lr += 2 * a.groups) {
+      const int lr2 = lr + a.groups < nr ? lr + a.groups : lr;  // second row in flight (ILP)
+      float acc[2][NMAT][T];
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
+      for (int m = 0; m < NMAT; ++m) {
 #pragma unroll
-          for (int t = 0; t < T; ++t) acc[m][t] = 0.f;
-          const uint8_t *row = st + (m * a.rows_per_stage + lr) * a.row_bytes;
-          if (TYPE == T_Q4_K)
-            q4k_slice<T>(row, blk, j, h, xs, acc[m]);
-          else
-            q6k_slice<T>(row, a.nb, blk, j, h, xs, acc[m]);
+        for (int t = 0; t < T; ++t) acc[0][m][t] = acc[1][m][t] = 0.f;
+        const uint8_t *row0 = st + (m * G.rps + lr) * G.row_bytes;
+        const uint8_t *row1 = st + (m * G.rps + lr2) * G.row_bytes;
+        if (q4) {
+          q4k_slice<T>(row0, blk, j, h, xs, acc[0][m]);
+          q4k_slice<T>(row1, blk, j, h, xs, acc[1][m]);
+        } else {
+          q6k_slice<T>(row0, a.nb, blk, j, h, xs, acc[0][m]);
+          q6k_slice<T>(row1, a.nb, blk, j, h, xs, acc[1][m]);
         }
+      }
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
 #pragma unroll
           for (int t = 0; t < T; ++t) {
-            float v = acc[m][t];
+            float v = acc[rr][m][t];
             v += __shfl_xor_sync(seg, v, 1);
             v += __shfl_xor_sync(seg, v, 2);
             v += __shfl_xor_sync(seg, v, 4);
-            if ((s & 7) == 0) rd[((lr * NMAT + m) * T + t) * a.nb + blk] = v;
+            const int row = rr ? lr2 : lr;
+            if ((s & 7) == 0 && (rr == 0 || lr2 != lr)) rd[((row * NMAT + m) * T + t) * a.nb + blk] = v;
           }
-      }
     }
     __syncthreads();  // stage slot fully consumed; partials complete
-    if (tid == 0 && it + a.nstage < n_iter) issue(it + a.nstage);
+    if (tid == 0 && ppos < r_end) issue_next();
     for (int idx = tid; idx < nr * T; idx += blockDim.x) {
       const int lr = idx / T, t = idx % T;
       float v[NMAT];
@@ -308,10 +382,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs 
         for (int b = 0; b < a.nb; ++b) sum += p[b];
         v[m] = sum;
       }
-      float out = v[0];
-      if (NMAT == 2) out = gelu_tanh_mul(v[0], v[NMAT - 1]);
-      a.y[int64_t(t) * a.ldy + r0 + lr] = out;
+      G.y[int64_t(t) * G.ldy + l0 + lr] = NMAT == 2 ? gelu_tanh_mul(v[0], v[NMAT - 1]) : v[0];
     }
+    pos += nr;
   }
 }
 
@@ -448,40 +521,72 @@ unsigned *device_error_ptr() {
   return cache[dev];
 }
 
-constexpr int GEMV_SMEM_BUDGET = 200 * 1024;
 constexpr int GEMV_STAGE_TARGET = 24 * 1024;
 
-template <int TYPE, int NMAT, int T>
+template <int NMAT, int T>
 static cudaError_t launch_qgemv_t(QGemvArgs a, cudaStream_t st) {
-  auto kern = qgemv_kernel<TYPE, NMAT, T>;
-  const int S = a.nb * 8;
-  a.groups = GEMV_THREADS / S;
-  const int per_row = a.row_bytes * NMAT;
-  int rps = (GEMV_STAGE_TARGET / per_row) / a.groups * a.groups;
-  if (rps < a.groups) rps = a.groups;
-  a.rows_per_stage = rps;
-  const int stage_bytes = rps * per_row;
-  const int red_bytes = ((2 * rps * NMAT * T * a.nb * 4 + 127) / 128) * 128;
-  int nst = (GEMV_SMEM_BUDGET - 128 - red_bytes) / stage_bytes;
+  auto kern = qgemv_kernel<NMAT, T>;
+  const int ctas_per_sm = T == 1 ? 2 : 1;
+  const int budget = T == 1 ? 100 * 1024 : 200 * 1024;  // two CTAs (or two kernels) per SM when T == 1
+  const int red_bytes = ((2 * a.rps_max * NMAT * T * a.nb * 4 + 127) / 128) * 128;
+  int nst = (budget - 128 - red_bytes) / a.stage_bytes;
   if (nst > 8) nst = 8;
   if (nst < 1) return cudaErrorInvalidValue;
   a.nstage = nst;
-  const size_t smem = 128 + red_bytes + size_t(nst) * stage_bytes;
+  const size_t smem = 128 + red_bytes + size_t(nst) * a.stage_bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  int64_t ctas = (a.rows + a.groups - 1) / a.groups;
-  if (ctas > num_sms()) ctas = num_sms();
-  return launch_pdl(kern, dim3(unsigned(ctas)), dim3(a.groups * S), smem, st, a);
+  int64_t ctas = (a.total_rows + a.groups - 1) / a.groups;
+  if (ctas > int64_t(ctas_per_sm) * num_sms()) ctas = int64_t(ctas_per_sm) * num_sms();
+  return launch_pdl(kern, dim3(unsigned(ctas)), dim3(a.groups * a.nb * 8), smem, st, a);
 }
 
-template <int TYPE, int NMAT>
-static cudaError_t launch_qgemv_n(QGemvArgs a, int T, cudaStream_t st) {
+template <int NMAT>
+static cudaError_t launch_qgemv_n(const QGemvArgs &a, int T, cudaStream_t st) {
   switch (T) {
-    case 1: return launch_qgemv_t<TYPE, NMAT, 1>(a, st);
-    case 2: return launch_qgemv_t<TYPE, NMAT, 2>(a, st);
-    case 3: return launch_qgemv_t<TYPE, NMAT, 3>(a, st);
-    default: return launch_qgemv_t<TYPE, NMAT, 4>(a, st);
+    case 1: return launch_qgemv_t<NMAT, 1>(a, st);
+    case 2: return launch_qgemv_t<NMAT, 2>(a, st);
+    case 3: return launch_qgemv_t<NMAT, 3>(a, st);
+    default: return launch_qgemv_t<NMAT, 4>(a, st);
   }
+}
+
+cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvPrologue pro, int64_t n_tok,
+                       cudaStream_t st) {
+  if (n_tok <= 0) return cudaSuccess;
+  if (nseg < 1 || nseg > MAX_SEG || (nmat != 1 && nmat != 2)) return cudaErrorInvalidValue;
+  if (K % QK_K || K / QK_K * 8 > GEMV_THREADS) return cudaErrorInvalidValue;
+  QGemvArgs a = {};
+  a.nseg = nseg;
+  a.nb = int(K / QK_K);
+  a.groups = GEMV_THREADS / (a.nb * 8);
+  a.err = device_error_ptr();
+  a.pro = pro;
+  for (int i = 0; i < nseg; ++i) {
+    GemvSeg sg = segs[i];
+    if (sg.type != T_Q4_K && sg.type != T_Q6_K) return cudaErrorInvalidValue;
+    if (!sg.w[0] || (nmat == 2 && !sg.w[1]) || sg.rows <= 0) return cudaErrorInvalidValue;
+    sg.row_bytes = device_row_bytes(sg.type, K);
+    int rps = (GEMV_STAGE_TARGET / (sg.row_bytes * nmat)) / a.groups * a.groups;
+    if (rps < a.groups) rps = a.groups;
+    sg.rps = rps;
+    if (rps * sg.row_bytes * nmat > a.stage_bytes) a.stage_bytes = rps * sg.row_bytes * nmat;
+    if (rps > a.rps_max) a.rps_max = rps;
+    a.seg[i] = sg;
+    a.total_rows += sg.rows;
+  }
+  for (int64_t t0 = 0; t0 < n_tok; t0 += GEMV_MAX_T) {
+    const int T = int(n_tok - t0 < GEMV_MAX_T ? n_tok - t0 : GEMV_MAX_T);
+    QGemvArgs c = a;
+    if (c.pro.x) c.pro.x += t0 * K;
+    if (c.pro.a) c.pro.a += t0 * K;
+    if (c.pro.resid_in) c.pro.resid_in += t0 * K;
+    if (c.pro.resid_out) c.pro.resid_out += t0 * K;
+    for (int i = 0; i < nseg; ++i) c.seg[i].y += t0 * c.seg[i].ldy;
+    const cudaError_t e = nmat == 2 ? launch_qgemv_n<2>(c, T, st) : launch_qgemv_n<1>(c, T, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t gemv(int type, const void *w0, const void *w1, int64_t rows, int64_t K, const float *x, int64_t n_tok,
@@ -489,27 +594,17 @@ cudaError_t gemv(int type, const void *w0, const void *w1, int64_t rows, int64_t
   if (rows <= 0 || n_tok <= 0) return cudaSuccess;
   const int nmat = w1 ? 2 : 1;
   if (type == T_Q4_K || type == T_Q6_K) {
-    if (K % QK_K || K / QK_K * 8 > GEMV_THREADS) return cudaErrorInvalidValue;
-    QGemvArgs a = {};
-    a.w[0] = static_cast<const uint8_t *>(w0);
-    a.w[1] = static_cast<const uint8_t *>(w1 ? w1 : w0);
-    a.rows = rows;
-    a.nb = int(K / QK_K);
-    a.row_bytes = device_row_bytes(type, K);
-    a.ldy = int(ldy);
-    a.err = device_error_ptr();
-    for (int64_t t0 = 0; t0 < n_tok; t0 += GEMV_MAX_T) {
-      const int T = int(n_tok - t0 < GEMV_MAX_T ? n_tok - t0 : GEMV_MAX_T);
-      a.x = x + t0 * K;
-      a.y = y + t0 * ldy;
-      cudaError_t e;
-      if (type == T_Q4_K)
-        e = nmat == 2 ? launch_qgemv_n<T_Q4_K, 2>(a, T, st) : launch_qgemv_n<T_Q4_K, 1>(a, T, st);
-      else
-        e = nmat == 2 ? launch_qgemv_n<T_Q6_K, 2>(a, T, st) : launch_qgemv_n<T_Q6_K, 1>(a, T, st);
-      if (e != cudaSuccess) return e;
-    }
-    return cudaSuccess;
+    GemvSeg sg = {};
+    sg.w[0] = static_cast<const uint8_t *>(w0);
+    sg.w[1] = static_cast<const uint8_t *>(w1);
+    sg.y = y;
+    sg.rows = rows;
+    sg.type = type;
+    sg.ldy = int(ldy);
+    GemvPrologue pro = {};
+    pro.mode = 0;
+    pro.x = x;
+    return gemv_fused(&sg, 1, nmat, K, pro, n_tok, st);
   }
   const int threads = 256;
   int64_t blocks = (rows * 32 + threads - 1) / threads;

@@ -51,6 +51,30 @@ cudaError_t dequantize(int type, const void *w_gguf, int64_t n_rows, int64_t K, 
 cudaError_t gemv(int type, const void *w0, const void *w1, int64_t rows, int64_t K, const float *x, int64_t n_tok,
                  float *y, int64_t ldy, cudaStream_t st);
 
+// One matrix (or gate/up pair) of a fused K-quant GEMV launch; all segments share K.
+struct GemvSeg {
+  const uint8_t *w[2];  // device layout; w[1] only for pairs
+  float *y;             // output rows [T][ldy]
+  int64_t rows;
+  int type;             // T_Q4_K or T_Q6_K
+  int row_bytes;        // filled by the launcher
+  int rps;              // rows per stage, filled by the launcher
+  int ldy;
+};
+// How the launch forms x:  mode 0: x given;  mode 1: x = rms_norm(a) * w_next;
+// mode 2: r = resid_in + (w_post ? rms_norm(a) * w_post : a), r *= scale, resid_out = r (CTA 0),
+//         x = w_next ? rms_norm(r) * w_next : r.   resid_out must not alias resid_in.
+struct GemvPrologue {
+  int mode;
+  const float *x, *a, *resid_in;
+  float *resid_out;
+  const float *w_post, *scale, *w_next;
+  float eps;
+};
+// K-quant GEMV over 1..3 segments (nmat = 2: every segment is a gate/up pair with GeGLU).
+cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvPrologue pro, int64_t n_tok,
+                       cudaStream_t st);
+
 // ---- elementwise / norms / attention (ops.cu)
 // out[t] = rms_norm(x[t]) * w   (real_math.rs:30-47)
 cudaError_t rms_norm(const float *x, const float *w, int64_t n_tok, int dim, float eps, float *out, cudaStream_t st);

@@ -260,6 +260,8 @@ struct sfc_stage {
   int64_t kv_slot_stride = 0;  // elements
   int64_t kv_bytes = 0;
   // activations
+  float *resid2 = nullptr;  // residual ping-pong partner for the fused GEMV prologues
+  bool fused = false;       // every layer matrix is a K-quant the fused GEMV handles
   float *resid = nullptr, *xn = nullptr, *proj = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
         *act = nullptr, *hn = nullptr, *score_dev = nullptr;
   uint32_t *ids_dev = nullptr;
@@ -489,6 +491,14 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
     SFC_REQUIRE(h->logits_w && h->output_norm, "tail without layers needs logits tensors");
     h->hidden = int(h->output_norm->dims[0]);
   }
+  h->fused = !h->layers.empty() && h->hidden % 256 == 0 && h->q_dim % 256 == 0 && h->ffn % 256 == 0 &&
+             h->hidden <= 10240 && h->q_dim <= 10240 && h->ffn <= 10240;
+  for (auto &L : h->layers)
+    for (DevTensor *t : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
+      if (t->type != T_Q4_K && t->type != T_Q6_K) h->fused = false;
+  if (h->output_norm)
+    SFC_REQUIRE(h->output_norm->in_dim == h->hidden, "output_norm.weight has %lld elements but hidden is %d",
+                (long long)h->output_norm->in_dim, h->hidden);
   if (h->token_embd) {
     SFC_REQUIRE(h->token_embd->dims.size() == 2 && h->token_embd->dims[0] == h->hidden,
                 "token_embd.weight dims do not match hidden %d", h->hidden);
@@ -584,7 +594,8 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   };
   int rc;
   const int64_t H = h->hidden;
-  if ((rc = alloc((void **)&h->resid, T * H * 4)) || (rc = alloc((void **)&h->xn, T * H * 4)) ||
+  if ((rc = alloc((void **)&h->resid, T * H * 4)) || (rc = alloc((void **)&h->resid2, T * H * 4)) ||
+      (rc = alloc((void **)&h->xn, T * H * 4)) ||
       (rc = alloc((void **)&h->proj, T * H * 4)) || (rc = alloc((void **)&h->q, T * std::max(h->q_dim, 1) * 4)) ||
       (rc = alloc((void **)&h->k, T * std::max(h->k_dim, 1) * 4)) ||
       (rc = alloc((void **)&h->v, T * std::max(h->k_dim, 1) * 4)) ||
@@ -628,7 +639,7 @@ void destroy_stage(sfc_stage *h) {
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
   if (h->decode_graph) cudaGraphExecDestroy(h->decode_graph);
-  for (void *p : {(void *)h->resid, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
+  for (void *p : {(void *)h->resid, (void *)h->resid2, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
                   (void *)h->seq_dev, h->scratch, h->kv_arena, h->weight_arena})
@@ -691,8 +702,83 @@ AttnParams attn_params(sfc_stage *h, const Layer &L) {
 
 #define F32P(t) ((t) ? static_cast<const float *>((t)->dev) : nullptr)
 
+GemvSeg seg_of(const DevTensor *w, const DevTensor *w2, float *y, int64_t ldy) {
+  GemvSeg g = {};
+  g.w[0] = static_cast<const uint8_t *>(w->dev);
+  g.w[1] = w2 ? static_cast<const uint8_t *>(w2->dev) : nullptr;
+  g.y = y;
+  g.rows = w->rows;
+  g.type = w->type;
+  g.ldy = int(ldy);
+  return g;
+}
+
+// Fused layer loop for K-quant stages: the residual add + RMSNorm that precede the q/k/v and
+// gate/up projections run in those GEMVs' prologues (real_forward.rs:1690-1696 and :1738-1749),
+// so a layer is 5-6 launches.  Residual rows ping-pong between h->resid and h->resid2.
+cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  const int H = h->hidden;
+  float *cur = h->resid, *other = h->resid2;
+  for (size_t li = 0; li < h->layers.size(); ++li) {
+    const Layer &L = h->layers[li];
+    GemvPrologue pro = {};
+    pro.eps = h->eps;
+    pro.w_next = F32P(L.attn_norm);
+    if (li == 0) {
+      pro.mode = L.attn_norm ? 1 : 0;
+      pro.x = cur;
+      pro.a = cur;
+    } else {
+      const Layer &P = h->layers[li - 1];
+      pro.mode = 2;
+      pro.a = h->proj;
+      pro.resid_in = cur;
+      pro.resid_out = other;
+      pro.w_post = F32P(P.post_ffw);
+      pro.scale = F32P(P.scale);
+      std::swap(cur, other);
+    }
+    const GemvSeg qkv[3] = {seg_of(L.q, nullptr, h->q, h->q_dim), seg_of(L.k, nullptr, h->k, h->k_dim),
+                            seg_of(L.v, nullptr, h->v, h->k_dim)};
+    if ((e = gemv_fused(qkv, 3, 1, H, pro, T, st))) return e;
+    const AttnParams ap = attn_params(h, L);
+    const KVLayer kv = kv_layer(h, li);
+    if ((e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev, T, ap, st))) return e;
+    if ((e = attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, nullptr, nullptr, T, max_keys, ap, h->scratch,
+                       h->attn_scratch, st)))
+      return e;
+    const GemvSeg o = seg_of(L.o, nullptr, h->proj, H);
+    GemvPrologue po = {};
+    po.mode = 0;
+    po.x = h->att;
+    if ((e = gemv_fused(&o, 1, 1, h->q_dim, po, T, st))) return e;
+    GemvPrologue pf = {};
+    pf.mode = 2;
+    pf.eps = h->eps;
+    pf.a = h->proj;
+    pf.resid_in = cur;
+    pf.resid_out = other;
+    pf.w_post = F32P(L.post_attn);
+    pf.w_next = F32P(L.ffn_norm);
+    std::swap(cur, other);
+    const GemvSeg gu = seg_of(L.gate, L.up, h->act, h->ffn);
+    if ((e = gemv_fused(&gu, 1, 2, H, pf, T, st))) return e;
+    const GemvSeg d = seg_of(L.down, nullptr, h->proj, H);
+    GemvPrologue pd = {};
+    pd.mode = 0;
+    pd.x = h->act;
+    if ((e = gemv_fused(&d, 1, 1, h->ffn, pd, T, st))) return e;
+  }
+  const Layer &Z = h->layers.back();
+  if ((e = add_norm(cur, h->proj, F32P(Z.post_ffw), F32P(Z.scale), 0, nullptr, nullptr, T, H, h->eps, st))) return e;
+  if (cur != h->resid) e = cudaMemcpyAsync(h->resid, cur, size_t(T) * H * 4, cudaMemcpyDeviceToDevice, st);
+  return e;
+}
+
 // All layers over the T rows in h->resid (device tables already uploaded).
 cudaError_t run_layers(sfc_stage *h, int64_t T, int64_t max_keys, cudaStream_t st) {
+  if (h->fused) return run_layers_fused(h, T, max_keys, st);
   cudaError_t e = cudaSuccess;
   const int H = h->hidden;
   for (size_t li = 0; li < h->layers.size(); ++li) {

@@ -55,12 +55,13 @@ __global__ void synth_q4k_kernel(uint64_t key, int64_t n_blocks, float sigma, ui
   const uint16_t dm = f2h_bits(__fmul_rn(fabsf(synth_normal(key, base + 1)), sigma));
   uint32_t *p32 = reinterpret_cast<uint32_t *>(p);  // 144 B blocks are 16 B aligned
   p32[0] = uint32_t(d) | (uint32_t(dm) << 16);
-  // bytes 4..143: u64 word k supplies bytes 4 + 8k .. 11 + 8k
-  for (int k = 0; k < 18; ++k) {
+  // bytes 4..143: u64 word k supplies bytes 4 + 8k .. 11 + 8k (the 18th word only its low half)
+  for (int k = 0; k < 17; ++k) {
     const uint64_t r = mix64(key, base + 2 + k);
     p32[1 + 2 * k] = uint32_t(r);
     p32[2 + 2 * k] = uint32_t(r >> 32);
   }
+  p32[35] = uint32_t(mix64(key, base + 2 + 17));
 }
 
 __global__ void synth_q6k_kernel(uint64_t key, int64_t n_blocks, float sigma, uint8_t *__restrict__ out) {

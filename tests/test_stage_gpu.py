@@ -37,6 +37,22 @@ def gpu_stage(sf, shape, start, end, head, tail, kv_f32=False, **kw):
                                **kw).load_layout("m", f"s{start}", start, end, head, tail)
 
 
+# Stage outputs with an fp16 KV cache are compared with the oracle's fp16-rounded cache.  The two
+# paths differ by ~1e-7 before rounding, so a cached K/V element can land on the other side of an
+# fp16 rounding boundary (one fp16 ulp = 2^-11 relative); this synthetic model's attention has no
+# 1/sqrt(d) scale (real_math.rs:2697-2744) and is sharply peaked, so such flips move hidden states
+# by up to ~1e-2 after a few decode steps.  For the fp16 cache the bar is therefore identical greedy
+# tokens at every step plus 1e-2 normwise; with the f32 cache (the reference's own precision) the
+# strict 1e-3 bar applies to every hidden state.
+def stage_close(got, ref, kv_f32, what):
+    from gpu_util import rel_errors
+    norm, mx = rel_errors(got, ref)
+    if kv_f32:
+        assert norm <= 1e-3 and mx <= 1e-3, f"{what}: normwise {norm:.3e}, max/max {mx:.3e}"
+    else:
+        assert norm <= 1e-2, f"{what}: normwise {norm:.3e} (fp16 KV)"
+
+
 @pytest.mark.parametrize("kv_f32", [False, True])
 def test_two_stage_prefill_decode_matches_oracle(sf, kv_f32):
     spec, shape = shape_pair()
@@ -44,16 +60,16 @@ def test_two_stage_prefill_decode_matches_oracle(sf, kv_f32):
     gh, gt = gpu_stage(sf, shape, 0, 1, True, False, kv_f32), gpu_stage(sf, shape, 2, 3, False, True, kv_f32)
     prompt = so.synth_tokens(4, "p", 37, spec.vocab)
     h_o, h_g = oh.begin_token_ids("r", prompt), gh.begin_token_ids("r", prompt)
-    assert_close(h_g, h_o, what="head prefill")
+    stage_close(h_g, h_o, kv_f32, "head prefill")
     t_o, t_g = ot.continue_forward("r", h_o), gt.continue_forward("r", h_o)
-    assert_close(t_g, t_o, what="tail prefill")
+    stage_close(t_g, t_o, kv_f32, "tail prefill")
     tok_o, tok_g = ot.sample_tail(t_o[-1])[0], gt.sample_tail(t_g)[0]
     assert tok_o == tok_g
     for step in range(6):  # incremental decode keeps KV on both sides
         h_o, h_g = oh.begin_token_ids("r", [tok_o]), gh.begin_token_ids("r", [tok_g])
-        assert_close(h_g, h_o, what=f"head step {step}")
+        stage_close(h_g, h_o, kv_f32, f"head step {step}")
         t_o, t_g = ot.continue_forward("r", h_o), gt.continue_forward("r", h_g)
-        assert_close(t_g, t_o, what=f"tail step {step}")
+        stage_close(t_g, t_o, kv_f32, f"tail step {step}")
         tok_o, tok_g = ot.sample_tail(t_o[-1])[0], gt.sample_tail(t_g)[0]
         assert tok_o == tok_g
     assert gh.session_len("r") == 37 + 6 and gt.session_len("r") == 37 + 6
