@@ -84,6 +84,17 @@ int sfc_logits_argmax(int ggml_type, const void *w_dev, int64_t vocab, int64_t d
                       int64_t n_tok, float cap, float *all_scores_dev, int64_t *argmax_dev, float *score_dev,
                       void *stream);
 
+/* Same computation as sfc_logits_argmax, for callers that cannot allocate device memory (code
+ * running under CUDA graph capture, processes whose device memory belongs to their own
+ * allocator).  No counterpart in the reference.  It allocates nothing: its per-CTA partials live
+ * in a fixed 64 KiB array inside the library (enough for GPUs with up to 512 SMs; larger needs
+ * return SFC_E_NOMEM).  The first call on each device looks up that array's device address, so
+ * make it before any stream capture.  All calls share the array: calls whose kernels overlap on
+ * the GPU (e.g. on two streams at once) race; nothing in it needs to start at zero. */
+int sfc_logits_argmax_noalloc(int ggml_type, const void *w_dev, int64_t vocab, int64_t dim, const float *h_dev,
+                              int64_t n_tok, float cap, float *all_scores_dev, int64_t *argmax_dev,
+                              float *score_dev, void *stream);
+
 /* Seeded synthetic tensor in GGUF layout (deterministic; same bytes on every device). */
 int sfc_synth_tensor(int ggml_type, uint64_t seed, const char *name, int64_t rows, int64_t in_dim, float sigma,
                      float mean, void *out_dev, void *stream);
