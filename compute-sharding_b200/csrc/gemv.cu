@@ -25,68 +25,85 @@
 
 namespace sfc {
 
-constexpr int GEMV_THREADS = 320;  // 40 Q4_K blocks x 8 slices; 80-slice rows -> 4 row groups
-constexpr int GEMV_MAX_T = 4;
+// Threads per CTA: 1-token launches use 512 threads (16 warps, <= 128 registers each), 2-token
+// launches 320 (up to 204 registers for the per-token activation planes).
+template <int T>
+struct GemvCfg {
+  static constexpr int THREADS = T == 1 ? 512 : 320;
+};
+constexpr int GEMV_MAX_THREADS = 512;
+constexpr int GEMV_MAX_T = 2;
+constexpr int SLICE = 64;              // activations per thread per row: one 64-group of a 256-block
+constexpr int SLICES_PER_BLOCK = 4;
 
 __device__ unsigned g_device_error = 0;
 long long g_kernel_launches = 0;
 
 // ---------------------------------------------------------------- activations
-// Per-thread view of the activation slice for one token: digit planes for the two
-// 16-element halves (A = elements j*64+16h+[0,16), B = A+32), block scale 2^e and
-// half sums of the quantized values.
+// Per-thread view of the activation slice for one token: digit planes for the two 32-element
+// halves (A = elements j*64+[0,32), B = A+32) of block `blk`, the block scale 2^e, and sums of
+// the quantized values per 32 (Q4_K mins) and per 16 elements (Q6_K offset of 32).
 struct XSlice {
-  uint32_t p[3][2][4];  // [plane a,b,c][half][word] 4 signed digits per word
+  uint32_t p[3][2][8];  // [plane a,b,c][half][word] 4 signed digits per word
   float scale;
-  float sum[2];
+  float sum32[2];
+  float sum16[4];
 };
 
-// Split this thread's 32 activations into exact digit planes (see file header); the block
-// exponent is shared by the 8 slices (8 consecutive lanes) of one 256-element block.
-__device__ __forceinline__ void quantize_slice(const float (&v)[2][16], int lane, XSlice &xs) {
+// Split this thread's 64 activations into exact digit planes (see file header); the block
+// exponent is shared by the 4 slices (4 consecutive lanes) of one 256-element block.
+__device__ __forceinline__ void quantize_slice(const float (&v)[2][32], int lane, XSlice &xs) {
   float m = 0.f;
 #pragma unroll
   for (int half = 0; half < 2; ++half)
 #pragma unroll
-    for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[half][i]));
-  const unsigned seg = 0xFFu << (lane & 24);
+    for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(v[half][i]));
+  const unsigned seg = 0xFu << (lane & 28);
   m = fmaxf(m, __shfl_xor_sync(seg, m, 1));
   m = fmaxf(m, __shfl_xor_sync(seg, m, 2));
-  m = fmaxf(m, __shfl_xor_sync(seg, m, 4));
   // m < 2^E with E = biased exponent - 126 (zero and subnormal maxima clamp to E = -100)
   int E = int((__float_as_uint(m) >> 23) & 0xFF) - 126;
   if (E < -100) E = -100;
   const int up = 22 - E;  // x * 2^up has magnitude < 2^22; up in [-106, 122]
   const float pw = __uint_as_float(uint32_t(127 + up) << 23);  // 2^up, a normal float
   xs.scale = __uint_as_float(uint32_t(127 - up) << 23);        // 2^-up
+  // X = rint(x * 2^up): x * 2^up is exact and |X| <= 2^22, so adding 1.5 * 2^23 in one fused
+  // multiply-add rounds to the nearest integer, which then sits in the low mantissa bits:
+  // bits(fma(x, 2^up, 1.5*2^23)) = 0x4B400000 + X.  Balanced base-256 digits without carries:
+  // Y = X + 0x808080 lies in [0, 2^24) and its bytes y2, y1, y0 give
+  // X = (y2-128)*65536 + (y1-128)*256 + (y0-128); the int8 digit y-128 is the byte y XOR 0x80,
+  // so each plane word is a byte gather (prmt) plus an xor.
+  constexpr float kRound = 12582912.0f;                         // 1.5 * 2^23
+  constexpr uint32_t kBias = 0x4B400000u - 0x808080u;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    int isum = 0;
+    uint32_t ysum[2] = {0u, 0u};
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      uint32_t pa = 0, pb = 0, pc = 0;
+    for (int w = 0; w < 8; ++w) {
+      uint32_t Y[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const int X = __float2int_rn(v[half][4 * w + k] * pw);  // exact power-of-two scaling
-        isum += X;
-        const int c = (X << 24) >> 24;
-        const int X1 = (X - c) >> 8;
-        const int b = (X1 << 24) >> 24;
-        const int a = (X1 - b) >> 8;
-        pa |= uint32_t(a & 0xFF) << (8 * k);
-        pb |= uint32_t(b & 0xFF) << (8 * k);
-        pc |= uint32_t(c & 0xFF) << (8 * k);
+        Y[k] = __float_as_uint(fmaf(v[half][4 * w + k], pw, kRound)) - kBias;
+        ysum[w >> 2] += Y[k];
       }
-      xs.p[0][half][w] = pa;
-      xs.p[1][half][w] = pb;
-      xs.p[2][half][w] = pc;
+      // byte i of plane word = byte (plane) of Y[i]
+      const uint32_t lo01 = __byte_perm(Y[0], Y[1], 0x5140);  // [Y0.b0, Y1.b0, Y0.b1, Y1.b1]
+      const uint32_t lo23 = __byte_perm(Y[2], Y[3], 0x5140);
+      const uint32_t hi01 = __byte_perm(Y[0], Y[1], 0x7362);  // [Y0.b2, Y1.b2, Y0.b3, Y1.b3]
+      const uint32_t hi23 = __byte_perm(Y[2], Y[3], 0x7362);
+      xs.p[2][half][w] = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;  // c: bytes 0
+      xs.p[1][half][w] = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;  // b: bytes 1
+      xs.p[0][half][w] = __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u;  // a: bytes 2
     }
-    xs.sum[half] = float(isum) * xs.scale;
+    // sum of X over 16 elements = sum of Y - 16 * 0x808080 (exact in 32-bit arithmetic)
+    const int s0 = int(ysum[0] - 16u * 0x808080u), s1 = int(ysum[1] - 16u * 0x808080u);
+    xs.sum16[2 * half] = float(s0) * xs.scale;
+    xs.sum16[2 * half + 1] = float(s1) * xs.scale;
+    xs.sum32[half] = float(s0 + s1) * xs.scale;
   }
 }
 
-// sum over the 4 words of one half: exact int32 dot of 16 unsigned weights with 16 digits
-__device__ __forceinline__ int dot16(const uint32_t (&wq)[4], const uint32_t (&xp)[4]) {
+__device__ __forceinline__ int dot16(const uint32_t *wq, const uint32_t *xp) {
   int s = 0;
 #pragma unroll
   for (int w = 0; w < 4; ++w) s = dp4a_us(wq[w], xp[w], s);
@@ -97,79 +114,101 @@ __device__ __forceinline__ float combine_planes(int ia, int ib, int ic) {
   return (float(ia) * 65536.0f + float(ib) * 256.0f) + float(ic);
 }
 
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t b) {  // (a & mask) | b
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(b));
+  return r;
+}
+
 // ---------------------------------------------------------------- per-row slice dots
-// Q4_K (GGUF layout): returns sum over this thread's 32 elements of w*x for each token.
+// Q4_K (GGUF layout): adds this thread's 64-element dot to acc[t] for every token.
 template <int T>
-__device__ __forceinline__ void q4k_slice(const uint8_t *__restrict__ row, int blk, int j, int h,
+__device__ __forceinline__ void q4k_slice(const uint8_t *__restrict__ row, int blk, int j,
                                           const XSlice (&xs)[T], float (&acc)[T]) {
   const uint8_t *bp = row + blk * BLOCK_Q4_K;
   const uint4 hd = lds128(bp);
-  const uint4 qv = lds128(bp + 16 + j * 32 + h * 16);
+  const uint4 q0 = lds128(bp + 16 + j * 32), q1 = lds128(bp + 32 + j * 32);
   const float d = h2f_bits(uint16_t(hd.x & 0xFFFF));
   const float dmin = h2f_bits(uint16_t(hd.x >> 16));
-  // get_scale_min_k4 for sub-blocks 2j (A) and 2j+1 (B), quants.rs:252-261
+  // get_scale_min_k4 for sub-blocks 2j (A) and 2j+1 (B), quants.rs:252-261; the two bytes of
+  // each of the three scale words sit side by side, so extract them as a 16-bit pair.
   int scA, mA, scB, mB;
   {
-    const uint32_t s0 = hd.y, s1 = hd.z, s2 = hd.w;
-    const int k = (2 * j) & 3;
-    const uint32_t b0a = (s0 >> (8 * k)) & 0xFF, b1a = (s1 >> (8 * k)) & 0xFF, b2a = (s2 >> (8 * k)) & 0xFF;
-    const uint32_t b0b = (s0 >> (8 * k + 8)) & 0xFF, b1b = (s1 >> (8 * k + 8)) & 0xFF,
-                   b2b = (s2 >> (8 * k + 8)) & 0xFF;
-    const bool lo = j < 2;  // selects, not branches: j differs across the lanes of a warp
-    scA = lo ? int(b0a & 63) : int((b2a & 15) | ((b0a >> 6) << 4));
-    mA = lo ? int(b1a & 63) : int((b2a >> 4) | ((b1a >> 6) << 4));
-    scB = lo ? int(b0b & 63) : int((b2b & 15) | ((b0b >> 6) << 4));
-    mB = lo ? int(b1b & 63) : int((b2b >> 4) | ((b1b >> 6) << 4));
+    const uint32_t sel = (j & 1) ? 0x4342u : 0x4140u;  // bytes (2j&3, 2j&3+1) -> 16-bit lanes
+    const uint32_t x0 = __byte_perm(hd.y, 0u, sel), x1 = __byte_perm(hd.z, 0u, sel), x2 = __byte_perm(hd.w, 0u, sel);
+    uint32_t sc, mn;
+    if (j < 2) {
+      sc = x0 & 0x003F003Fu;
+      mn = x1 & 0x003F003Fu;
+    } else {
+      sc = (x2 & 0x000F000Fu) | ((x0 >> 2) & 0x00300030u);
+      mn = ((x2 >> 4) & 0x000F000Fu) | ((x1 >> 2) & 0x00300030u);
+    }
+    scA = int(sc & 0xFFFF);
+    scB = int(sc >> 16);
+    mA = int(mn & 0xFFFF);
+    mB = int(mn >> 16);
   }
-  uint32_t lo[4], hi[4];
-  lo[0] = qv.x & 0x0F0F0F0Fu;
-  lo[1] = qv.y & 0x0F0F0F0Fu;
-  lo[2] = qv.z & 0x0F0F0F0Fu;
-  lo[3] = qv.w & 0x0F0F0F0Fu;
-  hi[0] = (qv.x >> 4) & 0x0F0F0F0Fu;
-  hi[1] = (qv.y >> 4) & 0x0F0F0F0Fu;
-  hi[2] = (qv.z >> 4) & 0x0F0F0F0Fu;
-  hi[3] = (qv.w >> 4) & 0x0F0F0F0Fu;
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  uint32_t lo[8], hi[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    lo[k] = w[k] & 0x0F0F0F0Fu;
+    hi[k] = (w[k] >> 4) & 0x0F0F0F0Fu;
+  }
   const float fmA = float(mA), fmB = float(mB);
 #pragma unroll
   for (int t = 0; t < T; ++t) {
     int I[3];
 #pragma unroll
-    for (int p = 0; p < 3; ++p) I[p] = scA * dot16(lo, xs[t].p[p][0]) + scB * dot16(hi, xs[t].p[p][1]);
+    for (int p = 0; p < 3; ++p)
+      I[p] = scA * (dot16(lo, xs[t].p[p][0]) + dot16(lo + 4, xs[t].p[p][0] + 4)) +
+             scB * (dot16(hi, xs[t].p[p][1]) + dot16(hi + 4, xs[t].p[p][1] + 4));
     const float f = combine_planes(I[0], I[1], I[2]);
-    acc[t] += d * (xs[t].scale * f) - dmin * (fmA * xs[t].sum[0] + fmB * xs[t].sum[1]);
+    acc[t] += d * (xs[t].scale * f) - dmin * (fmA * xs[t].sum32[0] + fmB * xs[t].sum32[1]);
   }
 }
 
 // Q6_K (device SoA layout per row: ql[nb][128] | qh[nb][64] | sc[nb][16] | d[nb] f16).
+// Slice j covers elements j*64..j*64+63 = 128-half n = j/2, quarter groups g = 2(j&1), 2(j&1)+1.
 template <int T>
-__device__ __forceinline__ void q6k_slice(const uint8_t *__restrict__ row, int nb, int blk, int j, int h,
+__device__ __forceinline__ void q6k_slice(const uint8_t *__restrict__ row, int nb, int blk, int j,
                                           const XSlice (&xs)[T], float (&acc)[T]) {
   const int n = j >> 1, jj = j & 1;
-  const uint8_t *ql = row + blk * 128 + n * 64 + h * 16;
-  const uint8_t *qh = row + nb * 128 + blk * 64 + n * 32 + h * 16;
-  const int8_t *sc = reinterpret_cast<const int8_t *>(row + nb * 192 + blk * 16 + n * 8 + h + 4 * jj);
+  const uint8_t *ql = row + blk * 128 + n * 64;
+  const uint8_t *qh = row + nb * 128 + blk * 64 + n * 32;
+  const uint32_t scw = *reinterpret_cast<const uint32_t *>(row + nb * 192 + blk * 16 + n * 8 + 4 * jj);
   const uint16_t dbits = *reinterpret_cast<const uint16_t *>(row + nb * 208 + blk * 2);
-  const uint4 qa = lds128(ql), qb = lds128(ql + 32), qhv = lds128(qh);
-  const int scA = sc[0], scB = sc[2];
+  const uint4 a0 = lds128(ql), a1 = lds128(ql + 16), b0 = lds128(ql + 32), b1 = lds128(ql + 48);
+  const uint4 h0 = lds128(qh), h1 = lds128(qh + 16);
+  const int sA0 = int(int8_t(scw & 0xFF)), sA1 = int(int8_t((scw >> 8) & 0xFF));
+  const int sB0 = int(int8_t((scw >> 16) & 0xFF)), sB1 = int(int8_t(scw >> 24));
   const float d = h2f_bits(dbits);
   const int sh = 4 * jj;
-  const uint32_t qa4[4] = {qa.x, qa.y, qa.z, qa.w}, qb4[4] = {qb.x, qb.y, qb.z, qb.w};
-  const uint32_t qh4[4] = {qhv.x, qhv.y, qhv.z, qhv.w};
-  uint32_t uA[4], uB[4];
+  const uint32_t qa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  const uint32_t qb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  const uint32_t qhw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  uint32_t uA[8], uB[8];
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    uA[w] = ((qa4[w] >> sh) & 0x0F0F0F0Fu) | (((qh4[w] >> sh) & 0x03030303u) << 4);
-    uB[w] = ((qb4[w] >> sh) & 0x0F0F0F0Fu) | (((qh4[w] >> (sh + 2)) & 0x03030303u) << 4);
+  for (int k = 0; k < 8; ++k) {
+    // 2 high bits of group g sit at bits 2g..2g+1 of each qh byte; move them to bits 4..5
+    const uint32_t hA = ((qhw[k] >> sh) << 4) & 0x30303030u;
+    const uint32_t hB = ((qhw[k] >> (sh + 2)) << 4) & 0x30303030u;
+    uA[k] = lop_and_or(qa[k] >> sh, 0x0F0F0F0Fu, hA);
+    uB[k] = lop_and_or(qb[k] >> sh, 0x0F0F0F0Fu, hB);
   }
 #pragma unroll
   for (int t = 0; t < T; ++t) {
     int I[3];
 #pragma unroll
-    for (int p = 0; p < 3; ++p) I[p] = scA * dot16(uA, xs[t].p[p][0]) + scB * dot16(uB, xs[t].p[p][1]);
+    for (int p = 0; p < 3; ++p)
+      I[p] = sA0 * dot16(uA, xs[t].p[p][0]) + sA1 * dot16(uA + 4, xs[t].p[p][0] + 4) +
+             sB0 * dot16(uB, xs[t].p[p][1]) + sB1 * dot16(uB + 4, xs[t].p[p][1] + 4);
     const float f = combine_planes(I[0], I[1], I[2]);
-    // sum (u - 32) * sc * x = sc * (sum u x - 32 sum x)
-    acc[t] += d * (xs[t].scale * f - 32.0f * (float(scA) * xs[t].sum[0] + float(scB) * xs[t].sum[1]));
+    // sum (u - 32) * sc * x = sc * (sum u x - 32 sum x), per 16-element scale group
+    const float corr = float(sA0) * xs[t].sum16[0] + float(sA1) * xs[t].sum16[1] + float(sB0) * xs[t].sum16[2] +
+                       float(sB1) * xs[t].sum16[3];
+    acc[t] += d * (xs[t].scale * f - 32.0f * corr);
   }
 }
 
@@ -192,6 +231,7 @@ struct QGemvArgs {
   int nstage;
   int stage_bytes;
   int rps_max;
+  int rcap;  // rows whose block partials the CTA can hold before it must finalize
   GemvPrologue pro;
   unsigned *err;
 };
@@ -199,13 +239,13 @@ struct QGemvArgs {
 // Segments let one launch cover several matrices with the same K (q, k and v of a layer):
 // the CTAs split the concatenated row space evenly and each stage stays inside one segment.
 template <int NMAT, int T>
-__global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(const QGemvArgs a) {
+__global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float pro_red[GEMV_THREADS / 32];
+  __shared__ float pro_red[GEMV_MAX_THREADS / 32];
   const int tid = threadIdx.x;
-  const int S = a.nb * 8;
+  const int S = a.nb * SLICES_PER_BLOCK;
   const int g = tid / S, s = tid % S;
-  const int blk = s >> 3, j = (s >> 1) & 3, h = s & 1;
+  const int blk = s >> 2, j = s & 3;
   const int lane = tid & 31;
   const int K = a.nb * QK_K;
 
@@ -213,9 +253,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(c
   const int64_t r_end = a.total_rows * (blockIdx.x + 1) / gridDim.x;
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-  float *red = reinterpret_cast<float *>(smem + 128);  // [2][rps_max][NMAT][T][nb]
-  const int red_stride = a.rps_max * NMAT * T * a.nb;
-  uint8_t *stages = smem + 128 + ((2 * red_stride * 4 + 127) / 128) * 128;
+  float *red = reinterpret_cast<float *>(smem + 128);  // [rcap][NMAT][T][nb] block partials
+  uint8_t *stages = smem + 128 + ((a.rcap * NMAT * T * a.nb * 4 + 127) / 128) * 128;
 
   // stage at global row `pos`: segment, first local row, row count
   auto stage_at = [&](int64_t pos, int &sg, int64_t &local0, int &nr) {
@@ -228,31 +267,54 @@ __global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(c
     if (a.seg[sg].rows - local0 < n) n = a.seg[sg].rows - local0;
     nr = int(n);
   };
-  int64_t ppos = r_begin;  // producer cursor (thread 0 only)
+  // Producer cursor: every thread tracks it (it is deterministic) so that refills are a uniform
+  // decision; only thread 0 issues the copies.
+  int64_t ppos = r_begin;
   int pit = 0;
   auto issue_next = [&]() {
     int sg, nr;
     int64_t l0;
     stage_at(ppos, sg, l0, nr);
-    const GemvSeg &G = a.seg[sg];
-    const int slot = pit % a.nstage;
-    const uint32_t bytes = uint32_t(nr) * G.row_bytes;
-    mbar_arrive_expect_tx(&bars[slot], bytes * NMAT);
+    if (tid == 0) {
+      const GemvSeg &G = a.seg[sg];
+      const int slot = pit % a.nstage;
+      const uint32_t bytes = uint32_t(nr) * G.row_bytes;
+      mbar_arrive_expect_tx(&bars[slot], bytes * NMAT);
 #pragma unroll
-    for (int m = 0; m < NMAT; ++m)
-      bulk_g2s(stages + slot * a.stage_bytes + m * G.rps * G.row_bytes, G.w[m] + l0 * G.row_bytes, bytes,
-               &bars[slot]);
+      for (int m = 0; m < NMAT; ++m)
+        bulk_g2s(stages + slot * a.stage_bytes + m * G.rps * G.row_bytes, G.w[m] + l0 * G.row_bytes, bytes,
+                 &bars[slot]);
+    }
     ppos += nr;
     ++pit;
+  };
+  // Writes the outputs of CTA-relative rows [c0, c1) from their block partials.
+  auto finalize = [&](int c0, int c1) {
+    for (int idx = tid; idx < (c1 - c0) * T; idx += blockDim.x) {
+      const int pr = idx / T, t = idx % T;
+      int sg, nr;
+      int64_t l0;
+      stage_at(r_begin + c0 + pr, sg, l0, nr);
+      float v[NMAT];
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m) {
+        const float *p = red + ((pr * NMAT + m) * T + t) * a.nb;
+        float sum = 0.f;
+        for (int b = 0; b < a.nb; ++b) sum += p[b];
+        v[m] = sum;
+      }
+      a.seg[sg].y[int64_t(t) * a.seg[sg].ldy + l0] = NMAT == 2 ? gelu_tanh_mul(v[0], v[NMAT - 1]) : v[0];
+    }
   };
 
   if (tid == 0) {
     for (int i = 0; i < a.nstage; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
-    // Weights never depend on the previous kernel: stream them before the dependency wait so
-    // their fetch overlaps the producer's tail (programmatic dependent launch).
-    while (pit < a.nstage && ppos < r_end) issue_next();
   }
+  // Weights never depend on the previous kernel: stream them before the dependency wait so their
+  // fetch overlaps the producer's tail (programmatic dependent launch).  Every thread advances
+  // the cursor; thread 0 (which initialised the barriers just above) issues the copies.
+  while (pit < a.nstage && ppos < r_end) issue_next();
   pdl_wait();
   pdl_launch_dependents();
 
@@ -260,7 +322,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(c
   XSlice xs[T];
   {
     const GemvPrologue &P = a.pro;
-    const int base = blk * QK_K + j * 64 + h * 16;
+    const int base = blk * QK_K + j * SLICE;
     // sum over row group 0 (whose slices cover K exactly once), identical in every thread
     auto block_sum = [&](float val) {
       float x = warp_sum(g == 0 ? val : 0.f);
@@ -274,12 +336,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(c
 #pragma unroll
     for (int t = 0; t < T; ++t) {
       const float *src = (P.mode == 0 ? P.x : P.a) + int64_t(t) * K + base;
-      float v[2][16];
+      float v[2][32];
       float ssq = 0.f;
 #pragma unroll
       for (int half = 0; half < 2; ++half)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 8; ++k) {
           const float4 f = *reinterpret_cast<const float4 *>(src + half * 32 + 4 * k);
           v[half][4 * k] = f.x;
           v[half][4 * k + 1] = f.y;
@@ -294,23 +356,32 @@ __global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(c
 #pragma unroll
         for (int half = 0; half < 2; ++half)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int idx = base + half * 32 + i;
-            float r = v[half][i];
-            if (P.mode == 1) {
-              r = r * s1;  // (x * scale) * w, real_math.rs:43
-            } else {
-              r = (P.w_post ? (r * s1) * P.w_post[idx] : r) + P.resid_in[int64_t(t) * K + idx];
-              if (P.scale) r = r * P.scale[0];
+          for (int k = 0; k < 8; ++k) {
+            const int idx = base + half * 32 + 4 * k;
+            float4 wp = make_float4(1.f, 1.f, 1.f, 1.f), rs = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (P.mode == 2) {
+              if (P.w_post) wp = *reinterpret_cast<const float4 *>(P.w_post + idx);
+              rs = *reinterpret_cast<const float4 *>(P.resid_in + int64_t(t) * K + idx);
             }
-            v[half][i] = r;
-            ssr += r * r;
+            const float wv[4] = {wp.x, wp.y, wp.z, wp.w}, rv[4] = {rs.x, rs.y, rs.z, rs.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float r = v[half][4 * k + e];
+              if (P.mode == 1) {
+                r = r * s1;  // (x * scale) * w, real_math.rs:43
+              } else {
+                r = (P.w_post ? (r * s1) * wv[e] : r) + rv[e];
+                if (P.scale) r = r * P.scale[0];
+              }
+              v[half][4 * k + e] = r;
+              ssr += r * r;
+            }
           }
         if (P.mode == 2 && P.resid_out && blockIdx.x == 0 && g == 0) {
 #pragma unroll
           for (int half = 0; half < 2; ++half)
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
+            for (int k = 0; k < 8; ++k)
               *reinterpret_cast<float4 *>(P.resid_out + int64_t(t) * K + base + half * 32 + 4 * k) =
                   make_float4(v[half][4 * k], v[half][4 * k + 1], v[half][4 * k + 2], v[half][4 * k + 3]);
         }
@@ -319,7 +390,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(c
 #pragma unroll
           for (int half = 0; half < 2; ++half)
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[half][i] = (v[half][i] * s2) * P.w_next[base + half * 32 + i];
+            for (int k = 0; k < 8; ++k) {
+              const float4 wn = *reinterpret_cast<const float4 *>(P.w_next + base + half * 32 + 4 * k);
+              v[half][4 * k] = (v[half][4 * k] * s2) * wn.x;
+              v[half][4 * k + 1] = (v[half][4 * k + 1] * s2) * wn.y;
+              v[half][4 * k + 2] = (v[half][4 * k + 2] * s2) * wn.z;
+              v[half][4 * k + 3] = (v[half][4 * k + 3] * s2) * wn.w;
+            }
         }
       }
       quantize_slice(v, lane, xs[t]);
@@ -327,65 +404,56 @@ __global__ void __launch_bounds__(GEMV_THREADS, (T == 1 ? 2 : 1)) qgemv_kernel(c
   }
   __syncthreads();  // barrier inits visible to all threads
 
-  const unsigned seg = 0xFFu << (lane & 24);
+  const unsigned seg = 0xFu << (lane & 28);
   int64_t pos = r_begin;
+  int pend0 = 0;  // CTA-relative row held in red[0]
   for (int it = 0; pos < r_end; ++it) {
     int sg, nr;
     int64_t l0;
     stage_at(pos, sg, l0, nr);
+    const int crow = int(pos - r_begin);
+    if (crow + nr - pend0 > a.rcap) {  // partial buffer full: emit the pending rows first
+      __syncthreads();
+      finalize(pend0, crow);
+      __syncthreads();
+      pend0 = crow;
+    }
     const GemvSeg &G = a.seg[sg];
     const int slot = it % a.nstage;
     mbar_wait_bounded(&bars[slot], (it / a.nstage) & 1, a.err);
     const uint8_t *st = stages + slot * a.stage_bytes;
-    float *rd = red + (it & 1) * red_stride;
     const bool q4 = G.type == T_Q4_K;
-    for (int lr = g; lr < nr; lr += 2 * a.groups) {
-      const int lr2 = lr + a.groups < nr ? lr + a.groups : lr;  // second row in flight (ILP)
-      float acc[2][NMAT][T];
+    for (int lr = g; lr < nr; lr += a.groups) {
+      float acc[NMAT][T];
 #pragma unroll
       for (int m = 0; m < NMAT; ++m) {
 #pragma unroll
-        for (int t = 0; t < T; ++t) acc[0][m][t] = acc[1][m][t] = 0.f;
-        const uint8_t *row0 = st + (m * G.rps + lr) * G.row_bytes;
-        const uint8_t *row1 = st + (m * G.rps + lr2) * G.row_bytes;
-        if (q4) {
-          q4k_slice<T>(row0, blk, j, h, xs, acc[0][m]);
-          q4k_slice<T>(row1, blk, j, h, xs, acc[1][m]);
-        } else {
-          q6k_slice<T>(row0, a.nb, blk, j, h, xs, acc[0][m]);
-          q6k_slice<T>(row1, a.nb, blk, j, h, xs, acc[1][m]);
+        for (int t = 0; t < T; ++t) acc[m][t] = 0.f;
+        const uint8_t *row = st + (m * G.rps + lr) * G.row_bytes;
+        if (q4)
+          q4k_slice<T>(row, blk, j, xs, acc[m]);
+        else
+          q6k_slice<T>(row, a.nb, blk, j, xs, acc[m]);
+      }
+      float *rd = red + (crow - pend0 + lr) * NMAT * T * a.nb;
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          float v = acc[m][t];
+          v += __shfl_xor_sync(seg, v, 1);
+          v += __shfl_xor_sync(seg, v, 2);
+          if ((s & 3) == 0) rd[(m * T + t) * a.nb + blk] = v;
         }
-      }
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr)
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-          for (int t = 0; t < T; ++t) {
-            float v = acc[rr][m][t];
-            v += __shfl_xor_sync(seg, v, 1);
-            v += __shfl_xor_sync(seg, v, 2);
-            v += __shfl_xor_sync(seg, v, 4);
-            const int row = rr ? lr2 : lr;
-            if ((s & 7) == 0 && (rr == 0 || lr2 != lr)) rd[((row * NMAT + m) * T + t) * a.nb + blk] = v;
-          }
     }
-    __syncthreads();  // stage slot fully consumed; partials complete
-    if (tid == 0 && ppos < r_end) issue_next();
-    for (int idx = tid; idx < nr * T; idx += blockDim.x) {
-      const int lr = idx / T, t = idx % T;
-      float v[NMAT];
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        const float *p = rd + ((lr * NMAT + m) * T + t) * a.nb;
-        float sum = 0.f;
-        for (int b = 0; b < a.nb; ++b) sum += p[b];
-        v[m] = sum;
-      }
-      G.y[int64_t(t) * G.ldy + l0 + lr] = NMAT == 2 ? gelu_tanh_mul(v[0], v[NMAT - 1]) : v[0];
+    if (ppos < r_end) {  // this slot is needed again: wait until every thread is done with it
+      __syncthreads();
+      issue_next();
     }
     pos += nr;
   }
+  __syncthreads();
+  finalize(pend0, int(r_end - r_begin));
 }
 
 // ---------------------------------------------------------------- float-weight GEMV
@@ -526,9 +594,30 @@ constexpr int GEMV_STAGE_TARGET = 24 * 1024;
 template <int NMAT, int T>
 static cudaError_t launch_qgemv_t(QGemvArgs a, cudaStream_t st) {
   auto kern = qgemv_kernel<NMAT, T>;
-  const int ctas_per_sm = T == 1 ? 2 : 1;
-  const int budget = T == 1 ? 100 * 1024 : 200 * 1024;  // two CTAs (or two kernels) per SM when T == 1
-  const int red_bytes = ((2 * a.rps_max * NMAT * T * a.nb * 4 + 127) / 128) * 128;
+  constexpr int THREADS = GemvCfg<T>::THREADS;
+  const int S = a.nb * SLICES_PER_BLOCK;
+  a.groups = THREADS / S;
+  if (a.groups < 1) return cudaErrorInvalidValue;
+  a.stage_bytes = 0;
+  a.rps_max = 0;
+  for (int i = 0; i < a.nseg; ++i) {
+    GemvSeg &sg = a.seg[i];
+    // rows per stage: a multiple of the row-group count so every group has the same rows
+    int rps = (GEMV_STAGE_TARGET / (sg.row_bytes * NMAT) + a.groups / 2) / a.groups * a.groups;
+    if (rps < a.groups) rps = a.groups;
+    sg.rps = rps;
+    if (rps * sg.row_bytes * NMAT > a.stage_bytes) a.stage_bytes = rps * sg.row_bytes * NMAT;
+    if (rps > a.rps_max) a.rps_max = rps;
+  }
+  int64_t ctas = (a.total_rows + a.groups - 1) / a.groups;
+  if (ctas > num_sms()) ctas = num_sms();
+  // hold every row of the CTA's slab when that fits (one finalize at the end), else rps_max rows
+  const int per_row = NMAT * T * a.nb * 4;
+  const int rows_per_cta = int((a.total_rows + ctas - 1) / ctas);
+  a.rcap = rows_per_cta * per_row <= 32 * 1024 ? rows_per_cta : a.rps_max;
+  if (a.rcap < a.rps_max) a.rcap = a.rps_max;
+  const int budget = 200 * 1024;  // one CTA per SM (the register file is full)
+  const int red_bytes = ((a.rcap * per_row + 127) / 128) * 128;
   int nst = (budget - 128 - red_bytes) / a.stage_bytes;
   if (nst > 8) nst = 8;
   if (nst < 1) return cudaErrorInvalidValue;
@@ -536,18 +625,14 @@ static cudaError_t launch_qgemv_t(QGemvArgs a, cudaStream_t st) {
   const size_t smem = 128 + red_bytes + size_t(nst) * a.stage_bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  int64_t ctas = (a.total_rows + a.groups - 1) / a.groups;
-  if (ctas > int64_t(ctas_per_sm) * num_sms()) ctas = int64_t(ctas_per_sm) * num_sms();
-  return launch_pdl(kern, dim3(unsigned(ctas)), dim3(a.groups * a.nb * 8), smem, st, a);
+  return launch_pdl(kern, dim3(unsigned(ctas)), dim3(a.groups * S), smem, st, a);
 }
 
 template <int NMAT>
 static cudaError_t launch_qgemv_n(const QGemvArgs &a, int T, cudaStream_t st) {
   switch (T) {
     case 1: return launch_qgemv_t<NMAT, 1>(a, st);
-    case 2: return launch_qgemv_t<NMAT, 2>(a, st);
-    case 3: return launch_qgemv_t<NMAT, 3>(a, st);
-    default: return launch_qgemv_t<NMAT, 4>(a, st);
+    default: return launch_qgemv_t<NMAT, 2>(a, st);
   }
 }
 
@@ -555,11 +640,10 @@ cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvP
                        cudaStream_t st) {
   if (n_tok <= 0) return cudaSuccess;
   if (nseg < 1 || nseg > MAX_SEG || (nmat != 1 && nmat != 2)) return cudaErrorInvalidValue;
-  if (K % QK_K || K / QK_K * 8 > GEMV_THREADS) return cudaErrorInvalidValue;
+  if (K % QK_K || K / QK_K * SLICES_PER_BLOCK > 320) return cudaErrorInvalidValue;
   QGemvArgs a = {};
   a.nseg = nseg;
   a.nb = int(K / QK_K);
-  a.groups = GEMV_THREADS / (a.nb * 8);
   a.err = device_error_ptr();
   a.pro = pro;
   for (int i = 0; i < nseg; ++i) {
@@ -567,11 +651,6 @@ cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvP
     if (sg.type != T_Q4_K && sg.type != T_Q6_K) return cudaErrorInvalidValue;
     if (!sg.w[0] || (nmat == 2 && !sg.w[1]) || sg.rows <= 0) return cudaErrorInvalidValue;
     sg.row_bytes = device_row_bytes(sg.type, K);
-    int rps = (GEMV_STAGE_TARGET / (sg.row_bytes * nmat)) / a.groups * a.groups;
-    if (rps < a.groups) rps = a.groups;
-    sg.rps = rps;
-    if (rps * sg.row_bytes * nmat > a.stage_bytes) a.stage_bytes = rps * sg.row_bytes * nmat;
-    if (rps > a.rps_max) a.rps_max = rps;
     a.seg[i] = sg;
     a.total_rows += sg.rows;
   }
