@@ -33,6 +33,9 @@ GEMV_BYTES = 10240 * 10 * 144 + 2560 * 4 + 10240 * 4
 # algorithmic weight bytes of one decode token through all 42 layers + tied fp16 logits
 LAYER_WEIGHT_BYTES = 60_518_400
 EMBD_BYTES = VOCAB * HIDDEN * 2
+# dram__bytes_read.sum + dram__bytes_write.sum of one qgemv_kernel<1,1> launch on that shape, from
+# the ncu capture summarised in profiles/qgemv_q4k_10240x2560_1tok.md (None until captured)
+GEMV_DRAM_BYTES = None
 
 
 def env_rank():
@@ -139,35 +142,51 @@ def run_reference(args):
 
 # ---------------------------------------------------------------- our arm
 def gemv_roofline(sf, torch, hbm_peak):
-    """Config-1 GEMV: Q4_K 10240 x 2560, one token, cycling > 2 x L2 of weight copies."""
+    """Config-1 GEMV: Q4_K 10240 x 2560, one token, cycling weight copies larger than twice the L2.
+
+    The launches are captured once in a CUDA graph (one launch per weight copy, back to back with
+    programmatic dependent launch, as inside a decode step) and the graph is replayed; CUDA events
+    on the replay stream give the average device time per launch."""
     dev = torch.device("cuda")
-    l2 = torch.cuda.get_device_properties(0).L2_cache_size if hasattr(torch.cuda.get_device_properties(0), "L2_cache_size") else 126 << 20
+    props = torch.cuda.get_device_properties(0)
+    l2 = getattr(props, "L2_cache_size", 126 << 20)
     wbytes = 10240 * 10 * 144
     copies = int(np.ceil(2 * l2 / wbytes)) + 2
     ws = [sf.synth_tensor(sf.Q4_K, 1, f"gemv.{i}", 10240, 2560, 0.02) for i in range(copies)]
     x = torch.randn(1, 2560, device=dev)
     y = torch.empty(1, 10240, device=dev)
-    st = torch.cuda.current_stream().cuda_stream
     lib = sf.lib
 
-    def run(i):
-        lib.sfc_matmul(sf.Q4_K, ws[i % copies].data_ptr(), 10240, 2560, x.data_ptr(), 1, y.data_ptr(), st)
+    def launch_all():
+        st = torch.cuda.current_stream().cuda_stream
+        for i in range(copies):
+            rc = lib.sfc_matmul(sf.Q4_K, ws[i].data_ptr(), 10240, 2560, x.data_ptr(), 1, y.data_ptr(), st)
+            if rc:
+                raise RuntimeError(f"sfc_matmul failed with {rc}")
 
-    for i in range(3 * copies):
-        run(i)
+    launch_all()  # first calls outside capture (device error flag lookup, etc.)
     torch.cuda.synchronize()
-    reps = 30 * copies
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        launch_all()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = 30
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(reps):
-        run(i)
+    for _ in range(reps):
+        g.replay()
     e1.record()
     torch.cuda.synchronize()
-    dur_s = e0.elapsed_time(e1) / 1e3 / reps
+    n = reps * copies
+    dur_s = e0.elapsed_time(e1) / 1e3 / n
     achieved = GEMV_BYTES / dur_s / 1e9
-    return {"kernel": "qgemv_kernel<Q4_K,1,1> (10240x2560, 1 token, cold L2)", "bound": "hbm",
+    del g
+    return {"kernel": "qgemv_kernel<1,1> (Q4_K 10240x2560, 1 token, weights cycled over > 2x L2)", "bound": "hbm",
             "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-            "us_per_launch": dur_s * 1e6, "bytes_per_launch": GEMV_BYTES, "traffic": None}
+            "us_per_launch": dur_s * 1e6, "launches_timed": n, "bytes_per_launch": GEMV_BYTES,
+            "traffic": GEMV_DRAM_BYTES}
 
 
 def run_single(args):
@@ -238,12 +257,6 @@ def run_single(args):
 
     roof = gemv_roofline(sf, torch, hbm_peak)
     roof["peak_kind"] = peak_kind
-    prof_file = ROOT / "profiles" / "qgemv_q4k_10240x2560_traffic.json"
-    if prof_file.exists():
-        try:
-            roof["traffic"] = json.loads(prof_file.read_text()).get("dram_bytes_per_launch")
-        except Exception:
-            pass
 
     cpu_tps, cores, desc = cpu_decode_sample(3)
     token_bytes = N_LAYERS * LAYER_WEIGHT_BYTES + EMBD_BYTES
@@ -297,6 +310,7 @@ def run_pipeline(args):
     torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0 = sf.kernel_launches()
     with ClockSampler(local) as clk:
         e0.record()
         for _ in range(args.steps):
@@ -307,6 +321,27 @@ def run_pipeline(args):
     t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     bs1_s = float(t)
+    launches = sf.kernel_launches() - k0
+
+    # e2e: the same bs1 decode through the public pipeline API, each step's input token copied
+    # from pinned host memory on the head and the sampled token read back to the host
+    htok = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+    if ranks.is_head:
+        htok.copy_(tok.view(1))
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        x = htok.to(dev, non_blocking=True) if ranks.is_head else None
+        nxt = pipe.step(["bs1"], [1], x)
+        if ranks.is_head:
+            htok.copy_(nxt.view(1))
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_s = float(t)
 
     # bs64: 8 microbatches of 8 sequences
     ctx = rng.integers(512, 3585, 64)
@@ -328,6 +363,12 @@ def run_pipeline(args):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     bs64_s = float(t)
     be.close()
+    roof = None
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        roof = gemv_roofline(sf, torch, hbm_peak)
+        roof["peak_kind"] = peak_kind
+    dist.barrier()
     if rank == 0:
         line = {"metric": METRIC, "value": args.steps / bs1_s, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": bs1_s * 1e3 / args.steps,
@@ -340,7 +381,10 @@ def run_pipeline(args):
                            "l2": "inputs larger than L2"},
                 "bs64": {"value": 64 * bsteps / bs64_s, "unit": "tokens/s", "steps": bsteps,
                          "microbatches": "8 x 8 sequences"},
-                "e2e": None, "clocks": clk.summary()}
+                "e2e": {"value": args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 8,
+                        "d2h_bytes_per_step": 8,
+                        "path": "Pipeline.step per token, token from pinned host memory to the head and back"},
+                "roofline": roof, "gpu_launches": launches, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
 

@@ -68,6 +68,8 @@ int sfc_device_error(unsigned *code) {
   return SFC_OK;
 }
 
+int64_t sfc_kernel_launches(void) { return g_kernel_launches; }
+
 int64_t sfc_weight_device_bytes(int ggml_type, int64_t rows, int64_t in_dim) {
   if (!type_supported(ggml_type) || rows < 0) {
     set_error("unsupported ggml type %d", ggml_type);

@@ -33,7 +33,6 @@ struct GemvCfg {
 };
 constexpr int GEMV_MAX_THREADS = 512;
 constexpr int GEMV_MAX_T = 2;
-constexpr int SLICE = 64;              // activations per thread per row: one 64-group of a 256-block
 constexpr int SLICES_PER_BLOCK = 4;
 
 __device__ unsigned g_device_error = 0;
@@ -50,57 +49,88 @@ struct XSlice {
   float sum16[4];
 };
 
-// Split this thread's 64 activations into exact digit planes (see file header); the block
-// exponent is shared by the 4 slices (4 consecutive lanes) of one 256-element block.
-__device__ __forceinline__ void quantize_slice(const float (&v)[2][32], int lane, XSlice &xs) {
+// Shared-memory record of one 64-element slice: the XSlice fields in order, padded to 60 words
+// so that consecutive records start 28 banks apart (conflict-free 16-byte loads).
+constexpr int XREC_WORDS = 60;
+
+__device__ __forceinline__ void load8(const float *p, int64_t off, float (&v)[8]) {
+  const float4 f0 = *reinterpret_cast<const float4 *>(p + off);
+  const float4 f1 = *reinterpret_cast<const float4 *>(p + off + 4);
+  v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+  v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+}
+
+__device__ __forceinline__ void store8(float *p, const float (&v)[8]) {
+  *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4 *>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Exact digit planes of one 256-element block held by a warp (lane l: elements 8l..8l+7); the
+// lane writes its part of the record of slice l/8 (half (l/4)&1, plane words 2(l&3), +1).
+__device__ __forceinline__ void quantize8(const float (&v)[8], int lane, uint32_t *rec) {
   float m = 0.f;
 #pragma unroll
-  for (int half = 0; half < 2; ++half)
-#pragma unroll
-    for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(v[half][i]));
-  const unsigned seg = 0xFu << (lane & 28);
-  m = fmaxf(m, __shfl_xor_sync(seg, m, 1));
-  m = fmaxf(m, __shfl_xor_sync(seg, m, 2));
+  for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
+  m = warp_max(m);
   // m < 2^E with E = biased exponent - 126 (zero and subnormal maxima clamp to E = -100)
   int E = int((__float_as_uint(m) >> 23) & 0xFF) - 126;
   if (E < -100) E = -100;
   const int up = 22 - E;  // x * 2^up has magnitude < 2^22; up in [-106, 122]
-  const float pw = __uint_as_float(uint32_t(127 + up) << 23);  // 2^up, a normal float
-  xs.scale = __uint_as_float(uint32_t(127 - up) << 23);        // 2^-up
+  const float pw = __uint_as_float(uint32_t(127 + up) << 23);     // 2^up, a normal float
+  const float scale = __uint_as_float(uint32_t(127 - up) << 23);  // 2^-up
   // X = rint(x * 2^up): x * 2^up is exact and |X| <= 2^22, so adding 1.5 * 2^23 in one fused
   // multiply-add rounds to the nearest integer, which then sits in the low mantissa bits:
   // bits(fma(x, 2^up, 1.5*2^23)) = 0x4B400000 + X.  Balanced base-256 digits without carries:
   // Y = X + 0x808080 lies in [0, 2^24) and its bytes y2, y1, y0 give
   // X = (y2-128)*65536 + (y1-128)*256 + (y0-128); the int8 digit y-128 is the byte y XOR 0x80,
   // so each plane word is a byte gather (prmt) plus an xor.
-  constexpr float kRound = 12582912.0f;                         // 1.5 * 2^23
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
   constexpr uint32_t kBias = 0x4B400000u - 0x808080u;
+  uint32_t Y[8], ys = 0;
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    uint32_t ysum[2] = {0u, 0u};
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      uint32_t Y[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        Y[k] = __float_as_uint(fmaf(v[half][4 * w + k], pw, kRound)) - kBias;
-        ysum[w >> 2] += Y[k];
-      }
-      // byte i of plane word = byte (plane) of Y[i]
-      const uint32_t lo01 = __byte_perm(Y[0], Y[1], 0x5140);  // [Y0.b0, Y1.b0, Y0.b1, Y1.b1]
-      const uint32_t lo23 = __byte_perm(Y[2], Y[3], 0x5140);
-      const uint32_t hi01 = __byte_perm(Y[0], Y[1], 0x7362);  // [Y0.b2, Y1.b2, Y0.b3, Y1.b3]
-      const uint32_t hi23 = __byte_perm(Y[2], Y[3], 0x7362);
-      xs.p[2][half][w] = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;  // c: bytes 0
-      xs.p[1][half][w] = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;  // b: bytes 1
-      xs.p[0][half][w] = __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u;  // a: bytes 2
-    }
-    // sum of X over 16 elements = sum of Y - 16 * 0x808080 (exact in 32-bit arithmetic)
-    const int s0 = int(ysum[0] - 16u * 0x808080u), s1 = int(ysum[1] - 16u * 0x808080u);
-    xs.sum16[2 * half] = float(s0) * xs.scale;
-    xs.sum16[2 * half + 1] = float(s1) * xs.scale;
-    xs.sum32[half] = float(s0 + s1) * xs.scale;
+  for (int e = 0; e < 8; ++e) {
+    Y[e] = __float_as_uint(fmaf(v[e], pw, kRound)) - kBias;
+    ys += Y[e];
   }
+  uint32_t wc[2], wb[2], wa[2];
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const uint32_t lo01 = __byte_perm(Y[4 * w], Y[4 * w + 1], 0x5140);  // [Y0.b0, Y1.b0, Y0.b1, Y1.b1]
+    const uint32_t lo23 = __byte_perm(Y[4 * w + 2], Y[4 * w + 3], 0x5140);
+    const uint32_t hi01 = __byte_perm(Y[4 * w], Y[4 * w + 1], 0x7362);  // [Y0.b2, Y1.b2, Y0.b3, Y1.b3]
+    const uint32_t hi23 = __byte_perm(Y[4 * w + 2], Y[4 * w + 3], 0x7362);
+    wc[w] = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;  // c: bytes 0
+    wb[w] = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;  // b: bytes 1
+    wa[w] = __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u;  // a: bytes 2
+  }
+  const int h = (lane >> 2) & 1, q = lane & 3;
+  uint32_t *pw0 = rec + h * 8 + 2 * q;
+  *reinterpret_cast<uint2 *>(pw0) = make_uint2(wa[0], wa[1]);
+  *reinterpret_cast<uint2 *>(pw0 + 16) = make_uint2(wb[0], wb[1]);
+  *reinterpret_cast<uint2 *>(pw0 + 32) = make_uint2(wc[0], wc[1]);
+  // sum of X over 16 (32) elements = sum of Y - 16 (32) * 0x808080, exact in 32-bit arithmetic
+  const uint32_t y16 = ys + __shfl_xor_sync(0xFFFFFFFFu, ys, 1);
+  const uint32_t y32 = y16 + __shfl_xor_sync(0xFFFFFFFFu, y16, 2);
+  if ((q & 1) == 0) rec[51 + 2 * h + (q >> 1)] = __float_as_uint(float(int(y16 - 16u * 0x808080u)) * scale);
+  if (q == 0) rec[49 + h] = __float_as_uint(float(int(y32 - 32u * 0x808080u)) * scale);
+  if ((lane & 7) == 0) rec[48] = __float_as_uint(scale);
+}
+
+__device__ __forceinline__ void load_slice(const uint32_t *rec, XSlice &xs) {
+#pragma unroll
+  for (int i = 0; i < 12; ++i) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(rec + 4 * i);
+    uint32_t *dst = &xs.p[0][0][0] + 4 * i;
+    dst[0] = w.x; dst[1] = w.y; dst[2] = w.z; dst[3] = w.w;
+  }
+  const uint4 u0 = *reinterpret_cast<const uint4 *>(rec + 48), u1 = *reinterpret_cast<const uint4 *>(rec + 52);
+  xs.scale = __uint_as_float(u0.x);
+  xs.sum32[0] = __uint_as_float(u0.y);
+  xs.sum32[1] = __uint_as_float(u0.z);
+  xs.sum16[0] = __uint_as_float(u0.w);
+  xs.sum16[1] = __uint_as_float(u1.x);
+  xs.sum16[2] = __uint_as_float(u1.y);
+  xs.sum16[3] = __uint_as_float(u1.z);
 }
 
 __device__ __forceinline__ int dot16(const uint32_t *wq, const uint32_t *xp) {
@@ -231,7 +261,8 @@ struct QGemvArgs {
   int nstage;
   int stage_bytes;
   int rps_max;
-  int rcap;  // rows whose block partials the CTA can hold before it must finalize
+  int rcap;       // rows whose block partials the CTA can hold before it must finalize
+  int red_bytes;  // bytes of the partials buffer (also holds the activation slice records)
   GemvPrologue pro;
   unsigned *err;
 };
@@ -241,7 +272,7 @@ struct QGemvArgs {
 template <int NMAT, int T>
 __global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float pro_red[GEMV_MAX_THREADS / 32];
+  __shared__ float pro_red[GEMV_MAX_T][GEMV_MAX_THREADS / 32];
   const int tid = threadIdx.x;
   const int S = a.nb * SLICES_PER_BLOCK;
   const int g = tid / S, s = tid % S;
@@ -254,7 +285,7 @@ __global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGe
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
   float *red = reinterpret_cast<float *>(smem + 128);  // [rcap][NMAT][T][nb] block partials
-  uint8_t *stages = smem + 128 + ((a.rcap * NMAT * T * a.nb * 4 + 127) / 128) * 128;
+  uint8_t *stages = smem + 128 + a.red_bytes;
 
   // stage at global row `pos`: segment, first local row, row count
   auto stage_at = [&](int64_t pos, int &sg, int64_t &local0, int &nr) {
@@ -318,91 +349,103 @@ __global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGe
   pdl_wait();
   pdl_launch_dependents();
 
-  // ---- activations: optional fused residual add + RMSNorm, then exact digit planes
+  // ---- activations, computed once per CTA.  Unit u = (token t, 256-block b) belongs to warp
+  // u % nwarps and lane l holds its elements 8l..8l+7, so every global access is a coalesced
+  // 1 KB piece of a row.  The optional fused residual add + RMSNorm passes run first; the last
+  // pass writes each 64-element slice's digit planes and sums into a shared-memory record
+  // (aliasing the row-partials buffer), from which every thread loads its own slice.
   XSlice xs[T];
   {
     const GemvPrologue &P = a.pro;
-    const int base = blk * QK_K + j * SLICE;
-    // sum over row group 0 (whose slices cover K exactly once), identical in every thread
-    auto block_sum = [&](float val) {
-      float x = warp_sum(g == 0 ? val : 0.f);
-      if (lane == 0) pro_red[tid >> 5] = x;
-      __syncthreads();
-      float sum = 0.f;
-      for (int w = 0; w < int(blockDim.x + 31) / 32; ++w) sum += pro_red[w];
-      __syncthreads();
-      return sum;
-    };
+    uint32_t *xrec = reinterpret_cast<uint32_t *>(red);
+    const int nwarps = int(blockDim.x) >> 5, warp = tid >> 5;
+    const int units = T * a.nb;
+    float s1[T], s2[T];
 #pragma unroll
-    for (int t = 0; t < T; ++t) {
-      const float *src = (P.mode == 0 ? P.x : P.a) + int64_t(t) * K + base;
-      float v[2][32];
-      float ssq = 0.f;
+    for (int t = 0; t < T; ++t) s1[t] = s2[t] = 1.0f;
+    // the 8 values of unit (t, b) after `step` prologue steps: 0 = input, 1 = after the first
+    // norm (+ residual), 2 = after the norm of the next op
+    auto value8 = [&](int t, int b, int step, float (&v)[8]) {
+      const int64_t off = int64_t(t) * K + b * QK_K + lane * 8;
+      const int col = b * QK_K + lane * 8;
+      load8(P.mode == 0 ? P.x : P.a, off, v);
+      if (P.mode == 0 || step == 0) return;
+      const float s1t = (T == 1 || t == 0) ? s1[0] : s1[T - 1];
+      if (P.mode == 1) {
 #pragma unroll
-      for (int half = 0; half < 2; ++half)
+        for (int e = 0; e < 8; ++e) v[e] = v[e] * s1t;  // (x * scale) * w, real_math.rs:43
+      } else {
+        float wp[8], rs[8];
+        if (P.w_post) load8(P.w_post, col, wp);
+        load8(P.resid_in, off, rs);
+        const float sc = P.scale ? P.scale[0] : 1.0f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float4 f = *reinterpret_cast<const float4 *>(src + half * 32 + 4 * k);
-          v[half][4 * k] = f.x;
-          v[half][4 * k + 1] = f.y;
-          v[half][4 * k + 2] = f.z;
-          v[half][4 * k + 3] = f.w;
-          ssq += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
-        }
-      if (P.mode != 0) {
-        const bool norm_a = P.mode == 1 || P.w_post;
-        const float s1 = norm_a ? 1.0f / sqrtf(block_sum(ssq) / float(K) + P.eps) : 1.0f;
-        float ssr = 0.f;
-#pragma unroll
-        for (int half = 0; half < 2; ++half)
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int idx = base + half * 32 + 4 * k;
-            float4 wp = make_float4(1.f, 1.f, 1.f, 1.f), rs = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (P.mode == 2) {
-              if (P.w_post) wp = *reinterpret_cast<const float4 *>(P.w_post + idx);
-              rs = *reinterpret_cast<const float4 *>(P.resid_in + int64_t(t) * K + idx);
-            }
-            const float wv[4] = {wp.x, wp.y, wp.z, wp.w}, rv[4] = {rs.x, rs.y, rs.z, rs.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float r = v[half][4 * k + e];
-              if (P.mode == 1) {
-                r = r * s1;  // (x * scale) * w, real_math.rs:43
-              } else {
-                r = (P.w_post ? (r * s1) * wv[e] : r) + rv[e];
-                if (P.scale) r = r * P.scale[0];
-              }
-              v[half][4 * k + e] = r;
-              ssr += r * r;
-            }
-          }
-        if (P.mode == 2 && P.resid_out && blockIdx.x == 0 && g == 0) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half)
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              *reinterpret_cast<float4 *>(P.resid_out + int64_t(t) * K + base + half * 32 + 4 * k) =
-                  make_float4(v[half][4 * k], v[half][4 * k + 1], v[half][4 * k + 2], v[half][4 * k + 3]);
-        }
-        const float s2 = (P.mode == 2 && P.w_next) ? 1.0f / sqrtf(block_sum(ssr) / float(K) + P.eps) : 1.0f;
-        if (P.w_next) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half)
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const float4 wn = *reinterpret_cast<const float4 *>(P.w_next + base + half * 32 + 4 * k);
-              v[half][4 * k] = (v[half][4 * k] * s2) * wn.x;
-              v[half][4 * k + 1] = (v[half][4 * k + 1] * s2) * wn.y;
-              v[half][4 * k + 2] = (v[half][4 * k + 2] * s2) * wn.z;
-              v[half][4 * k + 3] = (v[half][4 * k + 3] * s2) * wn.w;
-            }
+        for (int e = 0; e < 8; ++e) {
+          float r = (P.w_post ? (v[e] * s1t) * wp[e] : v[e]) + rs[e];
+          if (P.scale) r = r * sc;
+          v[e] = r;
         }
       }
-      quantize_slice(v, lane, xs[t]);
+      if (step == 1 || !P.w_next) return;
+      const float s2t = (T == 1 || t == 0) ? s2[0] : s2[T - 1];
+      float wn[8];
+      load8(P.w_next, col, wn);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = (v[e] * s2t) * wn[e];
+    };
+    // per-token sums over the CTA of sum(v^2) after `step` steps, in a fixed order
+    auto cta_sumsq = [&](int step, bool store_resid, float (&out)[T]) {
+      float part[T];
+#pragma unroll
+      for (int t = 0; t < T; ++t) part[t] = 0.f;
+      for (int u = warp; u < units; u += nwarps) {
+        const int t = u / a.nb, b = u % a.nb;
+        float v[8];
+        value8(t, b, step, v);
+        float q = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q += v[e] * v[e];
+        if (T == 1 || t == 0) part[0] += q; else part[T - 1] += q;
+        if (store_resid) store8(P.resid_out + int64_t(t) * K + b * QK_K + lane * 8, v);
+      }
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        const float w = warp_sum(part[t]);
+        if (lane == 0) pro_red[t][warp] = w;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        float sum = 0.f;
+        for (int w = 0; w < nwarps; ++w) sum += pro_red[t][w];
+        out[t] = sum;
+      }
+      __syncthreads();
+    };
+    if (P.mode != 0) {
+      float tot[T];
+      if (P.mode == 1 || P.w_post) {
+        cta_sumsq(0, false, tot);
+#pragma unroll
+        for (int t = 0; t < T; ++t) s1[t] = 1.0f / sqrtf(tot[t] / float(K) + P.eps);
+      }
+      if (P.mode == 2 && (P.w_next || (P.resid_out && blockIdx.x == 0))) {
+        cta_sumsq(1, P.resid_out && blockIdx.x == 0, tot);
+#pragma unroll
+        for (int t = 0; t < T; ++t) s2[t] = 1.0f / sqrtf(tot[t] / float(K) + P.eps);
+      }
     }
+    for (int u = warp; u < units; u += nwarps) {
+      const int t = u / a.nb, b = u % a.nb;
+      float v[8];
+      value8(t, b, 2, v);
+      quantize8(v, lane, xrec + ((t * a.nb + b) * SLICES_PER_BLOCK + (lane >> 3)) * XREC_WORDS);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < T; ++t) load_slice(xrec + ((t * a.nb + blk) * SLICES_PER_BLOCK + j) * XREC_WORDS, xs[t]);
   }
-  __syncthreads();  // barrier inits visible to all threads
+  __syncthreads();  // slices loaded (the records alias the partials) and barrier inits visible
 
   const unsigned seg = 0xFu << (lane & 28);
   int64_t pos = r_begin;
@@ -617,7 +660,11 @@ static cudaError_t launch_qgemv_t(QGemvArgs a, cudaStream_t st) {
   a.rcap = rows_per_cta * per_row <= 32 * 1024 ? rows_per_cta : a.rps_max;
   if (a.rcap < a.rps_max) a.rcap = a.rps_max;
   const int budget = 200 * 1024;  // one CTA per SM (the register file is full)
-  const int red_bytes = ((a.rcap * per_row + 127) / 128) * 128;
+  int red_bytes = a.rcap * per_row;
+  const int rec_bytes = T * a.nb * SLICES_PER_BLOCK * XREC_WORDS * 4;
+  if (rec_bytes > red_bytes) red_bytes = rec_bytes;
+  red_bytes = (red_bytes + 127) / 128 * 128;
+  a.red_bytes = red_bytes;
   int nst = (budget - 128 - red_bytes) / a.stage_bytes;
   if (nst > 8) nst = 8;
   if (nst < 1) return cudaErrorInvalidValue;

@@ -72,6 +72,7 @@ def _sig(name, res, *args):
 _sig("sfc_abi_version", _I)
 _sig("sfc_last_error", ctypes.c_char_p)
 _sig("sfc_device_error", _I, ctypes.POINTER(ctypes.c_uint))
+_sig("sfc_kernel_launches", ctypes.c_int64)
 _sig("sfc_weight_device_bytes", _I64, _I, _I64, _I64)
 _sig("sfc_prepare_weights", _I, _I, _P, _I64, _I64, _P, _P)
 _sig("sfc_dequantize_rows", _I, _I, _P, _I64, _I64, _P, _P)
@@ -207,6 +208,11 @@ def synth_tensor(ggml_type: int, seed: int, name: str, rows: int, in_dim: int, s
     _check(_lib.sfc_synth_tensor(ggml_type, seed, name.encode(), rows, in_dim, sigma, mean, _ptr(out),
                                  _stream(stream)), "sfc_synth_tensor")
     return out
+
+
+def kernel_launches() -> int:
+    """Compute-kernel launches issued by the library so far (graph replays not counted)."""
+    return int(_lib.sfc_kernel_launches())
 
 
 def device_error() -> int:

@@ -43,6 +43,10 @@ int sfc_abi_version(void);
 const char *sfc_last_error(void);
 /* Read and clear the device-side error word of the current device (0 = none). */
 int sfc_device_error(unsigned *code);
+/* Number of compute-kernel launches this library has issued in this process (stream launches
+ * and launches recorded into CUDA graphs; replays of a graph are not counted).  Load-time
+ * kernels (weight repacking, synthetic weight generation) are not counted. */
+int64_t sfc_kernel_launches(void);
 
 /* ------------------------------------------------------------------ kernel-level API
  * Device pointers, caller's stream.  Weights for sfc_matmul* must be in the device layout
