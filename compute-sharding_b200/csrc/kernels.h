@@ -118,6 +118,14 @@ struct KVLayer {
 // q/k/v post-processing for a batch: per-head norms, RoPE, KV append (real_forward.rs:1583-1662).
 cudaError_t qkv_post(float *q, const float *k, const float *v, int q_ld, int kv_ld, KVLayer kv, const SeqInfo *seqs,
                      const int32_t *tok_seq, int64_t n_tok, const AttnParams &p, cudaStream_t st);
+// Decode step (one new token per sequence, row t = sequence t): q/k/v head norms + RoPE, KV
+// append and attention in one launch (decode_attn.cu).  counters: n_seq * n_kv words, zero
+// before the first launch; every launch leaves them zero.
+bool decode_attention_supported(const AttnParams &p);
+size_t decode_attention_scratch_bytes(int64_t n_seq, const AttnParams &p, int64_t max_keys);
+cudaError_t decode_attention(const float *q, const float *k, const float *v, int q_ld, int kv_ld, float *out,
+                             KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, const AttnParams &p,
+                             void *scratch, size_t scratch_bytes, unsigned *counters, cudaStream_t st);
 // causal GQA attention over the cache (real_math.rs:2697-2744); tree masks via parent links.
 size_t attention_scratch_bytes(int64_t n_tok, const AttnParams &p, int64_t max_keys);
 // tok_limit (nullable): per-token number of visible cache positions (default pos+1);

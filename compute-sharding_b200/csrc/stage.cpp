@@ -269,6 +269,7 @@ struct sfc_stage {
   int32_t *tok_seq_dev = nullptr, *step_dev = nullptr;
   SeqInfo *seq_dev = nullptr;
   void *scratch = nullptr;
+  unsigned *attn_counters = nullptr;  // decode attention split counters, [max_batch][n_kv], kept zero
   size_t attn_scratch = 0, logit_scratch = 0;
   int64_t gen_capacity = 0;
   PinnedRing ring;
@@ -611,10 +612,15 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   ap.n_kv = std::max(h->n_kv, 1);
   ap.head_dim = std::max(h->head_dim, 1);
   size_t amax = 0;
-  for (int64_t t = 1; t <= T; ++t) amax = std::max(amax, attention_scratch_bytes(t, ap, h->max_ctx));
+  for (int64_t t = 1; t <= T; ++t) {
+    amax = std::max(amax, attention_scratch_bytes(t, ap, h->max_ctx));
+    amax = std::max(amax, decode_attention_scratch_bytes(t, ap, h->max_ctx));
+  }
   h->attn_scratch = amax;
   h->logit_scratch = logits_scratch_bytes(T);
   if ((rc = alloc(&h->scratch, int64_t(std::max(h->attn_scratch, h->logit_scratch))))) return rc;
+  if ((rc = alloc((void **)&h->attn_counters, T * ap.n_kv * 4))) return rc;
+  SFC_CUDA(cudaMemset(h->attn_counters, 0, size_t(T) * ap.n_kv * 4));
   rc = h->ring.init(size_t(T) * 8 + size_t(h->max_sessions) * sizeof(SeqInfo) + 256);
   if (rc) return rc;
   return SFC_OK;
@@ -642,7 +648,7 @@ void destroy_stage(sfc_stage *h) {
   for (void *p : {(void *)h->resid, (void *)h->resid2, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
-                  (void *)h->seq_dev, h->scratch, h->kv_arena, h->weight_arena})
+                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
   h->ring.destroy();
   if (h->ev0) cudaEventDestroy(h->ev0);
@@ -713,10 +719,23 @@ GemvSeg seg_of(const DevTensor *w, const DevTensor *w2, float *y, int64_t ldy) {
   return g;
 }
 
+// q/k/v post-processing, KV append and attention of one layer.  Decode batches (one new token
+// per sequence) use the single fused decode kernel; other batches the two-kernel path.
+cudaError_t layer_attention(sfc_stage *h, const AttnParams &ap, const KVLayer &kv, int64_t T, int64_t max_keys,
+                            bool decode, cudaStream_t st) {
+  if (decode && decode_attention_supported(ap))
+    return decode_attention(h->q, h->k, h->v, h->q_dim, h->k_dim, h->att, kv, h->seq_dev, T, max_keys, ap,
+                            h->scratch, h->attn_scratch, h->attn_counters, st);
+  cudaError_t e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev, T, ap, st);
+  if (e) return e;
+  return attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, nullptr, nullptr, T, max_keys, ap, h->scratch,
+                   h->attn_scratch, st);
+}
+
 // Fused layer loop for K-quant stages: the residual add + RMSNorm that precede the q/k/v and
 // gate/up projections run in those GEMVs' prologues (real_forward.rs:1690-1696 and :1738-1749),
 // so a layer is 5-6 launches.  Residual rows ping-pong between h->resid and h->resid2.
-cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, cudaStream_t st) {
+cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool decode, cudaStream_t st) {
   cudaError_t e = cudaSuccess;
   const int H = h->hidden;
   float *cur = h->resid, *other = h->resid2;
@@ -744,10 +763,7 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, cudaStre
     if ((e = gemv_fused(qkv, 3, 1, H, pro, T, st))) return e;
     const AttnParams ap = attn_params(h, L);
     const KVLayer kv = kv_layer(h, li);
-    if ((e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev, T, ap, st))) return e;
-    if ((e = attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, nullptr, nullptr, T, max_keys, ap, h->scratch,
-                       h->attn_scratch, st)))
-      return e;
+    if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
     const GemvSeg o = seg_of(L.o, nullptr, h->proj, H);
     GemvPrologue po = {};
     po.mode = 0;
@@ -777,8 +793,8 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, cudaStre
 }
 
 // All layers over the T rows in h->resid (device tables already uploaded).
-cudaError_t run_layers(sfc_stage *h, int64_t T, int64_t max_keys, cudaStream_t st) {
-  if (h->fused) return run_layers_fused(h, T, max_keys, st);
+cudaError_t run_layers(sfc_stage *h, int64_t T, int64_t max_keys, bool decode, cudaStream_t st) {
+  if (h->fused) return run_layers_fused(h, T, max_keys, decode, st);
   cudaError_t e = cudaSuccess;
   const int H = h->hidden;
   for (size_t li = 0; li < h->layers.size(); ++li) {
@@ -795,10 +811,7 @@ cudaError_t run_layers(sfc_stage *h, int64_t T, int64_t max_keys, cudaStream_t s
     if ((e = gemv(L.v->type, L.v->dev, nullptr, h->k_dim, H, h->xn, T, h->v, h->k_dim, st))) return e;
     const AttnParams ap = attn_params(h, L);
     const KVLayer kv = kv_layer(h, li);
-    if ((e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev, T, ap, st))) return e;
-    if ((e = attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, nullptr, nullptr, T, max_keys, ap, h->scratch,
-                       h->attn_scratch, st)))
-      return e;
+    if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
     if ((e = gemv(L.o->type, L.o->dev, nullptr, H, h->q_dim, h->att, T, h->proj, H, st))) return e;
     if ((e = add_norm(h->resid, h->proj, F32P(L.post_attn), nullptr, 1, F32P(L.ffn_norm), h->xn, T, H, h->eps, st)))
       return e;
@@ -867,7 +880,7 @@ int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t 
     SFC_CUDA(cudaMemcpyAsync(h->resid, in_dev, size_t(T) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
   }
   h->ring.release(ri, st);
-  SFC_CUDA(run_layers(h, T, max_keys, st));
+  SFC_CUDA(run_layers(h, T, max_keys, T == int64_t(seqs.size()), st));
   for (auto &s : seqs) s.s->len += s.n;
   return SFC_OK;
 }
@@ -1287,7 +1300,7 @@ int sfc_generate_greedy(sfc_stage *h, const char *request_id, const uint32_t *pr
       SFC_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
       cudaError_t e = embed(h->token_embd->type, h->token_embd->dev, h->vocab, h->hidden, h->tok_dev, 1, 1, h->resid,
                             device_error_ptr(), st);
-      if (!e) e = run_layers(h, 1, h->max_ctx, st);
+      if (!e) e = run_layers(h, 1, h->max_ctx, true, st);
       if (!e) {
         if (h->output_norm)
           e = rms_norm(h->resid, F32P(h->output_norm), 1, h->hidden, h->eps, h->hn, st);
