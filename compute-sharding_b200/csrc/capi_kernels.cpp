@@ -112,7 +112,25 @@ static int matmul_common(int ggml_type, const void *w0, const void *w1, int64_t 
   SFC_REQUIRE((ggml_type != T_Q4_K && ggml_type != T_Q6_K) || in_dim <= 10240,
               "K-quant in_dim %lld exceeds the GEMV limit 10240", (long long)in_dim);
   SFC_REQUIRE(w0 && x && y, "null pointer");
-  SFC_CUDA(gemv(ggml_type, w0, w1, out_dim, in_dim, x, n_tok, y, out_dim, static_cast<cudaStream_t>(stream)));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_tok >= QGEMM_MIN_TOKENS && qgemm_supported(ggml_type, in_dim)) {
+    // tensor-core GEMM; a gate/up pair writes both products to scratch and applies GeGLU after
+    const size_t gbytes = qgemm_scratch_bytes(n_tok, in_dim);
+    const size_t pair_bytes = w1 ? size_t(2) * n_tok * out_dim * 4 : 0;
+    void *scratch = nullptr;
+    int rc = device_scratch(gbytes + pair_bytes + 256, &scratch);
+    if (rc) return rc;
+    float *tmp = reinterpret_cast<float *>(static_cast<char *>(scratch) + (gbytes + 255) / 256 * 256);
+    QGemmOut outs[2] = {{ggml_type, w0, out_dim, w1 ? tmp : y, out_dim},
+                        {ggml_type, w1, out_dim, tmp + n_tok * out_dim, out_dim}};
+    GemmPrologue pro = {};
+    pro.mode = 0;
+    pro.x = x;
+    SFC_CUDA(qgemm(outs, w1 ? 2 : 1, in_dim, pro, n_tok, scratch, gbytes, st));
+    if (w1) SFC_CUDA(geglu(tmp, tmp + n_tok * out_dim, y, n_tok * out_dim, st));
+    return SFC_OK;
+  }
+  SFC_CUDA(gemv(ggml_type, w0, w1, out_dim, in_dim, x, n_tok, y, out_dim, st));
   return SFC_OK;
 }
 

@@ -118,6 +118,32 @@ struct KVLayer {
 // q/k/v post-processing for a batch: per-head norms, RoPE, KV append (real_forward.rs:1583-1662).
 cudaError_t qkv_post(float *q, const float *k, const float *v, int q_ld, int kv_ld, KVLayer kv, const SeqInfo *seqs,
                      const int32_t *tok_seq, int64_t n_tok, const AttnParams &p, cudaStream_t st);
+// Tensor-core K-quant GEMM (qgemm.cu) for 8+ tokens.  The activation operand is prepared from
+// the prologue inputs: mode 0 x; mode 1 RMSNorm(a) * w_next; mode 2 residual add + norms as in
+// GemvPrologue; `gate`/`up` non-null: x = gelu_tanh(gate) * up.  Up to 3 output matrices with the
+// same K per launch (e.g. q, k, v).
+struct GemmPrologue {
+  int mode;
+  const float *x, *a, *gate, *up, *resid_in;
+  float *resid_out;
+  const float *w_post, *scale, *w_next;
+  float eps;
+};
+struct QGemmOut {
+  int type;
+  const void *w;  // device layout (sfc_prepare_weights), 16-byte aligned
+  int64_t rows;
+  float *y;
+  int64_t ldy;
+};
+bool qgemm_supported(int type, int64_t K);
+size_t qgemm_scratch_bytes(int64_t n_tok, int64_t K);
+cudaError_t qgemm(const QGemmOut *outs, int nseg, int64_t K, const GemmPrologue &pro, int64_t n_tok, void *scratch,
+                  size_t scratch_bytes, cudaStream_t st);
+cudaError_t geglu(const float *gate, const float *up, float *out, int64_t n, cudaStream_t st);
+// Tokens from which the stage and the kernel-level API use the tensor-core GEMM.
+constexpr int64_t QGEMM_MIN_TOKENS = 8;
+
 // Decode step (one new token per sequence, row t = sequence t): q/k/v head norms + RoPE, KV
 // append and attention in one launch (decode_attn.cu).  counters: n_seq * n_kv words, zero
 // before the first launch; every launch leaves them zero.

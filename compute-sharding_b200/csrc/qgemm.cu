@@ -1,0 +1,744 @@
+// qgemm.cu — K-quant GEMM on the 5th-generation tensor cores (tcgen05 MMA with TMEM
+// accumulators) for prefill, batched decode and speculative verify (8 or more tokens).
+//
+// Replaces the multi-token path of the reference's row dots (crates/stage-forward-lab/src/
+// quants.rs:1801-1909 for Q4_K, :2594-2688 for Q6_K) as driven by real_math.rs:398-1124
+// (matmul_quantized_many_refs_range and its token-major variant), the gate/up pair of
+// real_math.rs:1584-1800 and the RMSNorm / residual steps around them (real_forward.rs:1690-1749).
+//
+// Arithmetic.  For weight row r and one 256-element block:
+//   Q4_K: w_i = d*sc_j*q_i - dmin*m_j      (j = 32-element sub-block, q 4-bit, sc/m 6-bit)
+//   Q6_K: w_i = d*sc_j*(q_i - 32)          (j = 16-element sub-block, q 6-bit, sc int8)
+// Operand A (weights) holds the integers a_i = sc_j*q_i (Q4_K: <= 945, exact in fp16) or
+// sc_j*(q_i-32) (Q6_K: |a| <= 4096; exact in fp16 up to 2048, within 1 above).  Activations of
+// each (token, block) are scaled by a power of two s and split x/s = hi + lo into two fp16 values
+// (~22 significant bits together); hi and lo rows of every token are the 2*TN columns of
+// operand B.  Per block the MMA chain accumulates sum_i a_i*hi_i and sum_i a_i*lo_i in fp32 TMEM
+// columns and the epilogue adds
+//   y += (d*s) * (D_hi + D_lo) - dmin * sum_j m_j * S_j       (S_j = fp32 sum of x over sub-block j)
+// so products are exact and rounding happens in fp32 sums, as in the reference.
+//
+// CTA = 128 weight rows x TN tokens, 320 threads, warp-specialised around mbarrier rings:
+//   warp 8   : producer — raw weight blocks of 128 strided rows through 2D TMA tensor maps,
+//              activation chunks (operand B, pre-swizzled by gemm_bprep_kernel) and per-block
+//              activation metadata with bulk copies
+//   warps 4-7: dequantise the raw blocks into 128-byte-swizzled fp16 A chunks (thread = row)
+//   warp 9   : one thread issues tcgen05.mma (M=128, N=2*TN, K=16) into one of two TMEM
+//              accumulators (double-buffered across 256-element blocks)
+//   warps 0-3: epilogue — tcgen05.ld a finished block's accumulator (TMEM lane = row), apply the
+//              block scales into per-thread fp32 sums, store y once at the end
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sfc {
+
+constexpr int QG_M = 128;        // weight rows per tile (UMMA M)
+constexpr int QG_KC = 64;        // K elements per chunk: one 128-byte swizzle row of fp16
+constexpr int QG_CPB = QK_K / QG_KC;  // chunks per 256-element block
+constexpr int QG_AST = 4;        // A/B ring slots (chunks)
+constexpr int QG_RST = 2;        // raw-block ring slots
+constexpr int QG_THREADS = 320;
+constexpr int QG_A_BYTES = QG_M * 128;  // one A chunk: 128 rows x 64 fp16
+constexpr int QG_RAW_BYTES = QG_M * 208;  // largest raw block of 128 rows (Q6_K ql+qh+sc)
+constexpr int QG_MAX_NB = 64;    // K <= 16384
+constexpr int QG_META = 9;       // per (token, block): s and 8 sub-block sums
+constexpr int QG_MAX_SEG = 3;
+
+struct QGemmSeg {
+  CUtensorMap map[4];  // Q4_K: [0] blocks; Q6_K: [0] ql, [1] qh, [2] scales, [3] d of all blocks
+  float *y;
+  int64_t ldy;
+  int rows;
+  int type;
+  int tile0;  // first global row tile of this segment
+};
+
+struct QGemmArgs {
+  QGemmSeg seg[QG_MAX_SEG];
+  int nseg;
+  int nb;        // 256-element blocks along K
+  int n_tok;     // valid tokens
+  int n_ttiles;  // token tiles
+  const uint8_t *bimg;   // [ttile][K/64 chunks][N rows x 128 B] swizzled fp16 (hi rows, then lo rows)
+  const float *bmeta;    // [ttile][nb][9][TN]
+  unsigned *err;
+};
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (A and B both fp16), fp32 accumulate
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+
+template <int NREG>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[NREG]);
+
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 16-byte piece j (8 fp16 along K) of row n in a 128-byte-swizzled K-major tile
+__device__ __forceinline__ uint32_t sw128_off(int n, int j) {
+  return uint32_t((n >> 3) * 1024 + (n & 7) * 128 + ((j ^ (n & 7)) << 4));
+}
+
+// fp16x2 of (lo16(a) * s, hi16(a) * s) for two small integers packed as bytes 0 and 2 of `nib2`
+// (<= 15): (1024 + q) * s - 1024 * s = q * s exactly (single rounding of an exact result).
+__device__ __forceinline__ uint32_t nib_times(uint32_t nib2, __half2 s2, __half2 negbias2) {
+  const uint32_t v = nib2 | 0x64006400u;  // fp16 1024 + q in each half
+  __half2 h = *reinterpret_cast<const __half2 *>(&v);
+  h = __hfma2(h, s2, negbias2);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// ---------------------------------------------------------------- GEMM kernel
+template <int TN>
+__global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_constant__ QGemmArgs a) {
+  constexpr int N = 2 * TN;             // B rows: hi then lo per token
+  constexpr int B_BYTES = N * 128;      // one B chunk
+  constexpr int TMEM_COLS = 2 * N < 32 ? 32 : 2 * N;
+  constexpr int BM_BYTES = QG_META * TN * 4;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned carve-up (swizzled operand tiles need it)
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t *sA = smem;                                  // [QG_AST][QG_A_BYTES]
+  uint8_t *sB = sA + QG_AST * QG_A_BYTES;              // [QG_AST][B_BYTES]
+  uint8_t *sRaw = sB + QG_AST * B_BYTES;               // [QG_RST][QG_RAW_BYTES]
+  uint8_t *sD = sRaw + QG_RST * QG_RAW_BYTES;          // Q6_K d of all blocks: [128][<= 128 B]
+  float *sBm = reinterpret_cast<float *>(sD + QG_M * 128);  // [2][9][TN]
+  float *sRm = sBm + 2 * QG_META * TN;                 // [2][128][10]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sRm + 2 * QG_M * 10);
+  uint64_t *a_full = bars, *a_empty = bars + 4, *b_full = bars + 8, *b_empty = bars + 12;
+  uint64_t *raw_full = bars + 16, *raw_empty = bars + 18, *acc_full = bars + 20, *acc_empty = bars + 22;
+  uint64_t *bm_full = bars + 24, *rm_full = bars + 26, *d_full = bars + 28;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 29);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // global row tile -> segment
+  int sg = 0;
+  while (sg + 1 < a.nseg && int(blockIdx.x) >= a.seg[sg + 1].tile0) ++sg;
+  const QGemmSeg &S = a.seg[sg];
+  const int row0 = (int(blockIdx.x) - S.tile0) * QG_M;
+  const int tt = blockIdx.y;
+  const int nb = a.nb, nchunk = nb * QG_CPB;
+  const bool q6 = S.type == T_Q6_K;
+  const int raw_bytes = q6 ? QG_M * 208 : QG_M * BLOCK_Q4_K;
+  const int dbox = (2 * nb + 15) / 16 * 16;
+
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&a_full[i], 128);
+      mbar_init(&a_empty[i], 1);
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 128);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+      mbar_init(&bm_full[i], 1);
+      mbar_init(&rm_full[i], 128);
+    }
+    mbar_init(d_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {  // TMEM for two accumulators of N fp32 columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto issue_raw = [&](int kb) {
+    const int rs = kb & 1;
+    uint8_t *dst = sRaw + rs * QG_RAW_BYTES;
+    mbar_arrive_expect_tx(&raw_full[rs], uint32_t(raw_bytes));
+    if (!q6) {
+      tma_load_2d(dst, &S.map[0], kb * BLOCK_Q4_K, row0, &raw_full[rs]);
+    } else {
+      tma_load_2d(dst, &S.map[0], kb * 128, row0, &raw_full[rs]);                       // ql [128][128]
+      tma_load_2d(dst + QG_M * 128, &S.map[1], nb * 128 + kb * 64, row0, &raw_full[rs]);  // qh [128][64]
+      tma_load_2d(dst + QG_M * 192, &S.map[2], nb * 192 + kb * 16, row0, &raw_full[rs]); // sc [128][16]
+    }
+  };
+  // weights never depend on the previous kernel: start them before the dependency wait
+  if (warp == 8 && lane == 0) {
+    if (q6) {
+      mbar_arrive_expect_tx(d_full, uint32_t(QG_M * dbox));
+      tma_load_2d(sD, &S.map[3], nb * 208, row0, d_full);
+    }
+    for (int kb = 0; kb < nb && kb < QG_RST; ++kb) issue_raw(kb);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+
+  if (warp == 8) {
+    // ---------------- producer
+    if (lane == 0) {
+      for (int kb = 0; kb < nb; ++kb) {
+        const int ph = (kb >> 1) & 1;
+        if (kb >= QG_RST) {
+          mbar_wait_bounded(&raw_empty[kb & 1], ph ^ 1, a.err);
+          issue_raw(kb);
+        }
+        mbar_wait_bounded(&acc_empty[kb & 1], ph ^ 1, a.err);  // epilogue done with block kb-2's metadata
+        mbar_arrive_expect_tx(&bm_full[kb & 1], BM_BYTES);
+        bulk_g2s(sBm + (kb & 1) * QG_META * TN, a.bmeta + (int64_t(tt) * nb + kb) * QG_META * TN, BM_BYTES,
+                 &bm_full[kb & 1]);
+        for (int c = 0; c < QG_CPB; ++c) {
+          const int cc = kb * QG_CPB + c, s = cc & 3;
+          mbar_wait_bounded(&b_empty[s], ((cc >> 2) & 1) ^ 1, a.err);
+          mbar_arrive_expect_tx(&b_full[s], B_BYTES);
+          bulk_g2s(sB + s * B_BYTES, a.bimg + (int64_t(tt) * nchunk + cc) * B_BYTES, B_BYTES, &b_full[s]);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(QG_M >> 4) << 24);
+      for (int kb = 0; kb < nb; ++kb) {
+        const int b = kb & 1;
+        mbar_wait_bounded(&acc_empty[b], ((kb >> 1) & 1) ^ 1, a.err);
+        tc_fence_after();
+        for (int c = 0; c < QG_CPB; ++c) {
+          const int cc = kb * QG_CPB + c, s = cc & 3, ph = (cc >> 2) & 1;
+          mbar_wait_bounded(&a_full[s], ph, a.err);
+          mbar_wait_bounded(&b_full[s], ph, a.err);
+          tc_fence_after();
+          const uint32_t abase = smem_u32(sA + s * QG_A_BYTES), bbase = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < QG_KC / 16; ++k)
+            tc_mma_f16(tmem + uint32_t(b * N), sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc,
+                       (c | k) != 0);
+          tc_commit(&a_empty[s]);
+          tc_commit(&b_empty[s]);
+        }
+        tc_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- dequantisers: thread r = row r of the tile
+    const int r = tid - 128;
+    if (q6) mbar_wait_bounded(d_full, 0, a.err);
+    for (int kb = 0; kb < nb; ++kb) {
+      const int rs = kb & 1, ph = (kb >> 1) & 1;
+      mbar_wait_bounded(&raw_full[rs], ph, a.err);
+      const uint8_t *raw = sRaw + rs * QG_RAW_BYTES;
+      // per-row block metadata for the epilogue (its buffer is free once block kb-2 is done)
+      mbar_wait_bounded(&acc_empty[kb & 1], ph ^ 1, a.err);
+      float *rm = sRm + ((kb & 1) * QG_M + r) * 10;
+      uint32_t scw[4];  // Q4_K: 6-bit scales of the 8 sub-blocks as bytes; Q6_K: 16 int8 scales
+      if (!q6) {
+        const uint4 hd = *reinterpret_cast<const uint4 *>(raw + r * BLOCK_Q4_K);
+        rm[0] = h2f_bits(uint16_t(hd.x & 0xFFFF));
+        rm[1] = h2f_bits(uint16_t(hd.x >> 16));
+        // get_scale_min_k4 (quants.rs:252-261) for sub-blocks 0..7
+        const uint32_t s0 = hd.y, s1 = hd.z, s2 = hd.w;  // bytes 0-3, 4-7, 8-11 of the scale array
+        const uint32_t sc_lo = s0 & 0x3F3F3F3Fu;                                        // sub 0..3
+        const uint32_t mn_lo = s1 & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);          // sub 4..7
+        const uint32_t mn_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+        scw[0] = sc_lo;
+        scw[1] = sc_hi;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          rm[2 + j] = float((mn_lo >> (8 * j)) & 0xFF);
+          rm[6 + j] = float((mn_hi >> (8 * j)) & 0xFF);
+        }
+      } else {
+        rm[0] = h2f_bits(*reinterpret_cast<const uint16_t *>(sD + r * dbox + kb * 2));
+        const uint4 sv = *reinterpret_cast<const uint4 *>(raw + QG_M * 192 + r * 16);
+        scw[0] = sv.x;
+        scw[1] = sv.y;
+        scw[2] = sv.z;
+        scw[3] = sv.w;
+      }
+      mbar_arrive(&rm_full[kb & 1]);
+      for (int c = 0; c < QG_CPB; ++c) {
+        const int cc = kb * QG_CPB + c, s = cc & 3;
+        mbar_wait_bounded(&a_empty[s], ((cc >> 2) & 1) ^ 1, a.err);
+        uint8_t *arow = sA + s * QG_A_BYTES;
+        if (!q6) {
+          // chunk c = elements 64c..64c+63: low nibbles of qs[32c..32c+31] (sub-block 2c), then high
+          // nibbles (sub-block 2c+1)
+          const uint8_t *qs = raw + r * BLOCK_Q4_K + 16 + 32 * c;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int sub = 2 * c + h;
+            const uint32_t scv = ((sub < 4 ? scw[0] : scw[1]) >> (8 * (sub & 3))) & 0xFF;
+            const __half2 s2 = __half2half2(__uint2half_rn(scv));
+            const __half2 nb2 = __half2half2(__uint2half_rn(1024u * scv));
+            const __half2 neg = __hneg2(nb2);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {  // 16-byte piece = 8 elements
+              const uint2 w = *reinterpret_cast<const uint2 *>(qs + 8 * p);
+              const uint32_t n0 = h ? (w.x >> 4) & 0x0F0F0F0Fu : w.x & 0x0F0F0F0Fu;
+              const uint32_t n1 = h ? (w.y >> 4) & 0x0F0F0F0Fu : w.y & 0x0F0F0F0Fu;
+              uint4 o;
+              o.x = nib_times(__byte_perm(n0, 0u, 0x4140), s2, neg);
+              o.y = nib_times(__byte_perm(n0, 0u, 0x4342), s2, neg);
+              o.z = nib_times(__byte_perm(n1, 0u, 0x4140), s2, neg);
+              o.w = nib_times(__byte_perm(n1, 0u, 0x4342), s2, neg);
+              *reinterpret_cast<uint4 *>(arow + sw128_off(r, 4 * h + p)) = o;
+            }
+          }
+        } else {
+          // chunk c: half n = c/2 of the block; c even: q1 (ql low, qh bits 0-1) then q2 (ql+32 low,
+          // qh bits 2-3); c odd: q3 (ql high, qh bits 4-5) then q4 (ql+32 high, qh bits 6-7)
+          const int n = c >> 1, odd = c & 1;
+          const uint8_t *ql = raw + r * 128 + 64 * n;
+          const uint8_t *qh = raw + QG_M * 128 + r * 64 + 32 * n;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // q1/q3 (h = 0) and q2/q4 (h = 1): 32 elements each
+            const int shift_l = odd ? 4 : 0;
+            const int shift_h = 2 * (2 * odd + h);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {  // 8 elements l = 8p..8p+7
+              const uint2 lw = *reinterpret_cast<const uint2 *>(ql + 32 * h + 8 * p);
+              const uint2 hw = *reinterpret_cast<const uint2 *>(qh + 8 * p);
+              // scale index: 8n + 2*(2*odd + h) + (l >= 16)
+              const int si = 8 * n + 2 * (2 * odd + h) + (p >= 2 ? 1 : 0);
+              const int wsel = si >> 2;
+              const uint32_t sword = wsel == 0 ? scw[0] : wsel == 1 ? scw[1] : wsel == 2 ? scw[2] : scw[3];
+              const int sc = int(int8_t((sword >> (8 * (si & 3))) & 0xFF));
+              uint32_t o[4];
+#pragma unroll
+              for (int e2 = 0; e2 < 4; ++e2) {
+                int v2[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const int e = 2 * e2 + u;
+                  const uint32_t lb = ((e < 4 ? lw.x : lw.y) >> (8 * (e & 3))) & 0xFF;
+                  const uint32_t hb = ((e < 4 ? hw.x : hw.y) >> (8 * (e & 3))) & 0xFF;
+                  const int q = int(((lb >> shift_l) & 0xF) | (((hb >> shift_h) & 3) << 4));
+                  v2[u] = sc * (q - 32);
+                }
+                const __half2 hv = __halves2half2(__int2half_rn(v2[0]), __int2half_rn(v2[1]));
+                o[e2] = *reinterpret_cast<const uint32_t *>(&hv);
+              }
+              *reinterpret_cast<uint4 *>(arow + sw128_off(r, 4 * h + p)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+        mbar_arrive(&a_full[s]);
+      }
+      mbar_arrive(&raw_empty[rs]);
+    }
+  } else {
+    // ---------------- epilogue: thread r = row r = TMEM lane r
+    const int r = tid;
+    float yacc[TN];
+#pragma unroll
+    for (int t = 0; t < TN; ++t) yacc[t] = 0.f;
+    const uint32_t lane_base = tmem + (uint32_t(32 * warp) << 16);
+    for (int kb = 0; kb < nb; ++kb) {
+      const int b = kb & 1, ph = (kb >> 1) & 1;
+      mbar_wait_bounded(&bm_full[b], ph, a.err);
+      mbar_wait_bounded(&rm_full[b], ph, a.err);
+      mbar_wait_bounded(&acc_full[b], ph, a.err);
+      tc_fence_after();
+      const float *rm = sRm + (b * QG_M + r) * 10;
+      const float *bm = sBm + b * QG_META * TN;
+      const float d = rm[0];
+      const float dmin = q6 ? 0.f : rm[1];
+      float mj[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mj[j] = q6 ? 0.f : rm[2 + j];
+      constexpr int G = TN < 16 ? TN : 16;
+#pragma unroll
+      for (int t0 = 0; t0 < TN; t0 += G) {
+        uint32_t hi[G], lo[G];
+        tmem_ld<G>(lane_base + uint32_t(b * N + t0), hi);
+        tmem_ld<G>(lane_base + uint32_t(b * N + TN + t0), lo);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < G; ++i) {
+          const int t = t0 + i;
+          const float v = __uint_as_float(hi[i]) + __uint_as_float(lo[i]);
+          float mn = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) mn += mj[j] * bm[(1 + j) * TN + t];
+          yacc[t] += (d * bm[t]) * v - dmin * mn;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[b]);
+    }
+    const int row = row0 + r;
+    if (row < S.rows) {
+      const int tok0 = tt * TN;
+#pragma unroll
+      for (int t = 0; t < TN; ++t)
+        if (tok0 + t < a.n_tok) S.y[int64_t(tok0 + t) * S.ldy + row] = yacc[t];
+    }
+  }
+  __syncwarp();  // producer / MMA warps: lanes 1-31 wait for lane 0 before the block barrier
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- operand B preparation
+// One CTA per token (rows of the padded token range; padding tokens write zeros).  Warp w takes
+// 256-element blocks w, w+8, ...; lane l holds elements 8l..8l+7 of the block.  The optional
+// prologue steps mirror the GEMV prologue (residual add + RMSNorm of the next op) and the GeGLU
+// of the gate/up pair (real_math.rs:79-85).
+constexpr int BP_WARPS = 8;
+
+__device__ __forceinline__ void ld8(const float *p, float (&v)[8]) {
+  const float4 f0 = *reinterpret_cast<const float4 *>(p), f1 = *reinterpret_cast<const float4 *>(p + 4);
+  v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+  v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+}
+
+__device__ __forceinline__ float gelu_tanh_mul_b(float v, float u) {
+  const float k = 0.7978845608028654f;
+  const float inner = k * (v + 0.044715f * v * v * v);
+  return 0.5f * v * (1.0f + tanhf(inner)) * u;
+}
+
+__global__ void __launch_bounds__(BP_WARPS * 32) gemm_bprep_kernel(GemmPrologue P, int64_t K, int n_tok, int TN,
+                                                                  uint8_t *__restrict__ img,
+                                                                  float *__restrict__ meta) {
+  __shared__ float red[BP_WARPS];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = int(K / QK_K), nchunk = nb * QG_CPB, N = 2 * TN;
+  const int tt = t / TN, tl = t % TN;
+  const bool valid = t < n_tok;
+  const int64_t roff = int64_t(t) * K;
+  float s1 = 1.f, s2 = 1.f;
+  auto value8 = [&](int b, int step, float (&v)[8]) {
+    const int col = b * QK_K + lane * 8;
+    if (P.gate) {  // GeGLU of the gate/up outputs
+      float g[8], u[8];
+      ld8(P.gate + roff + col, g);
+      ld8(P.up + roff + col, u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = gelu_tanh_mul_b(g[e], u[e]);
+      return;
+    }
+    ld8((P.mode == 0 ? P.x : P.a) + roff + col, v);
+    if (P.mode == 0 || step == 0) return;
+    if (P.mode == 1) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = v[e] * s1;
+    } else {
+      float wp[8], rs[8];
+      if (P.w_post) ld8(P.w_post + col, wp);
+      ld8(P.resid_in + roff + col, rs);
+      const float sc = P.scale ? P.scale[0] : 1.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float r = (P.w_post ? (v[e] * s1) * wp[e] : v[e]) + rs[e];
+        if (P.scale) r = r * sc;
+        v[e] = r;
+      }
+    }
+    if (step == 1 || !P.w_next) return;
+    float wn[8];
+    ld8(P.w_next + col, wn);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = (v[e] * s2) * wn[e];
+  };
+  auto cta_sumsq = [&](int step, bool store_resid) {
+    float part = 0.f;
+    for (int b = warp; b < nb; b += BP_WARPS) {
+      float v[8];
+      value8(b, step, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part += v[e] * v[e];
+      if (store_resid) {
+        float *o = P.resid_out + roff + b * QK_K + lane * 8;
+        *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+      }
+    }
+    part = warp_sum(part);
+    if (lane == 0) red[warp] = part;
+    __syncthreads();
+    float sum = 0.f;
+    for (int w = 0; w < BP_WARPS; ++w) sum += red[w];
+    __syncthreads();
+    return sum;
+  };
+  if (valid && !P.gate && P.mode != 0) {
+    if (P.mode == 1 || P.w_post) s1 = 1.0f / sqrtf(cta_sumsq(0, false) / float(K) + P.eps);
+    if (P.mode == 2 && (P.w_next || P.resid_out)) {
+      const float ss = cta_sumsq(1, P.resid_out != nullptr);
+      s2 = 1.0f / sqrtf(ss / float(K) + P.eps);
+    }
+  }
+  for (int b = warp; b < nb; b += BP_WARPS) {
+    float v[8];
+    if (valid) {
+      value8(b, 2, v);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    }
+    float m = 0.f, ssum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      m = fmaxf(m, fabsf(v[e]));
+      ssum += v[e];
+    }
+    m = warp_max(m);
+    int E = int((__float_as_uint(m) >> 23) & 0xFF) - 126;  // m < 2^E
+    if (E < -100) E = -100;
+    const float up = __uint_as_float(uint32_t(127 + 15 - E) << 23);  // 2^(15-E): |x * up| < 2^15
+    const float s = __uint_as_float(uint32_t(127 - 15 + E) << 23);   // 2^(E-15)
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e2 = 0; e2 < 4; ++e2) {
+      __half h[2], l[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float xs = v[2 * e2 + u] * up;
+        h[u] = __float2half_rn(xs);
+        l[u] = __float2half_rn(xs - __half2float(h[u]));
+      }
+      const __half2 h2 = __halves2half2(h[0], h[1]), l2 = __halves2half2(l[0], l[1]);
+      hw[e2] = *reinterpret_cast<const uint32_t *>(&h2);
+      lw[e2] = *reinterpret_cast<const uint32_t *>(&l2);
+    }
+    const int cc = b * QG_CPB + (lane >> 3), j = lane & 7;
+    uint8_t *chunk = img + (int64_t(tt) * nchunk + cc) * (N * 128);
+    *reinterpret_cast<uint4 *>(chunk + sw128_off(tl, j)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(chunk + sw128_off(TN + tl, j)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    // fp32 sums over the 32-element sub-blocks (4 lanes each), fixed order
+    ssum += __shfl_xor_sync(0xFFFFFFFFu, ssum, 1);
+    ssum += __shfl_xor_sync(0xFFFFFFFFu, ssum, 2);
+    float *mt = meta + (int64_t(tt) * nb + b) * QG_META * TN;
+    if (lane == 0) mt[tl] = valid ? s : 0.f;
+    if ((lane & 3) == 0) mt[(1 + (lane >> 2)) * TN + tl] = ssum;
+  }
+}
+
+// act = gelu_tanh(gate) * up, elementwise (real_math.rs:79-85)
+__global__ void geglu_kernel(const float *__restrict__ g, const float *__restrict__ u, float *__restrict__ out,
+                             int64_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    out[i] = gelu_tanh_mul_b(g[i], u[i]);
+}
+
+cudaError_t geglu(const float *gate, const float *up, float *out, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 8 * num_sms()) blocks = 8 * num_sms();
+  return launch_pdl(geglu_kernel, dim3(unsigned(blocks)), dim3(256), 0, st, gate, up, out, n);
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2D uint8 view [rows][row_bytes] of a weight tensor, box = box_x bytes x 128 rows
+static bool make_map(CUtensorMap *m, const void *base, int64_t row_bytes, int64_t rows, int box_x) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(row_bytes), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+  const cuuint32_t box[2] = {cuuint32_t(box_x), cuuint32_t(QG_M)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct MapKey {
+  const void *p;
+  int type;
+  int64_t rows, K;
+  bool operator==(const MapKey &o) const { return p == o.p && type == o.type && rows == o.rows && K == o.K; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey &k) const {
+    return std::hash<const void *>()(k.p) ^ (size_t(k.rows) * 131 + size_t(k.K) * 7 + size_t(k.type));
+  }
+};
+struct MapSet {
+  CUtensorMap map[4];
+};
+
+static bool weight_maps(int type, const void *w, int64_t rows, int64_t K, CUtensorMap (&out)[4]) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, MapSet, MapKeyHash> cache;
+  const MapKey key{w, type, rows, K};
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    MapSet s;
+    memset(&s, 0, sizeof(s));
+    const int64_t rb = device_row_bytes(type, K);
+    const int nb = int(K / QK_K);
+    bool ok;
+    if (type == T_Q4_K) {
+      ok = make_map(&s.map[0], w, rb, rows, BLOCK_Q4_K);
+    } else {
+      ok = make_map(&s.map[0], w, rb, rows, 128) && make_map(&s.map[1], w, rb, rows, 64) &&
+           make_map(&s.map[2], w, rb, rows, 16) && make_map(&s.map[3], w, rb, rows, (2 * nb + 15) / 16 * 16);
+    }
+    if (!ok) return false;
+    it = cache.emplace(key, s).first;
+  }
+  memcpy(out, it->second.map, sizeof(out));
+  return true;
+}
+
+static size_t qgemm_smem(int TN) {
+  return 1024 + size_t(QG_AST) * QG_A_BYTES + size_t(QG_AST) * 2 * TN * 128 + size_t(QG_RST) * QG_RAW_BYTES +
+         QG_M * 128 + 2 * QG_META * TN * 4 + 2 * QG_M * 10 * 4 + 30 * 8;
+}
+
+// Token-tile width: the largest of 64/32/16/8 that still gives every SM a CTA, else 8.
+static int pick_tn(int64_t row_tiles, int64_t n_tok) {
+  int best = 8;
+  for (int tn : {64, 32, 16, 8}) {
+    if (tn > ((n_tok + 7) / 8) * 8 && tn != 8) continue;
+    if (row_tiles * ((n_tok + tn - 1) / tn) * 4 >= int64_t(num_sms()) * 3) return tn;
+  }
+  return best;
+}
+
+size_t qgemm_scratch_bytes(int64_t n_tok, int64_t K) {
+  const int64_t tpad = (n_tok + 63) / 64 * 64;  // the widest token tile pads the most
+  const int64_t nb = K / QK_K;
+  return size_t(tpad) * size_t(K) * 4 + size_t(tpad) * nb * QG_META * 4 + 1024;
+}
+
+bool qgemm_supported(int type, int64_t K) {
+  return (type == T_Q4_K || type == T_Q6_K) && K % QK_K == 0 && K / QK_K <= QG_MAX_NB && encode_fn() != nullptr;
+}
+
+template <int TN>
+static cudaError_t launch_qgemm_t(QGemmArgs &a, int row_tiles, cudaStream_t st) {
+  const size_t smem = qgemm_smem(TN);
+  cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  return launch_pdl(qgemm_kernel<TN>, dim3(unsigned(row_tiles), unsigned(a.n_ttiles)), dim3(QG_THREADS), smem, st, a);
+}
+
+cudaError_t qgemm(const QGemmOut *outs, int nseg, int64_t K, const GemmPrologue &pro, int64_t n_tok, void *scratch,
+                  size_t scratch_bytes, cudaStream_t st) {
+  if (n_tok <= 0) return cudaSuccess;
+  if (nseg < 1 || nseg > QG_MAX_SEG || K % QK_K || K / QK_K > QG_MAX_NB) return cudaErrorInvalidValue;
+  if (scratch_bytes < qgemm_scratch_bytes(n_tok, K)) return cudaErrorInvalidValue;
+  QGemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.nseg = nseg;
+  a.nb = int(K / QK_K);
+  a.n_tok = int(n_tok);
+  a.err = device_error_ptr();
+  int tiles = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const QGemmOut &o = outs[i];
+    if ((o.type != T_Q4_K && o.type != T_Q6_K) || !o.w || !o.y || o.rows <= 0) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(o.w) % 16) return cudaErrorInvalidValue;
+    QGemmSeg &s = a.seg[i];
+    if (!weight_maps(o.type, o.w, o.rows, K, s.map)) return cudaErrorInvalidValue;
+    s.y = o.y;
+    s.ldy = o.ldy;
+    s.rows = int(o.rows);
+    s.type = o.type;
+    s.tile0 = tiles;
+    tiles += int((o.rows + QG_M - 1) / QG_M);
+  }
+  const int TN = pick_tn(tiles, n_tok);
+  a.n_ttiles = int((n_tok + TN - 1) / TN);
+  const int64_t tpad = int64_t(a.n_ttiles) * TN;
+  uint8_t *img = static_cast<uint8_t *>(scratch);
+  const size_t img_bytes = size_t(tpad) * size_t(K) * 4;
+  float *meta = reinterpret_cast<float *>(img + (img_bytes + 255) / 256 * 256);
+  a.bimg = img;
+  a.bmeta = meta;
+  cudaError_t e = launch_pdl(gemm_bprep_kernel, dim3(unsigned(tpad)), dim3(BP_WARPS * 32), 0, st, pro, K, int(n_tok),
+                             TN, img, meta);
+  if (e != cudaSuccess) return e;
+  switch (TN) {
+    case 64: return launch_qgemm_t<64>(a, tiles, st);
+    case 32: return launch_qgemm_t<32>(a, tiles, st);
+    case 16: return launch_qgemm_t<16>(a, tiles, st);
+    default: return launch_qgemm_t<8>(a, tiles, st);
+  }
+}
+
+}  // namespace sfc
