@@ -10,7 +10,8 @@
 //   Q4_K: w_i = d*sc_j*q_i - dmin*m_j      (j = 32-element sub-block, q 4-bit, sc/m 6-bit)
 //   Q6_K: w_i = d*sc_j*(q_i - 32)          (j = 16-element sub-block, q 6-bit, sc int8)
 // Operand A (weights) holds the integers a_i = sc_j*q_i (Q4_K: <= 945, exact in fp16) or
-// sc_j*(q_i-32) (Q6_K: |a| <= 4096; exact in fp16 up to 2048, within 1 above).  Activations of
+// sc_j*(q_i-32) (Q6_K: |a| <= 4096, so an fp16 value plus a second A tile with the exact
+// remainder in {-1, 0, 1}, both multiplied into the same accumulator).  Activations of
 // each (token, block) are scaled by a power of two s and split x/s = hi + lo into two fp16 values
 // (~22 significant bits together); hi and lo rows of every token are the 2*TN columns of
 // operand B.  Per block the MMA chain accumulates sum_i a_i*hi_i and sum_i a_i*lo_i in fp32 TMEM
@@ -179,6 +180,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   const bool q6 = S.type == T_Q6_K;
   const int raw_bytes = q6 ? QG_M * 208 : QG_M * BLOCK_Q4_K;
   const int dbox = (2 * nb + 15) / 16 * 16;
+  // A ring: Q4_K 4 slots of one 16 KB tile; Q6_K 2 slots of two tiles (fp16 products and their
+  // rounding remainders), the same 64 KB either way
+  const int alog = q6 ? 1 : 2, amask = (1 << alog) - 1, aslot = q6 ? 2 * QG_A_BYTES : QG_A_BYTES;
 
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) {
@@ -262,17 +266,21 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
         mbar_wait_bounded(&acc_empty[b], ((kb >> 1) & 1) ^ 1, a.err);
         tc_fence_after();
         for (int c = 0; c < QG_CPB; ++c) {
-          const int cc = kb * QG_CPB + c, s = cc & 3, ph = (cc >> 2) & 1;
-          mbar_wait_bounded(&a_full[s], ph, a.err);
-          mbar_wait_bounded(&b_full[s], ph, a.err);
+          const int cc = kb * QG_CPB + c, sa = cc & amask, sb = cc & 3;
+          mbar_wait_bounded(&a_full[sa], (cc >> alog) & 1, a.err);
+          mbar_wait_bounded(&b_full[sb], (cc >> 2) & 1, a.err);
           tc_fence_after();
-          const uint32_t abase = smem_u32(sA + s * QG_A_BYTES), bbase = smem_u32(sB + s * B_BYTES);
+          const uint32_t abase = smem_u32(sA + sa * aslot), bbase = smem_u32(sB + sb * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < QG_KC / 16; ++k)
+          for (int k = 0; k < QG_KC / 16; ++k) {
             tc_mma_f16(tmem + uint32_t(b * N), sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc,
                        (c | k) != 0);
-          tc_commit(&a_empty[s]);
-          tc_commit(&b_empty[s]);
+            if (q6)  // the rounding remainders of the Q6_K products (exact small integers)
+              tc_mma_f16(tmem + uint32_t(b * N), sw128_desc(abase + QG_A_BYTES + k * 32), sw128_desc(bbase + k * 32),
+                         idesc, 1u);
+          }
+          tc_commit(&a_empty[sa]);
+          tc_commit(&b_empty[sb]);
         }
         tc_commit(&acc_full[b]);
       }
@@ -316,9 +324,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       }
       mbar_arrive(&rm_full[kb & 1]);
       for (int c = 0; c < QG_CPB; ++c) {
-        const int cc = kb * QG_CPB + c, s = cc & 3;
-        mbar_wait_bounded(&a_empty[s], ((cc >> 2) & 1) ^ 1, a.err);
-        uint8_t *arow = sA + s * QG_A_BYTES;
+        const int cc = kb * QG_CPB + c, s = cc & amask;
+        mbar_wait_bounded(&a_empty[s], ((cc >> alog) & 1) ^ 1, a.err);
+        uint8_t *arow = sA + s * aslot;
         if (!q6) {
           // chunk c = elements 64c..64c+63: low nibbles of qs[32c..32c+31] (sub-block 2c), then high
           // nibbles (sub-block 2c+1)
@@ -362,22 +370,27 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
               const int wsel = si >> 2;
               const uint32_t sword = wsel == 0 ? scw[0] : wsel == 1 ? scw[1] : wsel == 2 ? scw[2] : scw[3];
               const int sc = int(int8_t((sword >> (8 * (si & 3))) & 0xFF));
-              uint32_t o[4];
+              uint32_t o[4], ol[4];
 #pragma unroll
               for (int e2 = 0; e2 < 4; ++e2) {
-                int v2[2];
+                __half hh[2], hl[2];
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                   const int e = 2 * e2 + u;
                   const uint32_t lb = ((e < 4 ? lw.x : lw.y) >> (8 * (e & 3))) & 0xFF;
                   const uint32_t hb = ((e < 4 ? hw.x : hw.y) >> (8 * (e & 3))) & 0xFF;
                   const int q = int(((lb >> shift_l) & 0xF) | (((hb >> shift_h) & 3) << 4));
-                  v2[u] = sc * (q - 32);
+                  const int v = sc * (q - 32);  // |v| <= 4096: fp16 hi plus an exact remainder in {-1, 0, 1}
+                  hh[u] = __int2half_rn(v);
+                  hl[u] = __int2half_rn(v - __half2int_rn(hh[u]));
                 }
-                const __half2 hv = __halves2half2(__int2half_rn(v2[0]), __int2half_rn(v2[1]));
+                const __half2 hv = __halves2half2(hh[0], hh[1]), lv = __halves2half2(hl[0], hl[1]);
                 o[e2] = *reinterpret_cast<const uint32_t *>(&hv);
+                ol[e2] = *reinterpret_cast<const uint32_t *>(&lv);
               }
               *reinterpret_cast<uint4 *>(arow + sw128_off(r, 4 * h + p)) = make_uint4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<uint4 *>(arow + QG_A_BYTES + sw128_off(r, 4 * h + p)) =
+                  make_uint4(ol[0], ol[1], ol[2], ol[3]);
             }
           }
         }

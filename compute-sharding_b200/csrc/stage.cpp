@@ -270,6 +270,11 @@ struct sfc_stage {
   SeqInfo *seq_dev = nullptr;
   void *scratch = nullptr;
   unsigned *attn_counters = nullptr;  // decode attention split counters, [max_batch][n_kv], kept zero
+  // tensor-core GEMM path for 8+ rows (K-quant stages): operand-B staging and the up-projection
+  bool gemm_ok = false;
+  void *gemm_scratch = nullptr;
+  size_t gemm_scratch_bytes = 0;
+  float *act2 = nullptr;
   size_t attn_scratch = 0, logit_scratch = 0;
   int64_t gen_capacity = 0;
   PinnedRing ring;
@@ -620,6 +625,20 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   h->logit_scratch = logits_scratch_bytes(T);
   if ((rc = alloc(&h->scratch, int64_t(std::max(h->attn_scratch, h->logit_scratch))))) return rc;
   if ((rc = alloc((void **)&h->attn_counters, T * ap.n_kv * 4))) return rc;
+  if (h->fused && T >= QGEMM_MIN_TOKENS) {
+    bool ok = true;
+    for (const Layer &L : h->layers)
+      for (const DevTensor *w : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
+        ok = ok && w && qgemm_supported(w->type, w->in_dim) && reinterpret_cast<uintptr_t>(w->dev) % 16 == 0;
+    if (ok) {
+      size_t gb = 0;
+      for (int64_t K : {int64_t(H), int64_t(h->q_dim), int64_t(h->ffn)}) gb = std::max(gb, qgemm_scratch_bytes(T, K));
+      if ((rc = alloc(&h->gemm_scratch, int64_t(gb))) || (rc = alloc((void **)&h->act2, T * std::max(h->ffn, 1) * 4)))
+        return rc;
+      h->gemm_scratch_bytes = gb;
+      h->gemm_ok = true;
+    }
+  }
   SFC_CUDA(cudaMemset(h->attn_counters, 0, size_t(T) * ap.n_kv * 4));
   rc = h->ring.init(size_t(T) * 8 + size_t(h->max_sessions) * sizeof(SeqInfo) + 256);
   if (rc) return rc;
@@ -648,7 +667,7 @@ void destroy_stage(sfc_stage *h) {
   for (void *p : {(void *)h->resid, (void *)h->resid2, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
-                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->kv_arena, h->weight_arena})
+                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemm_scratch, (void *)h->act2, h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
   h->ring.destroy();
   if (h->ev0) cudaEventDestroy(h->ev0);
@@ -735,7 +754,73 @@ cudaError_t layer_attention(sfc_stage *h, const AttnParams &ap, const KVLayer &k
 // Fused layer loop for K-quant stages: the residual add + RMSNorm that precede the q/k/v and
 // gate/up projections run in those GEMVs' prologues (real_forward.rs:1690-1696 and :1738-1749),
 // so a layer is 5-6 launches.  Residual rows ping-pong between h->resid and h->resid2.
+// Layer loop on the tensor-core GEMM (8+ rows): the same fused prologues run in the operand-B
+// preparation of each GEMM; q/k/v share one launch, gate and up another, and the GeGLU of the
+// pair is applied while preparing the down projection's input.
+cudaError_t run_layers_gemm(sfc_stage *h, int64_t T, int64_t max_keys, bool decode, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  const int H = h->hidden;
+  float *cur = h->resid, *other = h->resid2;
+  void *gs = h->gemm_scratch;
+  const size_t gsb = h->gemm_scratch_bytes;
+  for (size_t li = 0; li < h->layers.size(); ++li) {
+    const Layer &L = h->layers[li];
+    GemmPrologue pro = {};
+    pro.eps = h->eps;
+    pro.w_next = F32P(L.attn_norm);
+    if (li == 0) {
+      pro.mode = L.attn_norm ? 1 : 0;
+      pro.x = cur;
+      pro.a = cur;
+    } else {
+      const Layer &P = h->layers[li - 1];
+      pro.mode = 2;
+      pro.a = h->proj;
+      pro.resid_in = cur;
+      pro.resid_out = other;
+      pro.w_post = F32P(P.post_ffw);
+      pro.scale = F32P(P.scale);
+      std::swap(cur, other);
+    }
+    const QGemmOut qkv[3] = {{L.q->type, L.q->dev, L.q->rows, h->q, h->q_dim},
+                             {L.k->type, L.k->dev, L.k->rows, h->k, h->k_dim},
+                             {L.v->type, L.v->dev, L.v->rows, h->v, h->k_dim}};
+    if ((e = qgemm(qkv, 3, H, pro, T, gs, gsb, st))) return e;
+    const AttnParams ap = attn_params(h, L);
+    const KVLayer kv = kv_layer(h, li);
+    if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
+    const QGemmOut o = {L.o->type, L.o->dev, L.o->rows, h->proj, H};
+    GemmPrologue po = {};
+    po.mode = 0;
+    po.x = h->att;
+    if ((e = qgemm(&o, 1, h->q_dim, po, T, gs, gsb, st))) return e;
+    GemmPrologue pf = {};
+    pf.mode = 2;
+    pf.eps = h->eps;
+    pf.a = h->proj;
+    pf.resid_in = cur;
+    pf.resid_out = other;
+    pf.w_post = F32P(L.post_attn);
+    pf.w_next = F32P(L.ffn_norm);
+    std::swap(cur, other);
+    const QGemmOut gu[2] = {{L.gate->type, L.gate->dev, L.gate->rows, h->act, h->ffn},
+                            {L.up->type, L.up->dev, L.up->rows, h->act2, h->ffn}};
+    if ((e = qgemm(gu, 2, H, pf, T, gs, gsb, st))) return e;
+    const QGemmOut d = {L.down->type, L.down->dev, L.down->rows, h->proj, H};
+    GemmPrologue pd = {};
+    pd.mode = 0;
+    pd.gate = h->act;
+    pd.up = h->act2;
+    if ((e = qgemm(&d, 1, h->ffn, pd, T, gs, gsb, st))) return e;
+  }
+  const Layer &Z = h->layers.back();
+  if ((e = add_norm(cur, h->proj, F32P(Z.post_ffw), F32P(Z.scale), 0, nullptr, nullptr, T, H, h->eps, st))) return e;
+  if (cur != h->resid) e = cudaMemcpyAsync(h->resid, cur, size_t(T) * H * 4, cudaMemcpyDeviceToDevice, st);
+  return e;
+}
+
 cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool decode, cudaStream_t st) {
+  if (h->gemm_ok && T >= QGEMM_MIN_TOKENS) return run_layers_gemm(h, T, max_keys, decode, st);
   cudaError_t e = cudaSuccess;
   const int H = h->hidden;
   float *cur = h->resid, *other = h->resid2;
