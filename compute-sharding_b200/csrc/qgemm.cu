@@ -19,15 +19,15 @@
 //   y += (d*s) * (D_hi + D_lo) - dmin * sum_j m_j * S_j       (S_j = fp32 sum of x over sub-block j)
 // so products are exact and rounding happens in fp32 sums, as in the reference.
 //
-// CTA = 128 weight rows x TN tokens, 320 threads, warp-specialised around mbarrier rings:
-//   warp 8   : producer — raw weight blocks of 128 strided rows through 2D TMA tensor maps,
-//              activation chunks (operand B, pre-swizzled by gemm_bprep_kernel) and per-block
-//              activation metadata with bulk copies
-//   warps 4-7: dequantise the raw blocks into 128-byte-swizzled fp16 A chunks (thread = row)
+// CTA = 128 weight rows x TN tokens, 352 threads, warp-specialised around mbarrier rings:
+//   warp 8   : producer — raw weight blocks of 128 strided rows through 2D TMA tensor maps
+//   warp 10  : producer — activation chunks (operand B, pre-swizzled by gemm_bprep_kernel) and
+//              per-block activation metadata with bulk copies
+//   warps 0-7: dequantise the raw blocks into 128-byte-swizzled fp16 A chunks (two threads per row)
 //   warp 9   : one thread issues tcgen05.mma (M=128, N=2*TN, K=16) into one of two TMEM
 //              accumulators (double-buffered across 256-element blocks)
-//   warps 0-3: epilogue — tcgen05.ld a finished block's accumulator (TMEM lane = row), apply the
-//              block scales into per-thread fp32 sums, store y once at the end
+//   warps 0-3: also the epilogue, one block behind — tcgen05.ld a finished block's accumulator
+//              (TMEM lane = row), apply the block scales into per-thread fp32 sums, store y at the end
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -46,12 +46,17 @@ constexpr int QG_KC = 64;        // K elements per chunk: one 128-byte swizzle r
 constexpr int QG_CPB = QK_K / QG_KC;  // chunks per 256-element block
 constexpr int QG_AST = 4;        // A/B ring slots (chunks)
 constexpr int QG_RST = 2;        // raw-block ring slots
-constexpr int QG_THREADS = 320;
+constexpr int QG_THREADS = 352;
 constexpr int QG_A_BYTES = QG_M * 128;  // one A chunk: 128 rows x 64 fp16
 constexpr int QG_RAW_BYTES = QG_M * 208;  // largest raw block of 128 rows (Q6_K ql+qh+sc)
 constexpr int QG_MAX_NB = 64;    // K <= 16384
 constexpr int QG_META = 9;       // per (token, block): s and 8 sub-block sums
 constexpr int QG_MAX_SEG = 3;
+
+// B ring slots for a token-tile width: chunks of 2*TN rows x 128 B, up to 64 KB and 16 chunks
+__host__ __device__ constexpr int qg_b_slots(int tn) {
+  return (65536 / (tn * 256)) > 16 ? 16 : (65536 / (tn * 256)) < 4 ? 4 : (65536 / (tn * 256));
+}
 
 struct QGemmSeg {
   CUtensorMap map[4];  // Q4_K: [0] blocks; Q6_K: [0] ql, [1] qh, [2] scales, [3] d of all blocks
@@ -80,6 +85,43 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// bring a box into L2 ahead of its load into shared memory
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+// Non-suspending poll (mbarrier.test_wait): a thread parked by try_wait can wake well after the
+// phase completes, which stalls the single-thread MMA and producer loops.  Bounded like
+// mbar_wait_bounded.
+constexpr unsigned QG_SPIN_LIMIT = 1u << 28;
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_spin(uint64_t *bar, uint32_t parity, unsigned *err) {
+  for (unsigned i = 0; i < QG_SPIN_LIMIT; ++i)
+    if (mbar_test(bar, parity)) return true;
+  if (err) atomicExch(err, DEV_WAIT_TIMEOUT);
+  return false;
+}
+
+// One lane polls the barrier and the warp proceeds together (dozens of threads spinning on one
+// mbarrier slow down the threads that complete it).  For barriers that only order work; data
+// written by the async proxy is waited for by every reading thread.
+__device__ __forceinline__ void warp_wait(uint64_t *bar, uint32_t parity, unsigned *err) {
+  if ((threadIdx.x & 31) == 0) mbar_spin(bar, parity, err);
+  __syncwarp();
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -138,10 +180,9 @@ __device__ __forceinline__ uint32_t sw128_off(int n, int j) {
   return uint32_t((n >> 3) * 1024 + (n & 7) * 128 + ((j ^ (n & 7)) << 4));
 }
 
-// fp16x2 of (lo16(a) * s, hi16(a) * s) for two small integers packed as bytes 0 and 2 of `nib2`
-// (<= 15): (1024 + q) * s - 1024 * s = q * s exactly (single rounding of an exact result).
-__device__ __forceinline__ uint32_t nib_times(uint32_t nib2, __half2 s2, __half2 negbias2) {
-  const uint32_t v = nib2 | 0x64006400u;  // fp16 1024 + q in each half
+// fp16x2 (1024 + q0, 1024 + q1) -> (q0 * s, q1 * s): (1024 + q) * s - 1024 * s is exact and
+// representable (q <= 15, s <= 63), so the single rounding of the fused multiply-add is exact.
+__device__ __forceinline__ uint32_t half2_times(uint32_t v, __half2 s2, __half2 negbias2) {
   __half2 h = *reinterpret_cast<const __half2 *>(&v);
   h = __hfma2(h, s2, negbias2);
   return *reinterpret_cast<const uint32_t *>(&h);
@@ -154,20 +195,22 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   constexpr int B_BYTES = N * 128;      // one B chunk
   constexpr int TMEM_COLS = 2 * N < 32 ? 32 : 2 * N;
   constexpr int BM_BYTES = QG_META * TN * 4;
+  constexpr int BST = qg_b_slots(TN);   // B ring slots: up to 64 KB, at most 16 chunks (4 blocks)
+  constexpr int BLOG = BST == 16 ? 4 : BST == 8 ? 3 : 2;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned carve-up (swizzled operand tiles need it)
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t *sA = smem;                                  // [QG_AST][QG_A_BYTES]
-  uint8_t *sB = sA + QG_AST * QG_A_BYTES;              // [QG_AST][B_BYTES]
-  uint8_t *sRaw = sB + QG_AST * B_BYTES;               // [QG_RST][QG_RAW_BYTES]
+  uint8_t *sB = sA + QG_AST * QG_A_BYTES;              // [BST][B_BYTES]
+  uint8_t *sRaw = sB + BST * B_BYTES;                  // [QG_RST][QG_RAW_BYTES]
   uint8_t *sD = sRaw + QG_RST * QG_RAW_BYTES;          // Q6_K d of all blocks: [128][<= 128 B]
-  float *sBm = reinterpret_cast<float *>(sD + QG_M * 128);  // [2][9][TN]
-  float *sRm = sBm + 2 * QG_META * TN;                 // [2][128][10]
+  float *sBm = reinterpret_cast<float *>(sD + QG_M * 128);  // [4][9][TN]
+  float *sRm = sBm + 4 * QG_META * TN;                 // [2][128][10]
   uint64_t *bars = reinterpret_cast<uint64_t *>(sRm + 2 * QG_M * 10);
-  uint64_t *a_full = bars, *a_empty = bars + 4, *b_full = bars + 8, *b_empty = bars + 12;
-  uint64_t *raw_full = bars + 16, *raw_empty = bars + 18, *acc_full = bars + 20, *acc_empty = bars + 22;
-  uint64_t *bm_full = bars + 24, *rm_full = bars + 26, *d_full = bars + 28;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 29);
+  uint64_t *a_full = bars, *a_empty = bars + 4, *b_full = bars + 8, *b_empty = bars + 24;
+  uint64_t *raw_full = bars + 40, *raw_empty = bars + 42, *acc_full = bars + 44, *acc_empty = bars + 46;
+  uint64_t *bm_full = bars + 48, *bm_empty = bars + 52, *rm_full = bars + 56, *d_full = bars + 58;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 59);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // global row tile -> segment
@@ -186,18 +229,21 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
 
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) {
-      mbar_init(&a_full[i], 128);
+      mbar_init(&a_full[i], 8);
       mbar_init(&a_empty[i], 1);
+      mbar_init(&bm_full[i], 1);
+      mbar_init(&bm_empty[i], 4);
+    }
+    for (int i = 0; i < BST; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 128);
+      mbar_init(&raw_empty[i], 8);
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
-      mbar_init(&bm_full[i], 1);
-      mbar_init(&rm_full[i], 128);
+      mbar_init(&acc_empty[i], 4);
+      mbar_init(&rm_full[i], 4);
     }
     mbar_init(d_full, 1);
     fence_mbar_init();
@@ -213,8 +259,19 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  auto prefetch_raw_l2 = [&](int kb) {
+    if (kb >= nb) return;
+    if (!q6) {
+      tma_prefetch_2d(&S.map[0], kb * BLOCK_Q4_K, row0);
+    } else {
+      tma_prefetch_2d(&S.map[0], kb * 128, row0);
+      tma_prefetch_2d(&S.map[1], nb * 128 + kb * 64, row0);
+      tma_prefetch_2d(&S.map[2], nb * 192 + kb * 16, row0);
+    }
+  };
   auto issue_raw = [&](int kb) {
     const int rs = kb & 1;
+    prefetch_raw_l2(kb + QG_RST);
     uint8_t *dst = sRaw + rs * QG_RAW_BYTES;
     mbar_arrive_expect_tx(&raw_full[rs], uint32_t(raw_bytes));
     if (!q6) {
@@ -237,24 +294,28 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   pdl_launch_dependents();
 
   if (warp == 8) {
-    // ---------------- producer
+    // ---------------- producer of the raw weight blocks
+    if (lane == 0) {
+      for (int kb = QG_RST; kb < nb; ++kb) {
+        mbar_spin(&raw_empty[kb & 1], ((kb >> 1) & 1) ^ 1, a.err);
+        issue_raw(kb);
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------- producer of the activation chunks and per-block activation metadata (its own
+    // warp: spinning lanes of one warp would take turns)
     if (lane == 0) {
       for (int kb = 0; kb < nb; ++kb) {
-        const int ph = (kb >> 1) & 1;
-        if (kb >= QG_RST) {
-          mbar_wait_bounded(&raw_empty[kb & 1], ph ^ 1, a.err);
-          issue_raw(kb);
-        }
-        mbar_wait_bounded(&acc_empty[kb & 1], ph ^ 1, a.err);  // epilogue done with block kb-2's metadata
-        mbar_arrive_expect_tx(&bm_full[kb & 1], BM_BYTES);
-        bulk_g2s(sBm + (kb & 1) * QG_META * TN, a.bmeta + (int64_t(tt) * nb + kb) * QG_META * TN, BM_BYTES,
-                 &bm_full[kb & 1]);
         for (int c = 0; c < QG_CPB; ++c) {
-          const int cc = kb * QG_CPB + c, s = cc & 3;
-          mbar_wait_bounded(&b_empty[s], ((cc >> 2) & 1) ^ 1, a.err);
+          const int cc = kb * QG_CPB + c, s = cc & (BST - 1);
+          mbar_spin(&b_empty[s], ((cc >> BLOG) & 1) ^ 1, a.err);
           mbar_arrive_expect_tx(&b_full[s], B_BYTES);
           bulk_g2s(sB + s * B_BYTES, a.bimg + (int64_t(tt) * nchunk + cc) * B_BYTES, B_BYTES, &b_full[s]);
         }
+        const int m = kb & 3;
+        mbar_spin(&bm_empty[m], ((kb >> 2) & 1) ^ 1, a.err);  // epilogue done with block kb-4
+        mbar_arrive_expect_tx(&bm_full[m], BM_BYTES);
+        bulk_g2s(sBm + m * QG_META * TN, a.bmeta + (int64_t(tt) * nb + kb) * QG_META * TN, BM_BYTES, &bm_full[m]);
       }
     }
   } else if (warp == 9) {
@@ -263,12 +324,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       constexpr uint32_t idesc = (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(QG_M >> 4) << 24);
       for (int kb = 0; kb < nb; ++kb) {
         const int b = kb & 1;
-        mbar_wait_bounded(&acc_empty[b], ((kb >> 1) & 1) ^ 1, a.err);
+        mbar_spin(&acc_empty[b], ((kb >> 1) & 1) ^ 1, a.err);
         tc_fence_after();
         for (int c = 0; c < QG_CPB; ++c) {
-          const int cc = kb * QG_CPB + c, sa = cc & amask, sb = cc & 3;
-          mbar_wait_bounded(&a_full[sa], (cc >> alog) & 1, a.err);
-          mbar_wait_bounded(&b_full[sb], (cc >> 2) & 1, a.err);
+          const int cc = kb * QG_CPB + c, sa = cc & amask, sb = cc & (BST - 1);
+          mbar_spin(&a_full[sa], (cc >> alog) & 1, a.err);
+          mbar_spin(&b_full[sb], (cc >> BLOG) & 1, a.err);
           tc_fence_after();
           const uint32_t abase = smem_u32(sA + sa * aslot), bbase = smem_u32(sB + sb * B_BYTES);
 #pragma unroll
@@ -285,141 +346,30 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
         tc_commit(&acc_full[b]);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- dequantisers: thread r = row r of the tile
-    const int r = tid - 128;
-    if (q6) mbar_wait_bounded(d_full, 0, a.err);
-    for (int kb = 0; kb < nb; ++kb) {
-      const int rs = kb & 1, ph = (kb >> 1) & 1;
-      mbar_wait_bounded(&raw_full[rs], ph, a.err);
-      const uint8_t *raw = sRaw + rs * QG_RAW_BYTES;
-      // per-row block metadata for the epilogue (its buffer is free once block kb-2 is done)
-      mbar_wait_bounded(&acc_empty[kb & 1], ph ^ 1, a.err);
-      float *rm = sRm + ((kb & 1) * QG_M + r) * 10;
-      uint32_t scw[4];  // Q4_K: 6-bit scales of the 8 sub-blocks as bytes; Q6_K: 16 int8 scales
-      if (!q6) {
-        const uint4 hd = *reinterpret_cast<const uint4 *>(raw + r * BLOCK_Q4_K);
-        rm[0] = h2f_bits(uint16_t(hd.x & 0xFFFF));
-        rm[1] = h2f_bits(uint16_t(hd.x >> 16));
-        // get_scale_min_k4 (quants.rs:252-261) for sub-blocks 0..7
-        const uint32_t s0 = hd.y, s1 = hd.z, s2 = hd.w;  // bytes 0-3, 4-7, 8-11 of the scale array
-        const uint32_t sc_lo = s0 & 0x3F3F3F3Fu;                                        // sub 0..3
-        const uint32_t mn_lo = s1 & 0x3F3F3F3Fu;
-        const uint32_t sc_hi = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);          // sub 4..7
-        const uint32_t mn_hi = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
-        scw[0] = sc_lo;
-        scw[1] = sc_hi;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          rm[2 + j] = float((mn_lo >> (8 * j)) & 0xFF);
-          rm[6 + j] = float((mn_hi >> (8 * j)) & 0xFF);
-        }
-      } else {
-        rm[0] = h2f_bits(*reinterpret_cast<const uint16_t *>(sD + r * dbox + kb * 2));
-        const uint4 sv = *reinterpret_cast<const uint4 *>(raw + QG_M * 192 + r * 16);
-        scw[0] = sv.x;
-        scw[1] = sv.y;
-        scw[2] = sv.z;
-        scw[3] = sv.w;
-      }
-      mbar_arrive(&rm_full[kb & 1]);
-      for (int c = 0; c < QG_CPB; ++c) {
-        const int cc = kb * QG_CPB + c, s = cc & amask;
-        mbar_wait_bounded(&a_empty[s], ((cc >> alog) & 1) ^ 1, a.err);
-        uint8_t *arow = sA + s * aslot;
-        if (!q6) {
-          // chunk c = elements 64c..64c+63: low nibbles of qs[32c..32c+31] (sub-block 2c), then high
-          // nibbles (sub-block 2c+1)
-          const uint8_t *qs = raw + r * BLOCK_Q4_K + 16 + 32 * c;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int sub = 2 * c + h;
-            const uint32_t scv = ((sub < 4 ? scw[0] : scw[1]) >> (8 * (sub & 3))) & 0xFF;
-            const __half2 s2 = __half2half2(__uint2half_rn(scv));
-            const __half2 nb2 = __half2half2(__uint2half_rn(1024u * scv));
-            const __half2 neg = __hneg2(nb2);
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {  // 16-byte piece = 8 elements
-              const uint2 w = *reinterpret_cast<const uint2 *>(qs + 8 * p);
-              const uint32_t n0 = h ? (w.x >> 4) & 0x0F0F0F0Fu : w.x & 0x0F0F0F0Fu;
-              const uint32_t n1 = h ? (w.y >> 4) & 0x0F0F0F0Fu : w.y & 0x0F0F0F0Fu;
-              uint4 o;
-              o.x = nib_times(__byte_perm(n0, 0u, 0x4140), s2, neg);
-              o.y = nib_times(__byte_perm(n0, 0u, 0x4342), s2, neg);
-              o.z = nib_times(__byte_perm(n1, 0u, 0x4140), s2, neg);
-              o.w = nib_times(__byte_perm(n1, 0u, 0x4342), s2, neg);
-              *reinterpret_cast<uint4 *>(arow + sw128_off(r, 4 * h + p)) = o;
-            }
-          }
-        } else {
-          // chunk c: half n = c/2 of the block; c even: q1 (ql low, qh bits 0-1) then q2 (ql+32 low,
-          // qh bits 2-3); c odd: q3 (ql high, qh bits 4-5) then q4 (ql+32 high, qh bits 6-7)
-          const int n = c >> 1, odd = c & 1;
-          const uint8_t *ql = raw + r * 128 + 64 * n;
-          const uint8_t *qh = raw + QG_M * 128 + r * 64 + 32 * n;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {  // q1/q3 (h = 0) and q2/q4 (h = 1): 32 elements each
-            const int shift_l = odd ? 4 : 0;
-            const int shift_h = 2 * (2 * odd + h);
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {  // 8 elements l = 8p..8p+7
-              const uint2 lw = *reinterpret_cast<const uint2 *>(ql + 32 * h + 8 * p);
-              const uint2 hw = *reinterpret_cast<const uint2 *>(qh + 8 * p);
-              // scale index: 8n + 2*(2*odd + h) + (l >= 16)
-              const int si = 8 * n + 2 * (2 * odd + h) + (p >= 2 ? 1 : 0);
-              const int wsel = si >> 2;
-              const uint32_t sword = wsel == 0 ? scw[0] : wsel == 1 ? scw[1] : wsel == 2 ? scw[2] : scw[3];
-              const int sc = int(int8_t((sword >> (8 * (si & 3))) & 0xFF));
-              uint32_t o[4], ol[4];
-#pragma unroll
-              for (int e2 = 0; e2 < 4; ++e2) {
-                __half hh[2], hl[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                  const int e = 2 * e2 + u;
-                  const uint32_t lb = ((e < 4 ? lw.x : lw.y) >> (8 * (e & 3))) & 0xFF;
-                  const uint32_t hb = ((e < 4 ? hw.x : hw.y) >> (8 * (e & 3))) & 0xFF;
-                  const int q = int(((lb >> shift_l) & 0xF) | (((hb >> shift_h) & 3) << 4));
-                  const int v = sc * (q - 32);  // |v| <= 4096: fp16 hi plus an exact remainder in {-1, 0, 1}
-                  hh[u] = __int2half_rn(v);
-                  hl[u] = __int2half_rn(v - __half2int_rn(hh[u]));
-                }
-                const __half2 hv = __halves2half2(hh[0], hh[1]), lv = __halves2half2(hl[0], hl[1]);
-                o[e2] = *reinterpret_cast<const uint32_t *>(&hv);
-                ol[e2] = *reinterpret_cast<const uint32_t *>(&lv);
-              }
-              *reinterpret_cast<uint4 *>(arow + sw128_off(r, 4 * h + p)) = make_uint4(o[0], o[1], o[2], o[3]);
-              *reinterpret_cast<uint4 *>(arow + QG_A_BYTES + sw128_off(r, 4 * h + p)) =
-                  make_uint4(ol[0], ol[1], ol[2], ol[3]);
-            }
-          }
-        }
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
-        mbar_arrive(&a_full[s]);
-      }
-      mbar_arrive(&raw_empty[rs]);
-    }
   } else {
-    // ---------------- epilogue: thread r = row r = TMEM lane r
-    const int r = tid;
+    // ---------------- warps 0-7: dequantise (thread = row r, half `part` of every chunk); warps
+    // 0-3 also run the epilogue of the previous block (thread = row r = TMEM lane r)
+    const int r = tid & (QG_M - 1), part = tid >> 7;
+    const bool epi = warp < 4;
     float yacc[TN];
 #pragma unroll
     for (int t = 0; t < TN; ++t) yacc[t] = 0.f;
-    const uint32_t lane_base = tmem + (uint32_t(32 * warp) << 16);
-    for (int kb = 0; kb < nb; ++kb) {
+    const uint32_t lane_base = tmem + (uint32_t(32 * (warp & 3)) << 16);
+
+    auto epilogue = [&](int kb) {
       const int b = kb & 1, ph = (kb >> 1) & 1;
-      mbar_wait_bounded(&bm_full[b], ph, a.err);
-      mbar_wait_bounded(&rm_full[b], ph, a.err);
-      mbar_wait_bounded(&acc_full[b], ph, a.err);
+      mbar_wait_bounded(&bm_full[kb & 3], (kb >> 2) & 1, a.err);
+      warp_wait(&rm_full[b], ph, a.err);
+      warp_wait(&acc_full[b], ph, a.err);
       tc_fence_after();
       const float *rm = sRm + (b * QG_M + r) * 10;
-      const float *bm = sBm + b * QG_META * TN;
+      const float *bm = sBm + (kb & 3) * QG_META * TN;
       const float d = rm[0];
       const float dmin = q6 ? 0.f : rm[1];
       float mj[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) mj[j] = q6 ? 0.f : rm[2 + j];
-      constexpr int G = TN < 16 ? TN : 16;
+      constexpr int G = TN < 16 ? TN : (TN >= 64 ? 8 : 16);
 #pragma unroll
       for (int t0 = 0; t0 < TN; t0 += G) {
         uint32_t hi[G], lo[G];
@@ -437,14 +387,145 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[b]);
-    }
-    const int row = row0 + r;
-    if (row < S.rows) {
-      const int tok0 = tt * TN;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[b]);
+        mbar_arrive(&bm_empty[kb & 3]);
+      }
+    };
+
+    if (q6) mbar_wait_bounded(d_full, 0, a.err);
+    for (int kb = 0; kb < nb; ++kb) {
+      const int rs = kb & 1, ph = (kb >> 1) & 1;
+      mbar_wait_bounded(&raw_full[rs], ph, a.err);
+      const uint8_t *raw = sRaw + rs * QG_RAW_BYTES;
+      uint32_t scw[4];  // Q4_K: sc of sub-blocks 0-3 / 4-7 as bytes (scw[0], scw[1]); Q6_K: 16 int8 scales
+      if (!q6) {
+        const uint4 hd = *reinterpret_cast<const uint4 *>(raw + r * BLOCK_Q4_K);
+        // get_scale_min_k4 (quants.rs:252-261) for sub-blocks 0..7
+        scw[0] = hd.y & 0x3F3F3F3Fu;
+        scw[1] = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+        scw[2] = scw[3] = 0u;
+        if (part == 0) {
+          // per-row block metadata for the epilogue (its buffer is free once block kb-2 is done)
+          warp_wait(&acc_empty[kb & 1], ph ^ 1, a.err);
+          float *rm = sRm + ((kb & 1) * QG_M + r) * 10;
+          const uint32_t mn_lo = hd.z & 0x3F3F3F3Fu;
+          const uint32_t mn_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+          rm[0] = h2f_bits(uint16_t(hd.x & 0xFFFF));
+          rm[1] = h2f_bits(uint16_t(hd.x >> 16));
 #pragma unroll
-      for (int t = 0; t < TN; ++t)
-        if (tok0 + t < a.n_tok) S.y[int64_t(tok0 + t) * S.ldy + row] = yacc[t];
+          for (int j = 0; j < 4; ++j) {
+            rm[2 + j] = float((mn_lo >> (8 * j)) & 0xFF);
+            rm[6 + j] = float((mn_hi >> (8 * j)) & 0xFF);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&rm_full[kb & 1]);
+        }
+      } else {
+        const uint4 sv = *reinterpret_cast<const uint4 *>(raw + QG_M * 192 + r * 16);
+        scw[0] = sv.x;
+        scw[1] = sv.y;
+        scw[2] = sv.z;
+        scw[3] = sv.w;
+        if (part == 0) {
+          warp_wait(&acc_empty[kb & 1], ph ^ 1, a.err);
+          sRm[((kb & 1) * QG_M + r) * 10] = h2f_bits(*reinterpret_cast<const uint16_t *>(sD + r * dbox + kb * 2));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&rm_full[kb & 1]);
+        }
+      }
+      for (int c = 0; c < QG_CPB; ++c) {
+        const int cc = kb * QG_CPB + c, s = cc & amask;
+        warp_wait(&a_empty[s], ((cc >> alog) & 1) ^ 1, a.err);
+        uint8_t *arow = sA + s * aslot;
+        if (!q6) {
+          // chunk c = elements 64c..64c+63: low nibbles of qs[32c..32c+31] (sub-block 2c) are
+          // elements 0-31, high nibbles (sub-block 2c+1) elements 32-63.  This thread: bytes
+          // 16*part..16*part+15, i.e. pieces 2part, 2part+1 of each half.
+          const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * BLOCK_Q4_K + 16 + 32 * c + 16 * part);
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int sub = 2 * c + h;
+            const uint32_t scv = ((sub < 4 ? scw[0] : scw[1]) >> (8 * (sub & 3))) & 0xFF;
+            const __half2 s2 = __half2half2(__uint2half_rn(scv));
+            const __half2 neg = __hneg2(__half2half2(__uint2half_rn(1024u * scv)));
+#pragma unroll
+            for (int pp = 0; pp < 2; ++pp) {
+              uint32_t o[4];
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                const uint32_t word = wv[2 * pp + q];
+                const uint32_t nib = h ? (word >> 4) & 0x0F0F0F0Fu : word & 0x0F0F0F0Fu;
+                // bytes [q0, 0x64, q1, 0x64] = fp16x2 (1024 + q0, 1024 + q1)
+                o[2 * q] = half2_times(__byte_perm(nib, 0x64646464u, 0x4140), s2, neg);
+                o[2 * q + 1] = half2_times(__byte_perm(nib, 0x64646464u, 0x4342), s2, neg);
+              }
+              *reinterpret_cast<uint4 *>(arow + sw128_off(r, 4 * h + 2 * part + pp)) =
+                  make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        } else {
+          // chunk c: half n = c/2 of the block; h = 0: q1 (c even: ql low, qh bits 0-1) or q3
+          // (c odd: ql high, qh bits 4-5); h = 1: q2 / q4 (ql + 32, qh bits 2-3 / 6-7).  This
+          // thread: l = 16*part..16*part+15 of both.  sc*(q-32) = 16*sh*(q-32) + sl*(q-32) with
+          // sc = 16*sh + sl, sl in [0, 15]: both products are exact in fp16 and go to the two A tiles.
+          const int n = c >> 1, odd = c & 1;
+          const uint4 qhv = *reinterpret_cast<const uint4 *>(raw + QG_M * 128 + r * 64 + 32 * n + 16 * part);
+          const uint32_t hwv[4] = {qhv.x, qhv.y, qhv.z, qhv.w};
+          const __half2 c1056 = __half2half2(__ushort_as_half(0x6420u));  // 1056.0
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint4 qlv = *reinterpret_cast<const uint4 *>(raw + r * 128 + 64 * n + 32 * h + 16 * part);
+            const uint32_t lwv[4] = {qlv.x, qlv.y, qlv.z, qlv.w};
+            const int shift_l = odd ? 4 : 0;
+            const int shift_h = 2 * (2 * odd + h);
+            const int si = 8 * n + 2 * (2 * odd + h) + part;
+            const int wsel = si >> 2;
+            const uint32_t sword = wsel == 0 ? scw[0] : wsel == 1 ? scw[1] : wsel == 2 ? scw[2] : scw[3];
+            const int sc = int(int8_t((sword >> (8 * (si & 3))) & 0xFF));
+            const __half2 shi = __half2half2(__int2half_rn(16 * (sc >> 4)));
+            const __half2 slo = __half2half2(__int2half_rn(sc & 15));
+#pragma unroll
+            for (int pp = 0; pp < 2; ++pp) {
+              uint32_t oh[4], ol[4];
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                const uint32_t qw = ((lwv[2 * pp + q] >> shift_l) & 0x0F0F0F0Fu) |
+                                    (((hwv[2 * pp + q] >> shift_h) & 0x03030303u) << 4);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const uint32_t pk = __byte_perm(qw, 0x64646464u, e ? 0x4342 : 0x4140);
+                  const __half2 u = __hsub2(*reinterpret_cast<const __half2 *>(&pk), c1056);  // q - 32, exact
+                  const __half2 ph2 = __hmul2(u, shi), pl2 = __hmul2(u, slo);
+                  oh[2 * q + e] = *reinterpret_cast<const uint32_t *>(&ph2);
+                  ol[2 * q + e] = *reinterpret_cast<const uint32_t *>(&pl2);
+                }
+              }
+              const uint32_t off = sw128_off(r, 4 * h + 2 * part + pp);
+              *reinterpret_cast<uint4 *>(arow + off) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+              *reinterpret_cast<uint4 *>(arow + QG_A_BYTES + off) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+            }
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[s]);  // one arrival per warp
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      if (epi && kb > 0) epilogue(kb - 1);
+    }
+    if (epi) {
+      epilogue(nb - 1);
+      const int row = row0 + r;
+      if (row < S.rows) {
+        const int tok0 = tt * TN;
+#pragma unroll
+        for (int t = 0; t < TN; ++t)
+          if (tok0 + t < a.n_tok) S.y[int64_t(tok0 + t) * S.ldy + row] = yacc[t];
+      }
     }
   }
   __syncwarp();  // producer / MMA warps: lanes 1-31 wait for lane 0 before the block barrier
@@ -678,14 +759,14 @@ static bool weight_maps(int type, const void *w, int64_t rows, int64_t K, CUtens
 }
 
 static size_t qgemm_smem(int TN) {
-  return 1024 + size_t(QG_AST) * QG_A_BYTES + size_t(QG_AST) * 2 * TN * 128 + size_t(QG_RST) * QG_RAW_BYTES +
-         QG_M * 128 + 2 * QG_META * TN * 4 + 2 * QG_M * 10 * 4 + 30 * 8;
+  return 1024 + size_t(QG_AST) * QG_A_BYTES + size_t(qg_b_slots(TN)) * 2 * TN * 128 + size_t(QG_RST) * QG_RAW_BYTES +
+         QG_M * 128 + 4 * QG_META * TN * 4 + 2 * QG_M * 10 * 4 + 60 * 8;
 }
 
 // Token-tile width: the largest of 64/32/16/8 that still gives every SM a CTA, else 8.
 static int pick_tn(int64_t row_tiles, int64_t n_tok) {
   int best = 8;
-  for (int tn : {64, 32, 16, 8}) {
+  for (int tn : {32, 16, 8}) {
     if (tn > ((n_tok + 7) / 8) * 8 && tn != 8) continue;
     if (row_tiles * ((n_tok + tn - 1) / tn) * 4 >= int64_t(num_sms()) * 3) return tn;
   }
@@ -693,7 +774,7 @@ static int pick_tn(int64_t row_tiles, int64_t n_tok) {
 }
 
 size_t qgemm_scratch_bytes(int64_t n_tok, int64_t K) {
-  const int64_t tpad = (n_tok + 63) / 64 * 64;  // the widest token tile pads the most
+  const int64_t tpad = (n_tok + 31) / 32 * 32;  // the widest token tile pads the most
   const int64_t nb = K / QK_K;
   return size_t(tpad) * size_t(K) * 4 + size_t(tpad) * nb * QG_META * 4 + 1024;
 }
@@ -747,7 +828,6 @@ cudaError_t qgemm(const QGemmOut *outs, int nseg, int64_t K, const GemmPrologue 
                              TN, img, meta);
   if (e != cudaSuccess) return e;
   switch (TN) {
-    case 64: return launch_qgemm_t<64>(a, tiles, st);
     case 32: return launch_qgemm_t<32>(a, tiles, st);
     case 16: return launch_qgemm_t<16>(a, tiles, st);
     default: return launch_qgemm_t<8>(a, tiles, st);
