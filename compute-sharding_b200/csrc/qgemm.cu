@@ -24,8 +24,9 @@
 //   warp 10  : producer — activation chunks (operand B, pre-swizzled by gemm_bprep_kernel) and
 //              per-block activation metadata with bulk copies
 //   warps 0-7: dequantise the raw blocks into 128-byte-swizzled fp16 A chunks (two threads per row)
-//   warp 9   : one thread issues tcgen05.mma (M=128, N=2*TN, K=16) into one of two TMEM
-//              accumulators (double-buffered across 256-element blocks)
+//   warp 9   : one thread issues tcgen05.mma (M=128, N=2*TN, K=16), 8 per ring step (a step is
+//              one barrier handoff: each acquire-wait costs about as much as several MMAs), into
+//              one of two TMEM accumulators (double-buffered across 256-element blocks)
 //   warps 0-3: also the epilogue, one block behind — tcgen05.ld a finished block's accumulator
 //              (TMEM lane = row), apply the block scales into per-thread fp32 sums, store y at the end
 #include <cuda.h>
@@ -47,7 +48,8 @@ constexpr int QG_CPB = QK_K / QG_KC;  // chunks per 256-element block
 constexpr int QG_AST = 4;        // A/B ring slots (chunks)
 constexpr int QG_RST = 2;        // raw-block ring slots
 constexpr int QG_THREADS = 352;
-constexpr int QG_A_BYTES = QG_M * 128;  // one A chunk: 128 rows x 64 fp16
+constexpr int QG_A_BYTES = QG_M * 128;  // one A tile: 128 rows x 64 fp16
+constexpr int QG_A_SLOT = 2 * QG_A_BYTES;  // one A ring slot: Q4_K two chunks, Q6_K one chunk's two tiles
 constexpr int QG_RAW_BYTES = QG_M * 208;  // largest raw block of 128 rows (Q6_K ql+qh+sc)
 constexpr int QG_MAX_NB = 64;    // K <= 16384
 constexpr int QG_META = 9;       // per (token, block): s and 8 sub-block sums
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned carve-up (swizzled operand tiles need it)
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t *sA = smem;                                  // [QG_AST][QG_A_BYTES]
+  uint8_t *sA = smem;                                  // [2][QG_A_SLOT]
   uint8_t *sB = sA + QG_AST * QG_A_BYTES;              // [BST][B_BYTES]
   uint8_t *sRaw = sB + BST * B_BYTES;                  // [QG_RST][QG_RAW_BYTES]
   uint8_t *sD = sRaw + QG_RST * QG_RAW_BYTES;          // Q6_K d of all blocks: [128][<= 128 B]
@@ -223,9 +225,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   const bool q6 = S.type == T_Q6_K;
   const int raw_bytes = q6 ? QG_M * 208 : QG_M * BLOCK_Q4_K;
   const int dbox = (2 * nb + 15) / 16 * 16;
-  // A ring: Q4_K 4 slots of one 16 KB tile; Q6_K 2 slots of two tiles (fp16 products and their
-  // rounding remainders), the same 64 KB either way
-  const int alog = q6 ? 1 : 2, amask = (1 << alog) - 1, aslot = q6 ? 2 * QG_A_BYTES : QG_A_BYTES;
+  // A ring: 2 slots of 32 KB, one MMA step each: Q4_K two 64-element chunks, Q6_K one chunk as its
+  // two tiles (16*sh*(q-32) and sl*(q-32))
+  const int spb = q6 ? 4 : 2;   // MMA steps (8 MMAs, one barrier handoff each) per 256-element block
+  const int cps = q6 ? 1 : 2;   // 64-element chunks per step
 
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) {
@@ -326,22 +329,25 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
         const int b = kb & 1;
         mbar_spin(&acc_empty[b], ((kb >> 1) & 1) ^ 1, a.err);
         tc_fence_after();
-        for (int c = 0; c < QG_CPB; ++c) {
-          const int cc = kb * QG_CPB + c, sa = cc & amask, sb = cc & (BST - 1);
-          mbar_spin(&a_full[sa], (cc >> alog) & 1, a.err);
-          mbar_spin(&b_full[sb], (cc >> BLOG) & 1, a.err);
+        for (int st = 0; st < spb; ++st) {
+          const int gs = kb * spb + st, slot = gs & 1;
+          mbar_spin(&a_full[slot], (gs >> 1) & 1, a.err);  // A written and the step's B chunks landed
           tc_fence_after();
-          const uint32_t abase = smem_u32(sA + sa * aslot), bbase = smem_u32(sB + sb * B_BYTES);
+          const uint32_t abase = smem_u32(sA + slot * QG_A_SLOT);
+          for (int h2 = 0; h2 < cps; ++h2) {
+            const int gcc = kb * QG_CPB + (q6 ? st : 2 * st + h2), sb = gcc & (BST - 1);
+            const uint32_t bbase = smem_u32(sB + sb * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < QG_KC / 16; ++k) {
-            tc_mma_f16(tmem + uint32_t(b * N), sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc,
-                       (c | k) != 0);
-            if (q6)  // the rounding remainders of the Q6_K products (exact small integers)
-              tc_mma_f16(tmem + uint32_t(b * N), sw128_desc(abase + QG_A_BYTES + k * 32), sw128_desc(bbase + k * 32),
-                         idesc, 1u);
+            for (int k = 0; k < QG_KC / 16; ++k) {
+              tc_mma_f16(tmem + uint32_t(b * N), sw128_desc(abase + h2 * QG_A_BYTES + k * 32),
+                         sw128_desc(bbase + k * 32), idesc, (st | h2 | k) != 0);
+              if (q6)  // second Q6_K tile: sl*(q-32) (the first holds 16*sh*(q-32))
+                tc_mma_f16(tmem + uint32_t(b * N), sw128_desc(abase + QG_A_BYTES + k * 32),
+                           sw128_desc(bbase + k * 32), idesc, 1u);
+            }
+            tc_commit(&b_empty[sb]);
           }
-          tc_commit(&a_empty[sa]);
-          tc_commit(&b_empty[sb]);
+          tc_commit(&a_empty[slot]);
         }
         tc_commit(&acc_full[b]);
       }
@@ -435,10 +441,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
           if (lane == 0) mbar_arrive(&rm_full[kb & 1]);
         }
       }
-      for (int c = 0; c < QG_CPB; ++c) {
-        const int cc = kb * QG_CPB + c, s = cc & amask;
-        warp_wait(&a_empty[s], ((cc >> alog) & 1) ^ 1, a.err);
-        uint8_t *arow = sA + s * aslot;
+      for (int st = 0; st < spb; ++st) {
+        const int gs = kb * spb + st, slot = gs & 1;
+        warp_wait(&a_empty[slot], ((gs >> 1) & 1) ^ 1, a.err);
+        for (int h2 = 0; h2 < cps; ++h2) {
+        const int c = q6 ? st : 2 * st + h2;
+        uint8_t *arow = sA + slot * QG_A_SLOT + h2 * QG_A_BYTES;
         if (!q6) {
           // chunk c = elements 64c..64c+63: low nibbles of qs[32c..32c+31] (sub-block 2c) are
           // elements 0-31, high nibbles (sub-block 2c+1) elements 32-63.  This thread: bytes
@@ -509,9 +517,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
             }
           }
         }
+        }
+        if (warp == 0 && lane == 0)  // the step's activation chunks must have landed as well
+          for (int h2 = 0; h2 < cps; ++h2) {
+            const int gcc = kb * QG_CPB + (q6 ? st : 2 * st + h2);
+            mbar_spin(&b_full[gcc & (BST - 1)], (gcc >> BLOG) & 1, a.err);
+          }
         fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[s]);  // one arrival per warp
+        if (lane == 0) mbar_arrive(&a_full[slot]);  // one arrival per warp
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&raw_empty[rs]);
