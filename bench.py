@@ -34,8 +34,8 @@ GEMV_BYTES = 10240 * 10 * 144 + 2560 * 4 + 10240 * 4
 LAYER_WEIGHT_BYTES = 60_518_400
 EMBD_BYTES = VOCAB * HIDDEN * 2
 # dram__bytes_read.sum + dram__bytes_write.sum of one qgemv_kernel<1,1> launch on that shape, from
-# the ncu capture summarised in profiles/qgemv_q4k_10240x2560_1tok.md (None until captured)
-GEMV_DRAM_BYTES = None
+# the ncu capture summarised in profiles/qgemv_q4k_10240x2560_1tok.md
+GEMV_DRAM_BYTES = 14_804_992
 
 
 def env_rank():
