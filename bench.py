@@ -38,6 +38,14 @@ EMBD_BYTES = VOCAB * HIDDEN * 2
 GEMV_DRAM_BYTES = 14_804_992
 
 
+def bs1_config(world: int = 1) -> dict:
+    """`config` of the headline line, shared by both arms."""
+    return {"workload": "42-layer Gemma-style Q4_K_M greedy decode, batch 1, after a 512-token prompt",
+            "layers": N_LAYERS, "d_model": HIDDEN, "heads": "8q/4kv x 256", "ffn": 10240, "vocab": VOCAB,
+            "prompt": PROMPT, "parallelism": f"pp{world}", "kv": "fp16",
+            "l2": "inputs larger than L2 (3.9 GB of weights read per token)"}
+
+
 def env_rank():
     return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
 
@@ -133,8 +141,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "42-layer Gemma-style Q4_K_M decode, batch 1", "layers": N_LAYERS,
-                       "d_model": HIDDEN, "vocab": VOCAB},
+            "config": bs1_config(world),
             "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
             "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -264,10 +271,7 @@ def run_single(args):
         "metric": METRIC, "value": bs1_tps, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": bs1_s * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "42-layer Gemma-style Q4_K_M greedy decode, batch 1, after a 512-token prompt",
-                   "layers": N_LAYERS, "d_model": HIDDEN, "heads": "8q/4kv x 256", "ffn": 10240, "vocab": VOCAB,
-                   "prompt": PROMPT, "parallelism": "pp1", "kv": "fp16",
-                   "l2": "inputs larger than L2 (3.9 GB of weights read per token)"},
+        "config": bs1_config(1),
         "bs1_step_bandwidth_gbs": token_bytes / (bs1_s / args.steps) / 1e9,
         "bs64": {"value": bs64_tps, "unit": "tokens/s", "steps": bsteps, "ms_per_step": bs64_s * 1e3 / bsteps,
                  "workload": "64 sequences, contexts uniform 512..3584 (seeded synthetic KV), 1 token each per step"},
@@ -374,11 +378,8 @@ def run_pipeline(args):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": bs1_s * 1e3 / args.steps,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic",
-                "config": {"workload": "42-layer Gemma-style Q4_K_M greedy decode, batch 1, after a 512-token prompt",
-                           "layers": N_LAYERS, "d_model": HIDDEN, "vocab": VOCAB, "prompt": PROMPT,
-                           "parallelism": f"pp{world}", "split": even_stage_split(N_LAYERS, world),
-                           "handoff": "NCCL send/recv of f32 hidden rows", "kv": "fp16",
-                           "l2": "inputs larger than L2"},
+                "config": dict(bs1_config(world), split=even_stage_split(N_LAYERS, world),
+                               handoff="NCCL send/recv of f32 hidden rows"),
                 "bs64": {"value": 64 * bsteps / bs64_s, "unit": "tokens/s", "steps": bsteps,
                          "microbatches": "8 x 8 sequences"},
                 "e2e": {"value": args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 8,

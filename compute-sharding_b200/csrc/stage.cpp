@@ -1232,7 +1232,7 @@ int sfc_forward_dev(sfc_stage *h, const char *const *request_ids, const int32_t 
   SFC_REQUIRE(n_seq <= h->max_sessions, "batch of %d sequences exceeds max_sessions %d", n_seq, h->max_sessions);
   SFC_REQUIRE(h->is_head ? ids_dev != nullptr : in_dev != nullptr, "missing input");
   SFC_CUDA(cudaSetDevice(h->device));
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);  // NULL = the legacy default stream, as documented
   std::vector<SeqReq> seqs;
   int64_t T = 0;
   for (int i = 0; i < n_seq; ++i) {
@@ -1267,7 +1267,7 @@ int sfc_sample_dev(sfc_stage *h, const float *hidden_dev, int64_t n, int64_t *to
   SFC_REQUIRE(h && hidden_dev && tokens_dev && scores_dev, "null argument");
   SFC_CUDA(cudaSetDevice(h->device));
   return sample_rows(h, hidden_dev, n, tokens_dev, scores_dev,
-                     stream ? static_cast<cudaStream_t>(stream) : h->stream);
+                     static_cast<cudaStream_t>(stream));
 }
 
 int sfc_verify_greedy(sfc_stage *h, const float *hidden, const uint32_t *drafts, int64_t k, int64_t *accepted,

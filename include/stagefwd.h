@@ -10,7 +10,9 @@
  *    last failure on the calling thread is available from sfc_last_error().  Bad input
  *    (shapes, ids, offsets, sizes) is rejected on the host before any kernel runs.
  *  - "dev" pointers are device pointers on the handle's / current device; `stream` is a
- *    cudaStream_t (NULL = legacy default stream).  Host-pointer entry points synchronise.
+ *    cudaStream_t (NULL = legacy default stream).  Host-pointer entry points run on the stage's
+ *    own stream and synchronise it before returning; device-pointer work a caller queued on
+ *    another stream for the same stage must be complete (or event-ordered) before them.
  *  - Weight layouts are GGUF (ggml_type ids: F32=0, F16=1, Q4_K=12, Q6_K=14, BF16=30);
  *    rows hold `in_dim` elements, tensor dims are GGUF [in_dim, out_dim].
  *  - A stage handle is not re-entrant: one host thread drives it at a time (the reference's
