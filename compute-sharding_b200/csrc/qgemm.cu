@@ -77,6 +77,8 @@ struct QGemmArgs {
   int n_ttiles;  // token tiles
   const uint8_t *bimg;   // [ttile][K/64 chunks][N rows x 128 B] swizzled fp16 (hi rows, then lo rows)
   const float *bmeta;    // [ttile][nb][9][TN]
+  float *part;           // split-K partials [split][n_tok][tiles*128] (null: one split, write y)
+  int64_t part_ld;       // tiles * 128
   unsigned *err;
 };
 
@@ -222,6 +224,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   const int row0 = (int(blockIdx.x) - S.tile0) * QG_M;
   const int tt = blockIdx.y;
   const int nb = a.nb, nchunk = nb * QG_CPB;
+  // split-K: this CTA's blocks are kbeg .. kbeg+nbl-1; loops below run over the local index kb
+  // (ring slots and phases) and add kbeg where they address data
+  const int kbeg = int(int64_t(nb) * blockIdx.z / gridDim.z);
+  const int nbl = int(int64_t(nb) * (blockIdx.z + 1) / gridDim.z) - kbeg;
   const bool q6 = S.type == T_Q6_K;
   const int raw_bytes = q6 ? QG_M * 208 : QG_M * BLOCK_Q4_K;
   const int dbox = (2 * nb + 15) / 16 * 16;
@@ -263,13 +269,14 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   const uint32_t tmem = *tmem_slot;
 
   auto prefetch_raw_l2 = [&](int kb) {
-    if (kb >= nb) return;
+    if (kb >= nbl) return;
+    const int kg = kbeg + kb;
     if (!q6) {
-      tma_prefetch_2d(&S.map[0], kb * BLOCK_Q4_K, row0);
+      tma_prefetch_2d(&S.map[0], kg * BLOCK_Q4_K, row0);
     } else {
-      tma_prefetch_2d(&S.map[0], kb * 128, row0);
-      tma_prefetch_2d(&S.map[1], nb * 128 + kb * 64, row0);
-      tma_prefetch_2d(&S.map[2], nb * 192 + kb * 16, row0);
+      tma_prefetch_2d(&S.map[0], kg * 128, row0);
+      tma_prefetch_2d(&S.map[1], nb * 128 + kg * 64, row0);
+      tma_prefetch_2d(&S.map[2], nb * 192 + kg * 16, row0);
     }
   };
   auto issue_raw = [&](int kb) {
@@ -277,12 +284,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
     prefetch_raw_l2(kb + QG_RST);
     uint8_t *dst = sRaw + rs * QG_RAW_BYTES;
     mbar_arrive_expect_tx(&raw_full[rs], uint32_t(raw_bytes));
+    const int kg = kbeg + kb;
     if (!q6) {
-      tma_load_2d(dst, &S.map[0], kb * BLOCK_Q4_K, row0, &raw_full[rs]);
+      tma_load_2d(dst, &S.map[0], kg * BLOCK_Q4_K, row0, &raw_full[rs]);
     } else {
-      tma_load_2d(dst, &S.map[0], kb * 128, row0, &raw_full[rs]);                       // ql [128][128]
-      tma_load_2d(dst + QG_M * 128, &S.map[1], nb * 128 + kb * 64, row0, &raw_full[rs]);  // qh [128][64]
-      tma_load_2d(dst + QG_M * 192, &S.map[2], nb * 192 + kb * 16, row0, &raw_full[rs]); // sc [128][16]
+      tma_load_2d(dst, &S.map[0], kg * 128, row0, &raw_full[rs]);                       // ql [128][128]
+      tma_load_2d(dst + QG_M * 128, &S.map[1], nb * 128 + kg * 64, row0, &raw_full[rs]);  // qh [128][64]
+      tma_load_2d(dst + QG_M * 192, &S.map[2], nb * 192 + kg * 16, row0, &raw_full[rs]); // sc [128][16]
     }
   };
   // weights never depend on the previous kernel: start them before the dependency wait
@@ -291,7 +299,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       mbar_arrive_expect_tx(d_full, uint32_t(QG_M * dbox));
       tma_load_2d(sD, &S.map[3], nb * 208, row0, d_full);
     }
-    for (int kb = 0; kb < nb && kb < QG_RST; ++kb) issue_raw(kb);
+    for (int kb = 0; kb < nbl && kb < QG_RST; ++kb) issue_raw(kb);
   }
   pdl_wait();
   pdl_launch_dependents();
@@ -299,7 +307,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   if (warp == 8) {
     // ---------------- producer of the raw weight blocks
     if (lane == 0) {
-      for (int kb = QG_RST; kb < nb; ++kb) {
+      for (int kb = QG_RST; kb < nbl; ++kb) {
         mbar_spin(&raw_empty[kb & 1], ((kb >> 1) & 1) ^ 1, a.err);
         issue_raw(kb);
       }
@@ -308,24 +316,26 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
     // ---------------- producer of the activation chunks and per-block activation metadata (its own
     // warp: spinning lanes of one warp would take turns)
     if (lane == 0) {
-      for (int kb = 0; kb < nb; ++kb) {
+      for (int kb = 0; kb < nbl; ++kb) {
         for (int c = 0; c < QG_CPB; ++c) {
           const int cc = kb * QG_CPB + c, s = cc & (BST - 1);
           mbar_spin(&b_empty[s], ((cc >> BLOG) & 1) ^ 1, a.err);
           mbar_arrive_expect_tx(&b_full[s], B_BYTES);
-          bulk_g2s(sB + s * B_BYTES, a.bimg + (int64_t(tt) * nchunk + cc) * B_BYTES, B_BYTES, &b_full[s]);
+          bulk_g2s(sB + s * B_BYTES, a.bimg + (int64_t(tt) * nchunk + kbeg * QG_CPB + cc) * B_BYTES, B_BYTES,
+                   &b_full[s]);
         }
         const int m = kb & 3;
         mbar_spin(&bm_empty[m], ((kb >> 2) & 1) ^ 1, a.err);  // epilogue done with block kb-4
         mbar_arrive_expect_tx(&bm_full[m], BM_BYTES);
-        bulk_g2s(sBm + m * QG_META * TN, a.bmeta + (int64_t(tt) * nb + kb) * QG_META * TN, BM_BYTES, &bm_full[m]);
+        bulk_g2s(sBm + m * QG_META * TN, a.bmeta + (int64_t(tt) * nb + kbeg + kb) * QG_META * TN, BM_BYTES,
+                 &bm_full[m]);
       }
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(QG_M >> 4) << 24);
-      for (int kb = 0; kb < nb; ++kb) {
+      for (int kb = 0; kb < nbl; ++kb) {
         const int b = kb & 1;
         mbar_spin(&acc_empty[b], ((kb >> 1) & 1) ^ 1, a.err);
         tc_fence_after();
@@ -401,7 +411,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
     };
 
     if (q6) mbar_wait_bounded(d_full, 0, a.err);
-    for (int kb = 0; kb < nb; ++kb) {
+    for (int kb = 0; kb < nbl; ++kb) {
       const int rs = kb & 1, ph = (kb >> 1) & 1;
       mbar_wait_bounded(&raw_full[rs], ph, a.err);
       const uint8_t *raw = sRaw + rs * QG_RAW_BYTES;
@@ -436,7 +446,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
         scw[3] = sv.w;
         if (part == 0) {
           warp_wait(&acc_empty[kb & 1], ph ^ 1, a.err);
-          sRm[((kb & 1) * QG_M + r) * 10] = h2f_bits(*reinterpret_cast<const uint16_t *>(sD + r * dbox + kb * 2));
+          sRm[((kb & 1) * QG_M + r) * 10] = h2f_bits(*reinterpret_cast<const uint16_t *>(sD + r * dbox + (kbeg + kb) * 2));
           __syncwarp();
           if (lane == 0) mbar_arrive(&rm_full[kb & 1]);
         }
@@ -532,10 +542,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       if (epi && kb > 0) epilogue(kb - 1);
     }
     if (epi) {
-      epilogue(nb - 1);
+      epilogue(nbl - 1);
       const int row = row0 + r;
-      if (row < S.rows) {
-        const int tok0 = tt * TN;
+      const int tok0 = tt * TN;
+      if (a.part) {  // split-K partial of global row blockIdx.x*128 + r
+        float *pp = a.part + (int64_t(blockIdx.z) * a.n_tok) * a.part_ld + int64_t(blockIdx.x) * QG_M + r;
+#pragma unroll
+        for (int t = 0; t < TN; ++t)
+          if (tok0 + t < a.n_tok) pp[int64_t(tok0 + t) * a.part_ld] = yacc[t];
+      } else if (row < S.rows) {
 #pragma unroll
         for (int t = 0; t < TN; ++t)
           if (tok0 + t < a.n_tok) S.y[int64_t(tok0 + t) * S.ldy + row] = yacc[t];
@@ -778,19 +793,53 @@ static size_t qgemm_smem(int TN) {
 }
 
 // Token-tile width: the largest of 64/32/16/8 that still gives every SM a CTA, else 8.
-static int pick_tn(int64_t row_tiles, int64_t n_tok) {
-  int best = 8;
-  for (int tn : {32, 16, 8}) {
-    if (tn > ((n_tok + 7) / 8) * 8 && tn != 8) continue;
-    if (row_tiles * ((n_tok + tn - 1) / tn) * 4 >= int64_t(num_sms()) * 3) return tn;
-  }
-  return best;
+// Token-tile width: every tile costs a CTA about the same time (its block pipeline does not speed
+// up with fewer tokens), so use the widest tile the tokens fill: fewest CTAs and waves.
+static int pick_tn(int64_t n_tok) { return n_tok <= 8 ? 8 : n_tok <= 16 ? 16 : n_tok <= 32 ? 32 : 64; }
+
+// K splits: shapes with few row and token tiles (o, down: 20 row tiles) split K so the grid still
+// covers the SMs; each split keeps at least two 256-element blocks.
+static int pick_splits(int64_t ctas, int nb) {
+  if (ctas * 2 >= num_sms()) return 1;
+  int64_t s = num_sms() / ctas;
+  if (s > nb / 2) s = nb / 2;
+  return s < 1 ? 1 : int(s);
 }
 
+// Largest split-K partial buffer: splits x row tiles x token tiles <= SMs, tokens per tile <= 64.
+static size_t qgemm_part_bytes_max() { return size_t(num_sms()) * 64 * QG_M * 4 + 256; }
+
 size_t qgemm_scratch_bytes(int64_t n_tok, int64_t K) {
-  const int64_t tpad = (n_tok + 31) / 32 * 32;  // the widest token tile pads the most
+  const int64_t tpad = (n_tok + 63) / 64 * 64;  // the widest token tile pads the most
   const int64_t nb = K / QK_K;
-  return size_t(tpad) * size_t(K) * 4 + size_t(tpad) * nb * QG_META * 4 + 1024;
+  return size_t(tpad) * size_t(K) * 4 + 256 + size_t(tpad) * nb * QG_META * 4 + 256 + qgemm_part_bytes_max() + 1024;
+}
+
+struct QGemmOutMap {
+  float *y[QG_MAX_SEG];
+  int64_t ldy[QG_MAX_SEG];
+  int rows[QG_MAX_SEG];
+  int row0[QG_MAX_SEG];  // first global row (tile0 * 128) of each segment
+  int nseg;
+};
+
+// y[t][row] = sum over splits of the partials, in split order (deterministic)
+__global__ void splitk_reduce_kernel(const float *__restrict__ part, int nsplit, int n_tok, int64_t part_ld,
+                                     QGemmOutMap m) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t total = int64_t(n_tok) * part_ld;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int t = int(i / part_ld);
+    const int gr = int(i % part_ld);
+    int sg = 0;
+    while (sg + 1 < m.nseg && gr >= m.row0[sg + 1]) ++sg;
+    const int lr = gr - m.row0[sg];
+    if (lr >= m.rows[sg]) continue;
+    float v = 0.f;
+    for (int z = 0; z < nsplit; ++z) v += part[(int64_t(z) * n_tok + t) * part_ld + gr];
+    m.y[sg][int64_t(t) * m.ldy[sg] + lr] = v;
+  }
 }
 
 bool qgemm_supported(int type, int64_t K) {
@@ -798,11 +847,12 @@ bool qgemm_supported(int type, int64_t K) {
 }
 
 template <int TN>
-static cudaError_t launch_qgemm_t(QGemmArgs &a, int row_tiles, cudaStream_t st) {
+static cudaError_t launch_qgemm_t(QGemmArgs &a, int row_tiles, int nsplit, cudaStream_t st) {
   const size_t smem = qgemm_smem(TN);
   cudaError_t e = cudaFuncSetAttribute(qgemm_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return launch_pdl(qgemm_kernel<TN>, dim3(unsigned(row_tiles), unsigned(a.n_ttiles)), dim3(QG_THREADS), smem, st, a);
+  return launch_pdl(qgemm_kernel<TN>, dim3(unsigned(row_tiles), unsigned(a.n_ttiles), unsigned(nsplit)),
+                    dim3(QG_THREADS), smem, st, a);
 }
 
 cudaError_t qgemm(const QGemmOut *outs, int nseg, int64_t K, const GemmPrologue &pro, int64_t n_tok, void *scratch,
@@ -830,22 +880,44 @@ cudaError_t qgemm(const QGemmOut *outs, int nseg, int64_t K, const GemmPrologue 
     s.tile0 = tiles;
     tiles += int((o.rows + QG_M - 1) / QG_M);
   }
-  const int TN = pick_tn(tiles, n_tok);
+  const int TN = pick_tn(n_tok);
   a.n_ttiles = int((n_tok + TN - 1) / TN);
+  const int nsplit = pick_splits(int64_t(tiles) * a.n_ttiles, a.nb);
   const int64_t tpad = int64_t(a.n_ttiles) * TN;
   uint8_t *img = static_cast<uint8_t *>(scratch);
   const size_t img_bytes = size_t(tpad) * size_t(K) * 4;
   float *meta = reinterpret_cast<float *>(img + (img_bytes + 255) / 256 * 256);
+  const size_t meta_bytes = size_t(tpad) * a.nb * QG_META * 4;
   a.bimg = img;
   a.bmeta = meta;
+  if (nsplit > 1) {
+    a.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(meta) + (meta_bytes + 255) / 256 * 256);
+    a.part_ld = int64_t(tiles) * QG_M;
+    if (size_t(nsplit) * n_tok * a.part_ld * 4 > qgemm_part_bytes_max()) return cudaErrorInvalidValue;
+  }
   cudaError_t e = launch_pdl(gemm_bprep_kernel, dim3(unsigned(tpad)), dim3(BP_WARPS * 32), 0, st, pro, K, int(n_tok),
                              TN, img, meta);
   if (e != cudaSuccess) return e;
   switch (TN) {
-    case 32: return launch_qgemm_t<32>(a, tiles, st);
-    case 16: return launch_qgemm_t<16>(a, tiles, st);
-    default: return launch_qgemm_t<8>(a, tiles, st);
+    case 64: e = launch_qgemm_t<64>(a, tiles, nsplit, st); break;
+    case 32: e = launch_qgemm_t<32>(a, tiles, nsplit, st); break;
+    case 16: e = launch_qgemm_t<16>(a, tiles, nsplit, st); break;
+    default: e = launch_qgemm_t<8>(a, tiles, nsplit, st); break;
   }
+  if (e != cudaSuccess || nsplit == 1) return e;
+  QGemmOutMap m = {};
+  m.nseg = nseg;
+  for (int i = 0; i < nseg; ++i) {
+    m.y[i] = a.seg[i].y;
+    m.ldy[i] = a.seg[i].ldy;
+    m.rows[i] = a.seg[i].rows;
+    m.row0[i] = a.seg[i].tile0 * QG_M;
+  }
+  const int64_t total = n_tok * a.part_ld;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
+  return launch_pdl(splitk_reduce_kernel, dim3(unsigned(blocks)), dim3(256), 0, st, (const float *)a.part, nsplit,
+                    int(n_tok), a.part_ld, m);
 }
 
 }  // namespace sfc
