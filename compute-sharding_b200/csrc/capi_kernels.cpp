@@ -168,6 +168,17 @@ int sfc_logits_argmax(int ggml_type, const void *w_dev, int64_t vocab, int64_t d
   return SFC_OK;
 }
 
+int sfc_sample_temperature(const float *scores_dev, int64_t n, int64_t vocab, float temperature, uint64_t seed,
+                           int64_t *tokens_dev, void *stream) {
+  clear_error();
+  SFC_REQUIRE(scores_dev && tokens_dev, "null pointer");
+  SFC_REQUIRE(n >= 0 && vocab > 0, "bad shape");
+  SFC_REQUIRE(temperature > 0.f, "temperature must be positive (use the argmax for greedy)");
+  SFC_CUDA(sample_rows_temperature(scores_dev, n, vocab, temperature, seed, tokens_dev,
+                                   static_cast<cudaStream_t>(stream)));
+  return SFC_OK;
+}
+
 int sfc_synth_tensor(int ggml_type, uint64_t seed, const char *name, int64_t rows, int64_t in_dim, float sigma,
                      float mean, void *out_dev, void *stream) {
   SFC_REQUIRE(name && out_dev, "null pointer");

@@ -25,6 +25,15 @@ enum DeviceError : unsigned { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_ARG = 2 
 // hardware time hint, so this is seconds, far above any legitimate latency).
 constexpr unsigned MBAR_SPIN_LIMIT = 1u << 24;
 
+// SplitMix64 finaliser of key + (ctr + 1) * golden ratio: the counter-based hash behind the
+// synthetic weights and the seeded sampling uniforms (identical on host and device).
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t key, uint64_t ctr) {
+  uint64_t z = key + (ctr + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
 __device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 // ---- mbarrier + bulk async copy (TMA engine, non-tensor form) ----------------

@@ -116,8 +116,21 @@ struct KVLayer {
 };
 
 // q/k/v post-processing for a batch: per-head norms, RoPE, KV append (real_forward.rs:1583-1662).
+// rope_pos (nullable): per-row rotary position when it differs from the cache position (tree
+// verification: prefix length + node depth).
 cudaError_t qkv_post(float *q, const float *k, const float *v, int q_ld, int kv_ld, KVLayer kv, const SeqInfo *seqs,
-                     const int32_t *tok_seq, int64_t n_tok, const AttnParams &p, cudaStream_t st);
+                     const int32_t *tok_seq, const int32_t *rope_pos, int64_t n_tok, const AttnParams &p,
+                     cudaStream_t st);
+// KV of tree nodes kept after verification: for every layer, rows pos0 + path[i] -> pos0 + i of
+// `slot` (path strictly increasing, path[i] >= i, so no copy reads a row another one writes).
+cudaError_t kv_compact(void *kv_arena, int n_layers, int max_sessions, int64_t slot_stride, int slot, int n_kv,
+                       int64_t max_ctx, int head_dim, int elt_bytes, int pos0, const int32_t *path, int m,
+                       cudaStream_t st);
+// Temperature sampling of n rows of scores [n][vocab]: p ~ exp((s - max) / temperature), one
+// counter-based uniform per row (mix64(seed, row) >> 40, times 2^-24); contiguous vocabulary
+// segments of ceil(vocab / 1024) per thread, summed in index order, so the walk is reproducible.
+cudaError_t sample_rows_temperature(const float *scores, int64_t n, int64_t vocab, float temperature, uint64_t seed,
+                                    int64_t *out, cudaStream_t st);
 // Tensor-core K-quant GEMM (qgemm.cu) for 8+ tokens.  The activation operand is prepared from
 // the prologue inputs: mode 0 x; mode 1 RMSNorm(a) * w_next; mode 2 residual add + norms as in
 // GemvPrologue; `gate`/`up` non-null: x = gelu_tanh(gate) * up.  Up to 3 output matrices with the

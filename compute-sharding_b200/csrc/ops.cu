@@ -155,7 +155,8 @@ cudaError_t embed(int type, const void *table, int64_t vocab, int dim, const voi
 __global__ void __launch_bounds__(256) qkv_post_kernel(float *__restrict__ q, const float *__restrict__ k,
                                                       const float *__restrict__ v, int q_ld, int kv_ld, KVLayer kv,
                                                       const SeqInfo *__restrict__ seqs,
-                                                      const int32_t *__restrict__ tok_seq, AttnParams p) {
+                                                      const int32_t *__restrict__ tok_seq,
+                                                      const int32_t *__restrict__ rope_pos, AttnParams p) {
   __shared__ float hv[1024];
   __shared__ float sh[8];
   pdl_wait();
@@ -189,7 +190,8 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(float *__restrict__ q, co
   }
   __syncthreads();
   const SeqInfo sq = seqs[tok_seq[t]];
-  const int pos = sq.pos0 + (t - sq.tok0);
+  const int pos = sq.pos0 + (t - sq.tok0);          // cache position of this row
+  const int rpos = rope_pos ? rope_pos[t] : pos;     // rotary position (tree nodes: prefix + depth)
   if (kind != 2 && p.rope_freqs) {
     const int hde = hd & ~1;
     const int rd = min(p.rotary_dim, hde) & ~1;
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(float *__restrict__ q, co
     for (int i = threadIdx.x; i < n_ang; i += 256) {
       const float inv_freq = 1.0f / powf(p.rope_theta, 2.0f * float(i) / denom);
       const float fs = i < p.n_freqs ? p.rope_freqs[i] : 1.0f;
-      const float th = float(pos) * inv_freq * fs;
+      const float th = float(rpos) * inv_freq * fs;
       float sn, cs;
       sincosf(th, &sn, &cs);
       const float x0 = hv[i], x1 = hv[half + i];
@@ -225,11 +227,12 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(float *__restrict__ q, co
 }
 
 cudaError_t qkv_post(float *q, const float *k, const float *v, int q_ld, int kv_ld, KVLayer kv, const SeqInfo *seqs,
-                     const int32_t *tok_seq, int64_t n_tok, const AttnParams &p, cudaStream_t st) {
+                     const int32_t *tok_seq, const int32_t *rope_pos, int64_t n_tok, const AttnParams &p,
+                     cudaStream_t st) {
   if (n_tok <= 0) return cudaSuccess;
   if (p.head_dim > 1024) return cudaErrorInvalidValue;
   return launch_pdl(qkv_post_kernel, dim3(unsigned(n_tok), unsigned(p.n_heads + 2 * p.n_kv)), dim3(256), 0, st, q, k,
-                    v, q_ld, kv_ld, kv, seqs, tok_seq, p);
+                    v, q_ld, kv_ld, kv, seqs, tok_seq, rope_pos, p);
 }
 
 // ---------------------------------------------------------------- attention

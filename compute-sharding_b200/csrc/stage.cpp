@@ -275,6 +275,13 @@ struct sfc_stage {
   void *gemm_scratch = nullptr;
   size_t gemm_scratch_bytes = 0;
   float *act2 = nullptr;
+  // draft-tree verification: per-row rotary positions, visible-key limits and ancestor masks of the
+  // current tree batch (set only while a tree forward runs), and the tail's score rows
+  int32_t *tree_rope_dev = nullptr, *tree_limit_dev = nullptr, *tree_path_dev = nullptr;
+  uint64_t *tree_mask_dev = nullptr;
+  bool tree_active = false;
+  float *tree_scores = nullptr;
+  int64_t tree_scores_rows = 0;
   size_t attn_scratch = 0, logit_scratch = 0;
   int64_t gen_capacity = 0;
   PinnedRing ring;
@@ -609,7 +616,9 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
       (rc = alloc((void **)&h->act, T * std::max(h->ffn, 1) * 4)) || (rc = alloc((void **)&h->hn, T * H * 4)) ||
       (rc = alloc((void **)&h->score_dev, T * 4)) || (rc = alloc((void **)&h->ids_dev, T * 4)) ||
       (rc = alloc((void **)&h->tok_dev, T * 8)) || (rc = alloc((void **)&h->tok_seq_dev, T * 4)) ||
-      (rc = alloc((void **)&h->step_dev, 4)) ||
+      (rc = alloc((void **)&h->step_dev, 4)) || (rc = alloc((void **)&h->tree_rope_dev, T * 4)) ||
+      (rc = alloc((void **)&h->tree_limit_dev, T * 4)) || (rc = alloc((void **)&h->tree_path_dev, T * 4)) ||
+      (rc = alloc((void **)&h->tree_mask_dev, T * 8)) ||
       (rc = alloc((void **)&h->seq_dev, int64_t(h->max_sessions) * sizeof(SeqInfo))))
     return rc;
   AttnParams ap = {};
@@ -667,7 +676,9 @@ void destroy_stage(sfc_stage *h) {
   for (void *p : {(void *)h->resid, (void *)h->resid2, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
-                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemm_scratch, (void *)h->act2, h->kv_arena, h->weight_arena})
+                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
+                  (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores,
+                  h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
   h->ring.destroy();
   if (h->ev0) cudaEventDestroy(h->ev0);
@@ -742,13 +753,15 @@ GemvSeg seg_of(const DevTensor *w, const DevTensor *w2, float *y, int64_t ldy) {
 // per sequence) use the single fused decode kernel; other batches the two-kernel path.
 cudaError_t layer_attention(sfc_stage *h, const AttnParams &ap, const KVLayer &kv, int64_t T, int64_t max_keys,
                             bool decode, cudaStream_t st) {
-  if (decode && decode_attention_supported(ap))
+  if (decode && !h->tree_active && decode_attention_supported(ap))
     return decode_attention(h->q, h->k, h->v, h->q_dim, h->k_dim, h->att, kv, h->seq_dev, T, max_keys, ap,
                             h->scratch, h->attn_scratch, h->attn_counters, st);
-  cudaError_t e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev, T, ap, st);
+  const bool tr = h->tree_active;
+  cudaError_t e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev,
+                           tr ? h->tree_rope_dev : nullptr, T, ap, st);
   if (e) return e;
-  return attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, nullptr, nullptr, T, max_keys, ap, h->scratch,
-                   h->attn_scratch, st);
+  return attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, tr ? h->tree_limit_dev : nullptr,
+                   tr ? h->tree_mask_dev : nullptr, T, max_keys, ap, h->scratch, h->attn_scratch, st);
 }
 
 // Fused layer loop for K-quant stages: the residual add + RMSNorm that precede the q/k/v and
@@ -1288,6 +1301,126 @@ int sfc_verify_greedy(sfc_stage *h, const float *hidden, const uint32_t *drafts,
   while (acc < k && uint32_t(am[size_t(acc)]) == drafts[acc]) ++acc;
   *accepted = acc;
   *bonus = uint32_t(am[size_t(acc)]);
+  return SFC_OK;
+}
+
+int sfc_forward_tree(sfc_stage *h, const char *request_id, const uint32_t *ids, const float *in_hidden,
+                     const int32_t *parent, int64_t n, float *out_hidden) {
+  clear_error();
+  SFC_REQUIRE(h && request_id && parent && out_hidden, "null argument");
+  SFC_REQUIRE(h->is_head ? ids != nullptr : in_hidden != nullptr,
+              h->is_head ? "head stage needs token ids" : "non-head stage needs hidden rows");
+  SFC_REQUIRE(n >= 1 && n <= 64 && n <= h->max_batch, "tree of %lld nodes (1..64 and <= max_batch_tokens)",
+              (long long)n);
+  SFC_REQUIRE(parent[0] == -1, "node 0 must be the root (parent -1)");
+  auto it = h->sessions.find(request_id);
+  SFC_REQUIRE(it != h->sessions.end(), "unknown session %s", request_id);
+  Session *s = &it->second;
+  SFC_REQUIRE(s->len + n <= h->max_ctx, "session needs %lld positions but max_ctx is %d", (long long)(s->len + n),
+              h->max_ctx);
+  std::vector<int32_t> rope(static_cast<size_t>(n)), limit(static_cast<size_t>(n));
+  std::vector<uint64_t> mask(static_cast<size_t>(n));
+  std::vector<int32_t> depth(static_cast<size_t>(n), 0);
+  for (int64_t i = 0; i < n; ++i) {
+    if (i > 0) {
+      SFC_REQUIRE(parent[i] >= 0 && parent[i] < i, "parent[%lld] = %d must precede its node", (long long)i,
+                  parent[i]);
+      depth[size_t(i)] = depth[size_t(parent[i])] + 1;
+      mask[size_t(i)] = mask[size_t(parent[i])];
+    }
+    mask[size_t(i)] |= 1ull << i;  // ancestors and the node itself
+    rope[size_t(i)] = int32_t(s->len + depth[size_t(i)]);
+    limit[size_t(i)] = int32_t(s->len + i + 1);
+  }
+  SFC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = h->stream;
+  SFC_CUDA(cudaMemcpyAsync(h->tree_rope_dev, rope.data(), size_t(n) * 4, cudaMemcpyHostToDevice, st));
+  SFC_CUDA(cudaMemcpyAsync(h->tree_limit_dev, limit.data(), size_t(n) * 4, cudaMemcpyHostToDevice, st));
+  SFC_CUDA(cudaMemcpyAsync(h->tree_mask_dev, mask.data(), size_t(n) * 8, cudaMemcpyHostToDevice, st));
+  if (!h->is_head)
+    SFC_CUDA(cudaMemcpyAsync(h->hn, in_hidden, size_t(n) * h->hidden * 4, cudaMemcpyHostToDevice, st));
+  const int64_t len0 = s->len;
+  h->tree_active = true;
+  int rc = forward_chunk(h, {SeqReq{s, int32_t(n)}}, ids, false, h->hn, st);
+  h->tree_active = false;
+  s->len = len0;  // tentative: sfc_commit_tree keeps the accepted path
+  if (rc) return rc;
+  SFC_CUDA(cudaMemcpyAsync(out_hidden, h->resid, size_t(n) * h->hidden * 4, cudaMemcpyDeviceToHost, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  return SFC_OK;
+}
+
+int sfc_sample_tree(sfc_stage *h, const float *hidden, const int32_t *parent, const uint32_t *node_tokens, int64_t n,
+                    float temperature, uint64_t seed, int32_t *path, int64_t *n_path, uint32_t *next_token) {
+  clear_error();
+  SFC_REQUIRE(h && hidden && parent && node_tokens && path && n_path && next_token, "null argument");
+  SFC_REQUIRE(h->is_tail, "Only the tail stage may sample");
+  SFC_REQUIRE(n >= 1 && n <= 64 && n <= h->max_batch, "tree of %lld nodes (1..64 and <= max_batch_tokens)",
+              (long long)n);
+  SFC_REQUIRE(parent[0] == -1, "node 0 must be the root (parent -1)");
+  for (int64_t i = 1; i < n; ++i)
+    SFC_REQUIRE(parent[i] >= 0 && parent[i] < i, "parent[%lld] = %d must precede its node", (long long)i, parent[i]);
+  SFC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = h->stream;
+  if (h->tree_scores_rows < n) {
+    if (h->tree_scores) cudaFree(h->tree_scores);
+    h->tree_scores = nullptr;
+    h->tree_scores_rows = 0;
+    SFC_CUDA(cudaMalloc(&h->tree_scores, size_t(64) * h->vocab * 4));
+    h->tree_scores_rows = 64;
+  }
+  SFC_CUDA(cudaMemcpyAsync(h->proj, hidden, size_t(n) * h->hidden * 4, cudaMemcpyHostToDevice, st));
+  if (h->output_norm)
+    SFC_CUDA(rms_norm(h->proj, F32P(h->output_norm), n, h->hidden, h->eps, h->hn, st));
+  else
+    SFC_CUDA(cudaMemcpyAsync(h->hn, h->proj, size_t(n) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
+  SFC_CUDA(logits_argmax(h->logits_w->type, h->logits_w->dev, h->vocab, h->hidden, h->hn, n, h->softcap,
+                         h->tree_scores, h->tok_dev, h->score_dev, h->scratch, std::max(h->attn_scratch, h->logit_scratch),
+                         st));
+  if (temperature > 0.f)
+    SFC_CUDA(sample_rows_temperature(h->tree_scores, n, h->vocab, temperature, seed, h->tok_dev, st));
+  std::vector<int64_t> drawn(static_cast<size_t>(n));
+  SFC_CUDA(cudaMemcpyAsync(drawn.data(), h->tok_dev, size_t(n) * 8, cudaMemcpyDeviceToHost, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  // walk from the root: the token drawn at a node is accepted if a child carries it (the first
+  // such child in node order); the token drawn where the walk stops is the next token
+  int64_t m = 0, cur = 0;
+  path[m++] = 0;
+  for (;;) {
+    int64_t nxt = -1;
+    for (int64_t c = cur + 1; c < n; ++c)
+      if (parent[c] == cur && node_tokens[c] == uint32_t(drawn[size_t(cur)])) {
+        nxt = c;
+        break;
+      }
+    if (nxt < 0) break;
+    path[m++] = int32_t(nxt);
+    cur = nxt;
+  }
+  *n_path = m;
+  *next_token = uint32_t(drawn[size_t(cur)]);
+  return SFC_OK;
+}
+
+int sfc_commit_tree(sfc_stage *h, const char *request_id, const int32_t *path, int64_t n_path) {
+  clear_error();
+  SFC_REQUIRE(h && request_id && path, "null argument");
+  auto it = h->sessions.find(request_id);
+  SFC_REQUIRE(it != h->sessions.end(), "unknown session %s", request_id);
+  Session *s = &it->second;
+  SFC_REQUIRE(n_path >= 1 && n_path <= 64 && path[0] == 0, "path must start at the root and hold 1..64 nodes");
+  for (int64_t i = 1; i < n_path; ++i)
+    SFC_REQUIRE(path[i] > path[i - 1], "path nodes must increase");
+  SFC_REQUIRE(s->len + path[n_path - 1] < h->max_ctx, "path leaves the cache");
+  SFC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = h->stream;
+  if (h->kv_arena && !h->layers.empty()) {
+    SFC_CUDA(cudaMemcpyAsync(h->tree_path_dev, path, size_t(n_path) * 4, cudaMemcpyHostToDevice, st));
+    SFC_CUDA(kv_compact(h->kv_arena, int(h->layers.size()), h->max_sessions, h->kv_slot_stride, s->slot, h->n_kv,
+                        h->max_ctx, h->head_dim, h->kv_f32 ? 4 : 2, int(s->len), h->tree_path_dev, int(n_path), st));
+    SFC_CUDA(cudaStreamSynchronize(st));
+  }
+  s->len += n_path;
   return SFC_OK;
 }
 

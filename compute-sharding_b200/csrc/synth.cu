@@ -19,13 +19,6 @@
 
 namespace sfc {
 
-__host__ __device__ __forceinline__ uint64_t mix64(uint64_t key, uint64_t ctr) {
-  uint64_t z = key + (ctr + 1) * 0x9E3779B97F4A7C15ull;
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
 uint64_t mix64_host(uint64_t key, uint64_t ctr) { return mix64(key, ctr); }
 
 uint64_t tensor_key(uint64_t seed, const char *name) {

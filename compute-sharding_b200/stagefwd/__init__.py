@@ -92,6 +92,10 @@ _sig("sfc_sample_tail", _I, _P, _P, _I64, ctypes.POINTER(_U32), ctypes.POINTER(_
 _sig("sfc_forward_dev", _I, _P, ctypes.POINTER(ctypes.c_char_p), _P, _I, _P, _P, _P, _I, _P)
 _sig("sfc_sample_dev", _I, _P, _P, _I64, _P, _P, _P)
 _sig("sfc_verify_greedy", _I, _P, _P, _P, _I64, ctypes.POINTER(_I64), ctypes.POINTER(_U32))
+_sig("sfc_sample_temperature", _I, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64, _P, _P)
+_sig("sfc_forward_tree", _I, _P, ctypes.c_char_p, _P, _P, _P, ctypes.c_int64, _P)
+_sig("sfc_sample_tree", _I, _P, _P, _P, _P, ctypes.c_int64, ctypes.c_float, ctypes.c_uint64, _P, _P, _P)
+_sig("sfc_commit_tree", _I, _P, ctypes.c_char_p, _P, ctypes.c_int64)
 _sig("sfc_clear_decode_session", _I, _P, ctypes.c_char_p)
 _sig("sfc_rollback_kv", _I, _P, ctypes.c_char_p, _I64)
 _sig("sfc_session_len", _I64, _P, ctypes.c_char_p)
@@ -197,6 +201,16 @@ def logits_argmax(ggml_type: int, w_dev, vocab: int, dim: int, h, cap: float = 3
     _check(_lib.sfc_logits_argmax(ggml_type, _ptr(w_dev), vocab, dim, _ptr(h), n_tok, cap, _ptr(allsc), _ptr(idx),
                                   _ptr(sc), _stream(stream)), "sfc_logits_argmax")
     return idx, sc, allsc
+
+
+def sample_temperature(scores, temperature: float, seed: int, stream=None):
+    """Seeded temperature sampling of each row of scores [n][vocab] (sfc_sample_temperature)."""
+    import torch
+    scores = scores.contiguous()
+    out = torch.empty(scores.shape[0], dtype=torch.int64, device=scores.device)
+    _check(_lib.sfc_sample_temperature(_ptr(scores), scores.shape[0], scores.shape[1], float(temperature), int(seed),
+                                       _ptr(out), _stream(stream)), "sfc_sample_temperature")
+    return out
 
 
 def synth_tensor(ggml_type: int, seed: int, name: str, rows: int, in_dim: int, sigma: float, mean: float = 0.0,
@@ -318,6 +332,39 @@ class CudaStageBackend:
         _check(_lib.sfc_verify_greedy(self.h, hidden.ctypes.data, drafts.ctypes.data, drafts.shape[0],
                                       ctypes.byref(acc), ctypes.byref(bonus)), "verify_greedy")
         return int(acc.value), int(bonus.value)
+
+    def forward_tree(self, request_id: str, parent, ids=None, hidden=None) -> np.ndarray:
+        """Tree-masked forward of draft-tree nodes after the session's cache (sfc_forward_tree)."""
+        parent = np.ascontiguousarray(parent, dtype=np.int32)
+        n = parent.shape[0]
+        out = np.empty((n, self.hidden_dim), np.float32)
+        idp = hp = None
+        if ids is not None:
+            ids = np.ascontiguousarray(ids, dtype=np.uint32)
+            idp = ids.ctypes.data
+        if hidden is not None:
+            hidden = np.ascontiguousarray(np.atleast_2d(hidden), dtype=np.float32)
+            hp = hidden.ctypes.data
+        _check(_lib.sfc_forward_tree(self.h, request_id.encode(), idp, hp, parent.ctypes.data, n, out.ctypes.data),
+               "forward_tree")
+        return out
+
+    def sample_tree(self, hidden, parent, node_tokens, temperature: float = 0.0, seed: int = 0):
+        """Acceptance walk over a verified tree (sfc_sample_tree): (path, next_token)."""
+        hidden = np.ascontiguousarray(np.atleast_2d(hidden), dtype=np.float32)
+        parent = np.ascontiguousarray(parent, dtype=np.int32)
+        node_tokens = np.ascontiguousarray(node_tokens, dtype=np.uint32)
+        n = parent.shape[0]
+        path = np.empty(n, np.int32)
+        npath, nxt = _I64(0), _U32(0)
+        _check(_lib.sfc_sample_tree(self.h, hidden.ctypes.data, parent.ctypes.data, node_tokens.ctypes.data, n,
+                                    float(temperature), int(seed), path.ctypes.data, ctypes.byref(npath),
+                                    ctypes.byref(nxt)), "sample_tree")
+        return path[: npath.value].copy(), int(nxt.value)
+
+    def commit_tree(self, request_id: str, path):
+        path = np.ascontiguousarray(path, dtype=np.int32)
+        _check(_lib.sfc_commit_tree(self.h, request_id.encode(), path.ctypes.data, path.shape[0]), "commit_tree")
 
     def forward_dev(self, request_ids, seq_tokens, ids_dev=None, in_dev=None, out_dev=None, append=True,
                     stream=None):

@@ -90,6 +90,13 @@ int sfc_logits_argmax(int ggml_type, const void *w_dev, int64_t vocab, int64_t d
                       int64_t n_tok, float cap, float *all_scores_dev, int64_t *argmax_dev, float *score_dev,
                       void *stream);
 
+/* Seeded temperature sampling of n rows of scores [n][vocab] (e.g. the softcapped logits written
+ * by sfc_logits_argmax): row r draws from softmax(scores / temperature) with the uniform
+ * (mix64(seed, r) >> 40) * 2^-24, summing weights over 1024 contiguous vocabulary segments in index
+ * order.  No counterpart in the reference (it samples greedily); used by sfc_sample_tree. */
+int sfc_sample_temperature(const float *scores_dev, int64_t n, int64_t vocab, float temperature, uint64_t seed,
+                           int64_t *tokens_dev, void *stream);
+
 /* Same computation as sfc_logits_argmax, for callers that cannot allocate device memory (code
  * running under CUDA graph capture, processes whose device memory belongs to their own
  * allocator).  No counterpart in the reference.  It allocates nothing: its per-CTA partials live
@@ -183,6 +190,24 @@ int sfc_sample_dev(sfc_stage *h, const float *hidden_dev, int64_t n, int64_t *to
  * argmax at the first mismatch (or at k).  Returns accepted count and bonus token. */
 int sfc_verify_greedy(sfc_stage *h, const float *hidden, const uint32_t *drafts, int64_t k, int64_t *accepted,
                       uint32_t *bonus);
+
+/* Draft-tree verification, generalising verify_batch_at_tail's chain rule (lib.rs:2143-2185) to a
+ * tree.  Nodes 0..n-1 (n <= 64) in breadth-first order: node 0 is the last accepted token (the
+ * root, parent -1), parent[i] < i.  sfc_forward_tree runs the nodes after the session's cached
+ * positions (cache rows len .. len+n-1) with rotary position len + depth(i) and attention to
+ * the cache plus the node's ancestors only; the session length is left unchanged.  Head stages
+ * take token ids, other stages the previous stage's rows; out_hidden gets [n][H]. */
+int sfc_forward_tree(sfc_stage *h, const char *request_id, const uint32_t *ids, const float *in_hidden,
+                     const int32_t *parent, int64_t n, float *out_hidden);
+/* Tail: draws a token at every node (temperature <= 0: argmax of the softcapped logits; else a
+ * seeded sample of softmax(logits / temperature), one uniform per node from mix64(seed, node))
+ * and walks from the root while a child carries the drawn token.  path gets the node indices
+ * (starting with 0), n_path their count, next_token the token drawn where the walk stops. */
+int sfc_sample_tree(sfc_stage *h, const float *hidden, const int32_t *parent, const uint32_t *node_tokens, int64_t n,
+                    float temperature, uint64_t seed, int32_t *path, int64_t *n_path, uint32_t *next_token);
+/* Keeps the KV rows of the accepted path (len + path[i] -> len + i on every layer) and advances
+ * the session by n_path.  Call on every stage after sfc_sample_tree. */
+int sfc_commit_tree(sfc_stage *h, const char *request_id, const int32_t *path, int64_t n_path);
 
 /* Session management (real_forward.rs:294-317; rollback lib.rs:2236-2269). */
 int sfc_clear_decode_session(sfc_stage *h, const char *request_id);

@@ -500,3 +500,93 @@ class OracleStage:
         H = self.hidden
         vocab = dims[1] if dims[0] == H else dims[0]
         return logits_top_k(t, raw, vocab, H, h, top_k, self.softcap, want_all)
+
+
+# ---------------------------------------------------------------- draft-tree verification
+# No counterpart in the reference, which verifies a chain greedily
+# (crates/llama-stage-backend/src/lib.rs:2143-2185); these restate the library's tree rule and its
+# seeded temperature sampler so the GPU path has a CPU check.
+
+_M64 = (1 << 64) - 1
+
+
+def mix64(key: int, ctr: int) -> int:
+    """SplitMix64 finaliser of key + (ctr + 1) * golden ratio (the synthetic-weight hash)."""
+    z = (key + (ctr + 1) * 0x9E3779B97F4A7C15) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+def sampling_uniform(seed: int, row: int) -> np.float32:
+    """The per-row uniform in [0, 1): top 24 bits of mix64(seed, row), times 2^-24."""
+    return np.float32(mix64(seed, row) >> 40) * np.float32(1.0 / 16777216.0)
+
+
+def sample_temperature(scores: np.ndarray, temperature: float, seed: int, row: int, segments: int = 1024):
+    """Draw from softmax(scores / temperature) as the GPU sampler does: float32 weights
+    exp((s - max) * (1/T)) summed in index order over `segments` contiguous segments, segment
+    prefixes summed in order, target = u * total, and the owning segment walked from its prefix.
+    Returns the drawn index."""
+    s = np.asarray(scores, np.float32)
+    v = s.shape[0]
+    seg = (v + segments - 1) // segments
+    mx = np.float32(s.max())
+    inv_t = np.float32(1.0) / np.float32(temperature)
+    w = np.exp((s - mx) * inv_t).astype(np.float32)
+    seg_sums = np.zeros(segments, np.float32)
+    for j in range(segments):
+        acc = np.float32(0.0)
+        for x in w[j * seg:min((j + 1) * seg, v)]:
+            acc = np.float32(acc + x)
+        seg_sums[j] = acc
+    pre = np.zeros(segments, np.float32)
+    run = np.float32(0.0)
+    for j in range(segments):
+        pre[j] = run
+        run = np.float32(run + seg_sums[j])
+    target = np.float32(sampling_uniform(seed, row) * run)
+    pick = -1
+    for j in range(segments):
+        lo, hi = j * seg, min((j + 1) * seg, v)
+        if lo < hi and pre[j] <= target < np.float32(pre[j] + seg_sums[j]):
+            r = pre[j]
+            pick = hi - 1
+            for i in range(lo, hi):
+                r = np.float32(r + w[i])
+                if r > target:
+                    pick = i
+                    break
+            break
+    if pick < 0:
+        pick = v - 1
+    return pick
+
+
+def tree_walk(parent, node_tokens, drawn):
+    """From the root, move to the first child whose token equals the token drawn at the current
+    node; stop when none does.  Returns (path of node indices from 0, token drawn at the stop)."""
+    n = len(parent)
+    path, cur = [0], 0
+    while True:
+        nxt = next((c for c in range(cur + 1, n) if parent[c] == cur and node_tokens[c] == drawn[cur]), -1)
+        if nxt < 0:
+            return path, int(drawn[cur])
+        path.append(nxt)
+        cur = nxt
+
+
+def bfs_tree(branching, max_nodes: int):
+    """Parent array of a breadth-first tree with the given branching per level (root = node 0),
+    truncated to max_nodes."""
+    parent, frontier = [-1], [0]
+    for b in branching:
+        nxt = []
+        for p in frontier:
+            for _ in range(b):
+                if len(parent) >= max_nodes:
+                    return parent
+                parent.append(p)
+                nxt.append(len(parent) - 1)
+        frontier = nxt
+    return parent
