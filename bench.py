@@ -232,6 +232,28 @@ def run_single(args):
     e2e_s = time.perf_counter() - t0
     be.clear_decode_session("e2e")
 
+    # ---- speculative verify: 1024 cached positions, 16-node draft tree (branching 2-2-2-2, BFS,
+    # truncated), one tree-masked forward of the 42 layers + logits + acceptance walk (host API)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import stage_oracle as so
+    parent = np.array(so.bfs_tree([2, 2, 2, 2], 16), np.int32)
+    spec_res = {}
+    for label, temp in (("greedy", 0.0), ("t0.8", 0.8)):
+        times, accepted = [], []
+        for rep in range(max(args.warmup, 3) + 4):
+            be.fill_session_synthetic("verify", 1024, seed=7)
+            nodes = rng.integers(0, VOCAB, 16).astype(np.uint32)
+            t0 = time.perf_counter()
+            rows = be.forward_tree("verify", parent, ids=nodes)
+            path, _ = be.sample_tree(rows, parent, nodes, temperature=temp, seed=1000 + rep)
+            be.commit_tree("verify", path)
+            dt = time.perf_counter() - t0
+            if rep >= max(args.warmup, 3):
+                times.append(dt)
+                accepted.append(len(path) - 1)
+        spec_res[label] = {"ms_per_verify": 1e3 * statistics.median(times), "accepted_mean": float(np.mean(accepted))}
+    be.clear_decode_session("verify")
+
     # ---- bs64 batched decode, contexts 512..3584 (seeded), one token per sequence per step
     ctx = rng.integers(512, 3585, 64)
     names = [f"b{i}" for i in range(64)]
@@ -276,6 +298,10 @@ def run_single(args):
         "bs64": {"value": bs64_tps, "unit": "tokens/s", "steps": bsteps, "ms_per_step": bs64_s * 1e3 / bsteps,
                  "workload": "64 sequences, contexts uniform 512..3584 (seeded synthetic KV), 1 token each per step"},
         "gemv": {"value": roof["achieved"], "unit": "GB/s", "frac_of_hbm": roof["frac"]},
+        "spec_verify": dict(spec_res, workload="1024 cached positions, 16-node draft tree (2-2-2-2, BFS, truncated) "
+                                               "of random tokens: tree-masked forward of 42 layers, logits over "
+                                               "262144, acceptance walk (greedy / seeded T=0.8), KV compaction; "
+                                               "host buffers"),
         "e2e": {"value": args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 + HIDDEN * 4,
                 "d2h_bytes_per_step": HIDDEN * 4 + 8,
                 "path": "begin_token_ids + sample_tail through the C ABI with host buffers each token"},
