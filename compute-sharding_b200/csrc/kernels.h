@@ -129,6 +129,9 @@ cudaError_t kv_compact(void *kv_arena, int n_layers, int max_sessions, int64_t s
 // Temperature sampling of n rows of scores [n][vocab]: p ~ exp((s - max) / temperature), one
 // counter-based uniform per row (mix64(seed, row) >> 40, times 2^-24); contiguous vocabulary
 // segments of ceil(vocab / 1024) per thread, summed in index order, so the walk is reproducible.
+// Softcap in place and argmax (lowest index on ties) of raw score rows [n][vocab].
+cudaError_t scores_argmax(float *scores, int64_t n, int64_t vocab, float cap, int64_t *idx, float *score,
+                          cudaStream_t st);
 cudaError_t sample_rows_temperature(const float *scores, int64_t n, int64_t vocab, float temperature, uint64_t seed,
                                     int64_t *out, cudaStream_t st);
 // Tensor-core K-quant GEMM (qgemm.cu) for 8+ tokens.  The activation operand is prepared from

@@ -199,6 +199,63 @@ __global__ void logits_reduce_kernel(const float *__restrict__ part, int n_cta, 
   }
 }
 
+// Softcap and argmax of precomputed raw scores [n][vocab] (the tensor-core path of the logits for
+// many rows): one CTA per row, thread j scans a contiguous vocabulary segment in index order with
+// strict '>', segments merge keeping the lowest index on ties; capped scores are written back.
+constexpr int ARGMAX_THREADS = 1024;
+
+__global__ void __launch_bounds__(ARGMAX_THREADS) scores_argmax_kernel(float *__restrict__ scores, int64_t vocab,
+                                                                      float cap, int64_t *__restrict__ idx_out,
+                                                                      float *__restrict__ score_out) {
+  __shared__ float s_b[ARGMAX_THREADS / 32];
+  __shared__ int64_t s_i[ARGMAX_THREADS / 32];
+  pdl_wait();
+  pdl_launch_dependents();
+  float *row = scores + int64_t(blockIdx.x) * vocab;
+  const int64_t seg = (vocab + ARGMAX_THREADS - 1) / ARGMAX_THREADS;
+  const int64_t lo = int64_t(threadIdx.x) * seg, hi = lo + seg < vocab ? lo + seg : vocab;
+  float b = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int64_t i = lo; i < hi; ++i) {
+    const float v = softcap_score(row[i], cap);
+    row[i] = v;
+    if (v > b) {
+      b = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ob, oi, b, bi)) {
+      b = ob;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_b[threadIdx.x >> 5] = b;
+    s_i[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < ARGMAX_THREADS / 32; ++w)
+      if (better(s_b[w], s_i[w], b, bi)) {
+        b = s_b[w];
+        bi = s_i[w];
+      }
+    idx_out[blockIdx.x] = bi == INT64_MAX ? 0 : bi;
+    score_out[blockIdx.x] = b;
+  }
+}
+
+cudaError_t scores_argmax(float *scores, int64_t n, int64_t vocab, float cap, int64_t *idx, float *score,
+                          cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  return launch_pdl(scores_argmax_kernel, dim3(unsigned(n)), dim3(ARGMAX_THREADS), 0, st, scores, vocab, cap, idx,
+                    score);
+}
+
 static int logits_ctas() { return 2 * num_sms(); }
 
 size_t logits_scratch_bytes(int64_t n_tok) {

@@ -229,6 +229,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   const int kbeg = int(int64_t(nb) * blockIdx.z / gridDim.z);
   const int nbl = int(int64_t(nb) * (blockIdx.z + 1) / gridDim.z) - kbeg;
   const bool q6 = S.type == T_Q6_K;
+  const bool f16 = S.type == T_F16;  // fp16 weights (the tied embedding): A tiles come straight from TMA
   const int raw_bytes = q6 ? QG_M * 208 : QG_M * BLOCK_Q4_K;
   const int dbox = (2 * nb + 15) / 16 * 16;
   // A ring: 2 slots of 32 KB, one MMA step each: Q4_K two 64-element chunks, Q6_K one chunk as its
@@ -238,7 +239,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
 
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) {
-      mbar_init(&a_full[i], 8);
+      mbar_init(&a_full[i], f16 ? 1 : 8);
       mbar_init(&a_empty[i], 1);
       mbar_init(&bm_full[i], 1);
       mbar_init(&bm_empty[i], 4);
@@ -299,14 +300,30 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       mbar_arrive_expect_tx(d_full, uint32_t(QG_M * dbox));
       tma_load_2d(sD, &S.map[3], nb * 208, row0, d_full);
     }
-    for (int kb = 0; kb < nbl && kb < QG_RST; ++kb) issue_raw(kb);
+    if (!f16)
+      for (int kb = 0; kb < nbl && kb < QG_RST; ++kb) issue_raw(kb);
   }
   pdl_wait();
   pdl_launch_dependents();
 
   if (warp == 8) {
-    // ---------------- producer of the raw weight blocks
-    if (lane == 0) {
+    // ---------------- producer of the raw weight blocks (fp16 weights: of the A tiles themselves, in
+    // the 128-byte-swizzled layout the MMA reads, once the step's activation chunks have landed)
+    if (lane == 0 && f16) {
+      for (int kb = 0; kb < nbl; ++kb)
+        for (int st = 0; st < spb; ++st) {
+          const int gs = kb * spb + st, slot = gs & 1;
+          mbar_spin(&a_empty[slot], ((gs >> 1) & 1) ^ 1, a.err);
+          for (int h2 = 0; h2 < cps; ++h2) {
+            const int gcc = kb * QG_CPB + 2 * st + h2;
+            mbar_spin(&b_full[gcc & (BST - 1)], (gcc >> BLOG) & 1, a.err);
+          }
+          mbar_arrive_expect_tx(&a_full[slot], uint32_t(cps * QG_A_BYTES));
+          for (int h2 = 0; h2 < cps; ++h2)
+            tma_load_2d(sA + slot * QG_A_SLOT + h2 * QG_A_BYTES, &S.map[0], (kbeg + kb) * QK_K + (2 * st + h2) * QG_KC,
+                        row0, &a_full[slot]);
+        }
+    } else if (lane == 0) {
       for (int kb = QG_RST; kb < nbl; ++kb) {
         mbar_spin(&raw_empty[kb & 1], ((kb >> 1) & 1) ^ 1, a.err);
         issue_raw(kb);
@@ -375,16 +392,17 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
     auto epilogue = [&](int kb) {
       const int b = kb & 1, ph = (kb >> 1) & 1;
       mbar_wait_bounded(&bm_full[kb & 3], (kb >> 2) & 1, a.err);
-      warp_wait(&rm_full[b], ph, a.err);
+      if (!f16) warp_wait(&rm_full[b], ph, a.err);
       warp_wait(&acc_full[b], ph, a.err);
       tc_fence_after();
       const float *rm = sRm + (b * QG_M + r) * 10;
       const float *bm = sBm + (kb & 3) * QG_META * TN;
-      const float d = rm[0];
-      const float dmin = q6 ? 0.f : rm[1];
+      const float d = f16 ? 1.f : rm[0];
+      const bool mins = !q6 && !f16;
+      const float dmin = mins ? rm[1] : 0.f;
       float mj[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mj[j] = q6 ? 0.f : rm[2 + j];
+      for (int j = 0; j < 8; ++j) mj[j] = mins ? rm[2 + j] : 0.f;
       constexpr int G = TN < 16 ? TN : (TN >= 64 ? 8 : 16);
 #pragma unroll
       for (int t0 = 0; t0 < TN; t0 += G) {
@@ -411,7 +429,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
     };
 
     if (q6) mbar_wait_bounded(d_full, 0, a.err);
-    for (int kb = 0; kb < nbl; ++kb) {
+    if (f16 && epi)
+      for (int kb = 0; kb + 1 < nbl; ++kb) epilogue(kb);  // no dequant work: the epilogue only
+    for (int kb = 0; kb < (f16 ? 0 : nbl); ++kb) {
       const int rs = kb & 1, ph = (kb >> 1) & 1;
       mbar_wait_bounded(&raw_full[rs], ph, a.err);
       const uint8_t *raw = sRaw + rs * QG_RAW_BYTES;
@@ -747,6 +767,20 @@ static bool make_map(CUtensorMap *m, const void *base, int64_t row_bytes, int64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp16 rows [rows][K]: box 64 elements (128 B) x 128 rows, 128-byte swizzle, i.e. one A tile in
+// exactly the shared-memory layout the MMA descriptors describe
+static bool make_map_f16(CUtensorMap *m, const void *base, int64_t K, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(K * 2)};
+  const cuuint32_t box[2] = {cuuint32_t(QG_KC), cuuint32_t(QG_M)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct MapKey {
   const void *p;
   int type;
@@ -774,7 +808,9 @@ static bool weight_maps(int type, const void *w, int64_t rows, int64_t K, CUtens
     const int64_t rb = device_row_bytes(type, K);
     const int nb = int(K / QK_K);
     bool ok;
-    if (type == T_Q4_K) {
+    if (type == T_F16) {
+      ok = make_map_f16(&s.map[0], w, K, rows);
+    } else if (type == T_Q4_K) {
       ok = make_map(&s.map[0], w, rb, rows, BLOCK_Q4_K);
     } else {
       ok = make_map(&s.map[0], w, rb, rows, 128) && make_map(&s.map[1], w, rb, rows, 64) &&
@@ -843,7 +879,8 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ part, int nsplit,
 }
 
 bool qgemm_supported(int type, int64_t K) {
-  return (type == T_Q4_K || type == T_Q6_K) && K % QK_K == 0 && K / QK_K <= QG_MAX_NB && encode_fn() != nullptr;
+  return (type == T_Q4_K || type == T_Q6_K || type == T_F16) && K % QK_K == 0 && K / QK_K <= QG_MAX_NB &&
+         encode_fn() != nullptr;
 }
 
 template <int TN>
@@ -869,7 +906,8 @@ cudaError_t qgemm(const QGemmOut *outs, int nseg, int64_t K, const GemmPrologue 
   int tiles = 0;
   for (int i = 0; i < nseg; ++i) {
     const QGemmOut &o = outs[i];
-    if ((o.type != T_Q4_K && o.type != T_Q6_K) || !o.w || !o.y || o.rows <= 0) return cudaErrorInvalidValue;
+    if ((o.type != T_Q4_K && o.type != T_Q6_K && o.type != T_F16) || !o.w || !o.y || o.rows <= 0)
+      return cudaErrorInvalidValue;
     if (reinterpret_cast<uintptr_t>(o.w) % 16) return cudaErrorInvalidValue;
     QGemmSeg &s = a.seg[i];
     if (!weight_maps(o.type, o.w, o.rows, K, s.map)) return cudaErrorInvalidValue;

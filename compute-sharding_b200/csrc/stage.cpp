@@ -282,6 +282,8 @@ struct sfc_stage {
   bool tree_active = false;
   float *tree_scores = nullptr;
   int64_t tree_scores_rows = 0;
+  // tensor-core logits for 8+ rows (fp16 tied embedding): raw then capped scores of up to 64 rows
+  float *logit_scores = nullptr;
   size_t attn_scratch = 0, logit_scratch = 0;
   int64_t gen_capacity = 0;
   PinnedRing ring;
@@ -646,6 +648,9 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
         return rc;
       h->gemm_scratch_bytes = gb;
       h->gemm_ok = true;
+      if (h->is_tail && h->logits_w && h->logits_w->type == T_F16 && qgemm_supported(T_F16, H) &&
+          reinterpret_cast<uintptr_t>(h->logits_w->dev) % 16 == 0)
+        if ((rc = alloc((void **)&h->logit_scores, int64_t(64) * h->vocab * 4))) return rc;
     }
   }
   SFC_CUDA(cudaMemset(h->attn_counters, 0, size_t(T) * ap.n_kv * 4));
@@ -677,7 +682,7 @@ void destroy_stage(sfc_stage *h) {
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
                   (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
-                  (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores,
+                  (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores, (void *)h->logit_scores,
                   h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
   h->ring.destroy();
@@ -1030,9 +1035,36 @@ int forward_single(sfc_stage *h, const char *req, const uint32_t *ids_host, cons
 }
 
 // Tail: output_norm + logits argmax on `n` device rows.
+// Logits of rows [t0, t0+c) (c <= 64) on the tensor cores: output_norm runs in the GEMM's operand
+// preparation, the fp16 tied embedding is operand A, scores land in h->logit_scores and are then
+// capped in place with their argmax.
+int tail_logits_gemm(sfc_stage *h, const float *rows_dev, int64_t c, int64_t *tok_dev, float *score_dev,
+                     cudaStream_t st) {
+  GemmPrologue pro = {};
+  pro.mode = h->output_norm ? 1 : 0;
+  pro.x = rows_dev;
+  pro.a = rows_dev;
+  pro.w_next = F32P(h->output_norm);
+  pro.eps = h->eps;
+  const QGemmOut o = {T_F16, h->logits_w->dev, h->vocab, h->logit_scores, h->vocab};
+  SFC_CUDA(qgemm(&o, 1, h->hidden, pro, c, h->gemm_scratch, h->gemm_scratch_bytes, st));
+  SFC_CUDA(scores_argmax(h->logit_scores, c, h->vocab, h->softcap, tok_dev, score_dev, st));
+  return SFC_OK;
+}
+
+bool tail_gemm_eligible(sfc_stage *h, int64_t n) { return h->logit_scores && n >= QGEMM_MIN_TOKENS; }
+
 int sample_rows(sfc_stage *h, const float *rows_dev, int64_t n, int64_t *tok_dev, float *score_dev, cudaStream_t st) {
   SFC_REQUIRE(h->is_tail, "Only the tail stage may sample");
   SFC_REQUIRE(n > 0 && n <= h->max_batch, "sample rows %lld out of range", (long long)n);
+  if (tail_gemm_eligible(h, n)) {
+    for (int64_t t0 = 0; t0 < n; t0 += 64) {
+      const int64_t c = std::min<int64_t>(64, n - t0);
+      int rc = tail_logits_gemm(h, rows_dev + t0 * h->hidden, c, tok_dev + t0, score_dev + t0, st);
+      if (rc) return rc;
+    }
+    return SFC_OK;
+  }
   if (h->output_norm)
     SFC_CUDA(rms_norm(rows_dev, F32P(h->output_norm), n, h->hidden, h->eps, h->hn, st));
   else
@@ -1362,7 +1394,7 @@ int sfc_sample_tree(sfc_stage *h, const float *hidden, const int32_t *parent, co
     SFC_REQUIRE(parent[i] >= 0 && parent[i] < i, "parent[%lld] = %d must precede its node", (long long)i, parent[i]);
   SFC_CUDA(cudaSetDevice(h->device));
   cudaStream_t st = h->stream;
-  if (h->tree_scores_rows < n) {
+  if (!tail_gemm_eligible(h, n) && h->tree_scores_rows < n) {
     if (h->tree_scores) cudaFree(h->tree_scores);
     h->tree_scores = nullptr;
     h->tree_scores_rows = 0;
@@ -1370,15 +1402,21 @@ int sfc_sample_tree(sfc_stage *h, const float *hidden, const int32_t *parent, co
     h->tree_scores_rows = 64;
   }
   SFC_CUDA(cudaMemcpyAsync(h->proj, hidden, size_t(n) * h->hidden * 4, cudaMemcpyHostToDevice, st));
-  if (h->output_norm)
-    SFC_CUDA(rms_norm(h->proj, F32P(h->output_norm), n, h->hidden, h->eps, h->hn, st));
-  else
-    SFC_CUDA(cudaMemcpyAsync(h->hn, h->proj, size_t(n) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
-  SFC_CUDA(logits_argmax(h->logits_w->type, h->logits_w->dev, h->vocab, h->hidden, h->hn, n, h->softcap,
-                         h->tree_scores, h->tok_dev, h->score_dev, h->scratch, std::max(h->attn_scratch, h->logit_scratch),
-                         st));
-  if (temperature > 0.f)
-    SFC_CUDA(sample_rows_temperature(h->tree_scores, n, h->vocab, temperature, seed, h->tok_dev, st));
+  const float *capped = h->tree_scores;
+  if (tail_gemm_eligible(h, n)) {  // tensor-core logits: capped scores in h->logit_scores
+    int rc = tail_logits_gemm(h, h->proj, n, h->tok_dev, h->score_dev, st);
+    if (rc) return rc;
+    capped = h->logit_scores;
+  } else {
+    if (h->output_norm)
+      SFC_CUDA(rms_norm(h->proj, F32P(h->output_norm), n, h->hidden, h->eps, h->hn, st));
+    else
+      SFC_CUDA(cudaMemcpyAsync(h->hn, h->proj, size_t(n) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
+    SFC_CUDA(logits_argmax(h->logits_w->type, h->logits_w->dev, h->vocab, h->hidden, h->hn, n, h->softcap,
+                           h->tree_scores, h->tok_dev, h->score_dev, h->scratch,
+                           std::max(h->attn_scratch, h->logit_scratch), st));
+  }
+  if (temperature > 0.f) SFC_CUDA(sample_rows_temperature(capped, n, h->vocab, temperature, seed, h->tok_dev, st));
   std::vector<int64_t> drawn(static_cast<size_t>(n));
   SFC_CUDA(cudaMemcpyAsync(drawn.data(), h->tok_dev, size_t(n) * 8, cudaMemcpyDeviceToHost, st));
   SFC_CUDA(cudaStreamSynchronize(st));

@@ -196,3 +196,28 @@ def test_batched_decode_equals_full_rerun(sf, kv_f32):
     stage_close(out.cpu().numpy(), np.stack(full), kv_f32, "batched decode vs full rerun")
     assert all(g.session_len(f"inc{i}") == lens[i] + 1 for i in range(n_seq))
     g.close()
+
+
+def test_tail_logits_many_rows_match_single_rows(sf):
+    """Sampling 8+ rows at once takes the tensor-core logits (fp16 tied embedding as operand A,
+    output_norm in the operand preparation); it must pick the same tokens with the same capped
+    scores as the one-row path, and as the oracle."""
+    spec, shape = shape_pair(n_layers=1, vocab=8192)
+    g = gpu_stage(sf, shape, 0, 0, True, True)
+    o = oracle_stage(spec, 0, 0, True, True)
+    rows = so.synth_normal_f32(12, "tail.rows", 24 * shape.hidden).reshape(24, shape.hidden)
+    dev = torch.from_numpy(rows).cuda()
+    tk = torch.empty(24, dtype=torch.int64, device="cuda")
+    sc = torch.empty(24, dtype=torch.float32, device="cuda")
+    g.sample_dev(dev, tk, sc)
+    torch.cuda.synchronize()
+    for i in range(24):
+        t1 = torch.empty(1, dtype=torch.int64, device="cuda")
+        s1 = torch.empty(1, dtype=torch.float32, device="cuda")
+        g.sample_dev(dev[i:i + 1], t1, s1)
+        torch.cuda.synchronize()
+        assert int(tk[i]) == int(t1[0]), f"row {i}"
+        assert abs(float(sc[i]) - float(s1[0])) <= 1e-3 * max(1.0, abs(float(s1[0]))), f"row {i} score"
+        if i < 4:
+            assert int(tk[i]) == o.sample_tail(rows[i])[0]
+    g.close()
