@@ -161,6 +161,13 @@ template <int NREG>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[NREG]);
 
 template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
+template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -242,7 +249,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       mbar_init(&a_full[i], f16 ? 1 : 8);
       mbar_init(&a_empty[i], 1);
       mbar_init(&bm_full[i], 1);
-      mbar_init(&bm_empty[i], 4);
+      mbar_init(&bm_empty[i], 8);
     }
     for (int i = 0; i < BST; ++i) {
       mbar_init(&b_full[i], 1);
@@ -252,7 +259,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], 8);
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], 8);
       mbar_init(&rm_full[i], 4);
     }
     mbar_init(d_full, 1);
@@ -380,13 +387,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       }
     }
   } else {
-    // ---------------- warps 0-7: dequantise (thread = row r, half `part` of every chunk); warps
-    // 0-3 also run the epilogue of the previous block (thread = row r = TMEM lane r)
+    // ---------------- warps 0-7: dequantise (thread = row r, half `part` of every chunk) and run the
+    // epilogue of the previous block (thread = row r = TMEM lane r, tokens of half `part`)
     const int r = tid & (QG_M - 1), part = tid >> 7;
-    const bool epi = warp < 4;
-    float yacc[TN];
+    constexpr bool epi = true;
+    constexpr int TH = TN / 2;  // tokens per epilogue half
+    const int tb = part * TH;   // first token of this thread's half
+    float yacc[TH];
 #pragma unroll
-    for (int t = 0; t < TN; ++t) yacc[t] = 0.f;
+    for (int t = 0; t < TH; ++t) yacc[t] = 0.f;
     const uint32_t lane_base = tmem + (uint32_t(32 * (warp & 3)) << 16);
 
     auto epilogue = [&](int kb) {
@@ -403,21 +412,32 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       float mj[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) mj[j] = mins ? rm[2 + j] : 0.f;
-      constexpr int G = TN < 16 ? TN : (TN >= 64 ? 8 : 16);
+      constexpr int G = TH < 16 ? TH : 16;
 #pragma unroll
-      for (int t0 = 0; t0 < TN; t0 += G) {
+      for (int t0 = 0; t0 < TH; t0 += G) {
         uint32_t hi[G], lo[G];
-        tmem_ld<G>(lane_base + uint32_t(b * N + t0), hi);
-        tmem_ld<G>(lane_base + uint32_t(b * N + TN + t0), lo);
+        tmem_ld<G>(lane_base + uint32_t(b * N + tb + t0), hi);
+        tmem_ld<G>(lane_base + uint32_t(b * N + TN + tb + t0), lo);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < G; ++i) {
-          const int t = t0 + i;
-          const float v = __uint_as_float(hi[i]) + __uint_as_float(lo[i]);
-          float mn = 0.f;
+        for (int i = 0; i < G; i += 4) {
+          const int t = tb + t0 + i;  // four tokens: their scales and sub-block sums as 16-byte loads
+          const float4 s4 = *reinterpret_cast<const float4 *>(bm + t);
+          float4 mn = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) mn += mj[j] * bm[(1 + j) * TN + t];
-          yacc[t] += (d * bm[t]) * v - dmin * mn;
+          for (int j = 0; j < 8; ++j) {
+            const float4 q = *reinterpret_cast<const float4 *>(bm + (1 + j) * TN + t);
+            mn.x += mj[j] * q.x;
+            mn.y += mj[j] * q.y;
+            mn.z += mj[j] * q.z;
+            mn.w += mj[j] * q.w;
+          }
+          const float sv[4] = {s4.x, s4.y, s4.z, s4.w}, mv[4] = {mn.x, mn.y, mn.z, mn.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float v = __uint_as_float(hi[i + e]) + __uint_as_float(lo[i + e]);
+            yacc[t0 + i + e] += (d * sv[e]) * v - dmin * mv[e];
+          }
         }
       }
       tc_fence_before();
@@ -564,15 +584,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
     if (epi) {
       epilogue(nbl - 1);
       const int row = row0 + r;
-      const int tok0 = tt * TN;
+      const int tok0 = tt * TN + tb;
       if (a.part) {  // split-K partial of global row blockIdx.x*128 + r
         float *pp = a.part + (int64_t(blockIdx.z) * a.n_tok) * a.part_ld + int64_t(blockIdx.x) * QG_M + r;
 #pragma unroll
-        for (int t = 0; t < TN; ++t)
+        for (int t = 0; t < TH; ++t)
           if (tok0 + t < a.n_tok) pp[int64_t(tok0 + t) * a.part_ld] = yacc[t];
       } else if (row < S.rows) {
 #pragma unroll
-        for (int t = 0; t < TN; ++t)
+        for (int t = 0; t < TH; ++t)
           if (tok0 + t < a.n_tok) S.y[int64_t(tok0 + t) * S.ldy + row] = yacc[t];
       }
     }
