@@ -159,7 +159,8 @@ def gemv_roofline(sf, torch, hbm_peak):
     l2 = getattr(props, "L2_cache_size", 126 << 20)
     wbytes = 10240 * 10 * 144
     copies = int(np.ceil(2 * l2 / wbytes)) + 2
-    ws = [sf.synth_tensor(sf.Q4_K, 1, f"gemv.{i}", 10240, 2560, 0.02) for i in range(copies)]
+    ws = [sf.prepare_weights(sf.Q4_K, sf.synth_tensor(sf.Q4_K, 1, f"gemv.{i}", 10240, 2560, 0.02), 10240, 2560)
+          for i in range(copies)]
     x = torch.randn(1, 2560, device=dev)
     y = torch.empty(1, 10240, device=dev)
     lib = sf.lib

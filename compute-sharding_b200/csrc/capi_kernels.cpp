@@ -75,12 +75,12 @@ int64_t sfc_weight_device_bytes(int ggml_type, int64_t rows, int64_t in_dim) {
     set_error("unsupported ggml type %d", ggml_type);
     return SFC_E_INVALID;
   }
-  const int rb = device_row_bytes(ggml_type, in_dim);
-  if (rb < 0) {
+  const int64_t bytes = device_tensor_bytes(ggml_type, rows, in_dim);
+  if (bytes < 0) {
     set_error("in_dim %lld invalid for type %d", (long long)in_dim, ggml_type);
     return SFC_E_INVALID;
   }
-  return int64_t(rb) * rows;
+  return bytes;
 }
 
 int sfc_prepare_weights(int ggml_type, const void *gguf_dev, int64_t rows, int64_t in_dim, void *dst_dev,

@@ -17,6 +17,20 @@ constexpr int BLOCK_Q6_K = 210;
 
 enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_BF16 = 30 };
 
+// Device layout of K-quant weights (written by prepare_weights): rows in tiles of 16 (the last tile
+// zero-padded), one record per (tile, 256-element block), records tile-major (record index
+// tile * nb + block), so any tile's run of blocks is one contiguous byte range:
+//   Q4_K record, 2304 B:  hdr[16][16] (d, dmin, 12 packed scale bytes per row) | qs[16][128]
+//   Q6_K record, 3360 B:  ql[16][128] | qh[16][64] | sc[16][16] | d[16] (fp16)
+// Inside qs and ql the 16-byte chunk j of row r is stored at chunk j ^ (r & 7), inside qh at
+// j ^ ((r >> 1) & 3): the 8 rows that one warp reads at a time then hit distinct shared-memory banks.
+constexpr int KQ_TILE = 16;
+constexpr int REC_Q4_K = 2304;
+constexpr int REC_Q6_K = 3360;
+__host__ __device__ constexpr int kquant_rec_bytes(int type) {
+  return type == T_Q4_K ? REC_Q4_K : type == T_Q6_K ? REC_Q6_K : 0;
+}
+
 // Device-side error word: kernels whose bounded waits expire record a code here
 // instead of spinning forever; the host reads it after synchronising.
 enum DeviceError : unsigned { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1, DEV_BAD_ARG = 2 };

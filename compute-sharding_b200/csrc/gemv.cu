@@ -1,22 +1,29 @@
-// gemv.cu — dequant-fused K-quant GEMV for decode (1..4 tokens per pass).
+// gemv.cu — dequant-fused K-quant GEMV for decode (1 or 2 tokens per pass).
 //
 // Replaces the reference's row-dot hot loop (crates/stage-forward-lab/src/quants.rs:1801-1909
 // for Q4_K, :2594-2688 for Q6_K) driven by real_math.rs:398-733 (matmul_quantized_many_refs_range)
 // and the gate/up pair path real_math.rs:1584-1800 + GeGLU real_forward.rs:1716-1730.
 //
 // Design (B200):
-//  * Each CTA owns a contiguous slab of weight rows and streams it HBM -> shared memory with
-//    bulk async copies (the TMA engine, cp.async.bulk) into an mbarrier ring; all stages are
-//    requested up front so the whole slab is in flight at once.
-//  * Thread t owns one 32-element column slice (block b, 64-group j, half h) of every row and
-//    keeps its activations in registers for the whole kernel, so shared memory only carries
-//    weights.  Slices of one 256-block sit in 8 consecutive lanes (segment reduction by shuffle).
-//  * Activations are split exactly into three signed 8-bit digit planes per 256-block
-//    (x = 2^e (a*65536 + b*256 + c), |x| < 2^(e+22)), so nibble x digit products and their sums
-//    are exact int32 dp4a work; rounding happens only in the final fp32 combine.  This keeps
-//    the integer pipe, not the ALU pipe, as the compute path and stays within 2^-22 of x.
-//  * Q6_K weights use a per-row struct-of-arrays device layout (ql | qh | scales | d, row padded
-//    to 16 B) prepared once at load so every field is 16-byte aligned for vector smem loads.
+//  * Work unit = (16-row tile, 256-element block).  The units of all output rows (tile-major,
+//    block fastest) are split evenly over the CTAs, so every SM streams the same number of weight
+//    bytes whatever the row count.  A tile cut between two CTAs is finished by whichever of the
+//    two arrives second: both write their partial row sums to a small global buffer and the
+//    second sums them in a fixed order (deterministic).
+//  * Weights are in the tiled device layout (common.cuh): a stage = one tile's run of blocks is one
+//    contiguous range, so one producer warp streams it HBM -> shared memory with a single bulk
+//    async copy (cp.async.bulk, the TMA engine) per matrix into an mbarrier ring.  Weights never
+//    depend on the previous kernel, so the copies are issued before the dependency wait.
+//  * 15 consumer warps run the quant x activation products as exact integer MMAs on the tensor
+//    pipe (mma.sync m16n8k32, u8 x s8 -> s32): A = 16 rows x 32 quants of one sub-block, B = the
+//    activation split exactly into three signed 8-bit digit planes per 256-block,
+//    x = 2^e (a*65536 + b*256 + c) with |x| < 2^(e+22), one plane per MMA column.  Sub-block
+//    scales multiply the exact int32 results; rounding happens only in the final fp32 combine
+//    (more accurate than the reference's fp32 running sum, and not the lossy 8-bit activation
+//    quantization of the reference's GPU path, quantize_q8_1).
+//  * Q6_K: one MMA covers a 32-quant chunk with its two 16-element scale groups in separate
+//    columns (group-0 digit planes in columns 0-2, group-1 in 3-5), and the accumulator input
+//    carries -32 x (digit sums), so the MMA returns the exact sum of (q - 32) x digits.
 #include <cuda_runtime.h>
 #include <stdio.h>
 
@@ -25,34 +32,24 @@
 
 namespace sfc {
 
-// Threads per CTA: 1-token launches use 512 threads (16 warps, <= 128 registers each), 2-token
-// launches 320 (up to 204 registers for the per-token activation planes).
-template <int T>
-struct GemvCfg {
-  static constexpr int THREADS = T == 1 ? 512 : 320;
-};
-constexpr int GEMV_MAX_THREADS = 512;
+constexpr int GEMV_TILE = 16;       // weight rows per MMA tile
+constexpr int GEMV_CONSUMERS = 15;  // consumer warps per CTA (plus one producer warp: 512 threads)
+constexpr int GEMV_THREADS = (GEMV_CONSUMERS + 1) * 32;
 constexpr int GEMV_MAX_T = 2;
-constexpr int SLICES_PER_BLOCK = 4;
+constexpr int GEMV_MAX_STAGES = 12;
+constexpr int GEMV_MAX_SEG = 3;
+// floats of one CTA-boundary slot: two sides x 16 rows x (2 matrices x 2 tokens)
+constexpr int GEMV_SPLIT_SLOT = 2 * GEMV_TILE * 2 * GEMV_MAX_T;
+constexpr int GEMV_DEFAULT_SPLIT_CTAS = 1024;
 
 __device__ unsigned g_device_error = 0;
 long long g_kernel_launches = 0;
+// Boundary buffers for callers that pass none.  The counters start at zero and every launch
+// leaves them at zero (the second arrival resets its slot).
+__device__ unsigned g_gemv_cnt[GEMV_DEFAULT_SPLIT_CTAS];
+__device__ float g_gemv_part[GEMV_DEFAULT_SPLIT_CTAS * GEMV_SPLIT_SLOT];
 
-// ---------------------------------------------------------------- activations
-// Per-thread view of the activation slice for one token: digit planes for the two 32-element
-// halves (A = elements j*64+[0,32), B = A+32) of block `blk`, the block scale 2^e, and sums of
-// the quantized values per 32 (Q4_K mins) and per 16 elements (Q6_K offset of 32).
-struct XSlice {
-  uint32_t p[3][2][8];  // [plane a,b,c][half][word] 4 signed digits per word
-  float scale;
-  float sum32[2];
-  float sum16[4];
-};
-
-// Shared-memory record of one 64-element slice: the XSlice fields in order, padded to 60 words
-// so that consecutive records start 28 banks apart (conflict-free 16-byte loads).
-constexpr int XREC_WORDS = 60;
-
+// ---------------------------------------------------------------- small helpers
 __device__ __forceinline__ void load8(const float *p, int64_t off, float (&v)[8]) {
   const float4 f0 = *reinterpret_cast<const float4 *>(p + off);
   const float4 f1 = *reinterpret_cast<const float4 *>(p + off + 4);
@@ -65,9 +62,94 @@ __device__ __forceinline__ void store8(float *p, const float (&v)[8]) {
   *reinterpret_cast<float4 *>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-// Exact digit planes of one 256-element block held by a warp (lane l: elements 8l..8l+7); the
-// lane writes its part of the record of slice l/8 (half (l/4)&1, plane words 2(l&3), +1).
-__device__ __forceinline__ void quantize8(const float (&v)[8], int lane, uint32_t *rec) {
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t b) {  // (a & mask) | b
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(b));
+  return r;
+}
+
+// Byte permute against zero: selector 0x4440 | b zero-extends byte b; sext_sel(b) sign-extends it.
+__device__ __forceinline__ int prmt0(uint32_t a, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(a), "r"(sel));
+  return int(r);
+}
+__host__ __device__ constexpr uint32_t sext_sel(uint32_t b) {
+  return b | ((8u | b) << 4) | ((8u | b) << 8) | ((8u | b) << 12);
+}
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int r;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+// D = A (16 x 32 u8, row) * B (32 x 8 s8, col) + C, exact int32.  Fragment layout (lane = 4g + t):
+// a0/a2 = row g, k 4t..4t+3 / 16+4t..; a1/a3 = row g+8; b0/b1 = column g, k 4t.. / 16+4t..;
+// d0,d1 = row g, columns 2t, 2t+1; d2,d3 = row g+8.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1, int c0, int c1, int c2, int c3) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Barrier of the consumer warps only (the producer warp never joins).
+__device__ __forceinline__ void consumer_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(GEMV_CONSUMERS * 32) : "memory");
+}
+
+__device__ __forceinline__ float gelu_tanh_mul(float v, float u) {
+  // real_math.rs:79-85
+  const float k = 0.7978845608028654f;
+  const float inner = k * (v + 0.044715f * v * v * v);
+  return 0.5f * v * (1.0f + tanhf(inner)) * u;
+}
+
+// ---------------------------------------------------------------- activation fragments
+// Shared-memory image of the activations of all T tokens, built once per CTA:
+//  frag  [nb][4 chunk pairs][3T columns][4 t][4 words]  digit words in MMA B-fragment order:
+//        word k of (block b, pair cp, column P = 3*token + plane, t) holds the digits of elements
+//        32c + 4t + [0,4) (k even) or 32c + 16 + 4t + [0,4) (k odd), c = 2cp + k/2
+//  scale [nb][T]         2^-e of the block
+//  sum32 [nb][T][8]      sum of x over each 32-element sub-block (Q4_K mins)
+//  q6c   [nb][T][4 t][8 chunks][2]  Q6_K accumulator inputs of the two columns 2t, 2t+1 a lane
+//        holds: -32 x (digit sum of plane n%3 over 16-element group 2c + n/3), 0 for n >= 6
+struct XSmem {
+  uint32_t *frag;
+  float *scale;
+  float *sum32;
+  int *q6c;
+};
+
+__host__ __device__ inline int gemv_x_bytes(int nb, int T) {
+  const int scale_b = (nb * T * 4 + 15) / 16 * 16;
+  return nb * 768 * T + scale_b + nb * T * 32 + nb * T * 256;
+}
+
+__device__ __forceinline__ XSmem x_view(uint8_t *base, int nb, int T) {
+  XSmem x;
+  x.frag = reinterpret_cast<uint32_t *>(base);
+  uint8_t *p = base + nb * 768 * T;
+  x.scale = reinterpret_cast<float *>(p);
+  p += (nb * T * 4 + 15) / 16 * 16;
+  x.sum32 = reinterpret_cast<float *>(p);
+  p += nb * T * 32;
+  x.q6c = reinterpret_cast<int *>(p);
+  return x;
+}
+
+// Exact digit planes of one 256-element block held by a warp (lane l: elements 8l..8l+7).
+template <int T>
+__device__ __forceinline__ void emit_block(const float (&v)[8], int lane, int b, int tok, const XSmem &X) {
+  constexpr int NP = 3 * T;
   float m = 0.f;
 #pragma unroll
   for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(v[e]));
@@ -92,274 +174,460 @@ __device__ __forceinline__ void quantize8(const float (&v)[8], int lane, uint32_
     Y[e] = __float_as_uint(fmaf(v[e], pw, kRound)) - kBias;
     ys += Y[e];
   }
-  uint32_t wc[2], wb[2], wa[2];
+  uint32_t planes[3][2];  // [a, b, c][elements 8l..8l+3, 8l+4..8l+7]
 #pragma unroll
   for (int w = 0; w < 2; ++w) {
     const uint32_t lo01 = __byte_perm(Y[4 * w], Y[4 * w + 1], 0x5140);  // [Y0.b0, Y1.b0, Y0.b1, Y1.b1]
     const uint32_t lo23 = __byte_perm(Y[4 * w + 2], Y[4 * w + 3], 0x5140);
     const uint32_t hi01 = __byte_perm(Y[4 * w], Y[4 * w + 1], 0x7362);  // [Y0.b2, Y1.b2, Y0.b3, Y1.b3]
     const uint32_t hi23 = __byte_perm(Y[4 * w + 2], Y[4 * w + 3], 0x7362);
-    wc[w] = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;  // c: bytes 0
-    wb[w] = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;  // b: bytes 1
-    wa[w] = __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u;  // a: bytes 2
+    planes[2][w] = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;  // c: bytes 0
+    planes[1][w] = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;  // b: bytes 1
+    planes[0][w] = __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u;  // a: bytes 2
   }
-  const int h = (lane >> 2) & 1, q = lane & 3;
-  uint32_t *pw0 = rec + h * 8 + 2 * q;
-  *reinterpret_cast<uint2 *>(pw0) = make_uint2(wa[0], wa[1]);
-  *reinterpret_cast<uint2 *>(pw0 + 16) = make_uint2(wb[0], wb[1]);
-  *reinterpret_cast<uint2 *>(pw0 + 32) = make_uint2(wc[0], wc[1]);
-  // sum of X over 16 (32) elements = sum of Y - 16 (32) * 0x808080, exact in 32-bit arithmetic
+  // lane l = 4c + q holds elements 32c + 8q + [0, 8): words t = 2(q&1), 2(q&1)+1 of half q>>1
+  const int c = lane >> 2, q = lane & 3, t0 = 2 * (q & 1), k = (c & 1) * 2 + (q >> 1);
+#pragma unroll
+  for (int p = 0; p < 3; ++p) {
+    uint32_t *dst = X.frag + (((b * 4 + (c >> 1)) * NP + tok * 3 + p) * 4 + t0) * 4 + k;
+    dst[0] = planes[p][0];
+    dst[4] = planes[p][1];
+  }
+  // sum of X over 32 elements = sum of Y - 32 * 0x808080, exact in 32-bit arithmetic
   const uint32_t y16 = ys + __shfl_xor_sync(0xFFFFFFFFu, ys, 1);
   const uint32_t y32 = y16 + __shfl_xor_sync(0xFFFFFFFFu, y16, 2);
-  if ((q & 1) == 0) rec[51 + 2 * h + (q >> 1)] = __float_as_uint(float(int(y16 - 16u * 0x808080u)) * scale);
-  if (q == 0) rec[49 + h] = __float_as_uint(float(int(y32 - 32u * 0x808080u)) * scale);
-  if ((lane & 7) == 0) rec[48] = __float_as_uint(scale);
-}
-
-__device__ __forceinline__ void load_slice(const uint32_t *rec, XSlice &xs) {
+  if (q == 0) X.sum32[(b * T + tok) * 8 + c] = float(int(y32 - 32u * 0x808080u)) * scale;
+  if (lane == 0) X.scale[b * T + tok] = scale;
+  // Q6_K accumulator inputs: lanes 4c + {0,1} hold group 2c, lanes 4c + {2,3} group 2c + 1
+  int *q6 = X.q6c + (b * T + tok) * 64;
 #pragma unroll
-  for (int i = 0; i < 12; ++i) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(rec + 4 * i);
-    uint32_t *dst = &xs.p[0][0][0] + 4 * i;
-    dst[0] = w.x; dst[1] = w.y; dst[2] = w.z; dst[3] = w.w;
+  for (int p = 0; p < 3; ++p) {
+    int s = dp4a_ss(planes[p][1], 0x01010101u, dp4a_ss(planes[p][0], 0x01010101u, 0));
+    s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
+    const int n = (q >> 1) * 3 + p;  // column (group parity, plane)
+    if ((q & 1) == 0) q6[(n >> 1) * 16 + c * 2 + (n & 1)] = -32 * s;
   }
-  const uint4 u0 = *reinterpret_cast<const uint4 *>(rec + 48), u1 = *reinterpret_cast<const uint4 *>(rec + 52);
-  xs.scale = __uint_as_float(u0.x);
-  xs.sum32[0] = __uint_as_float(u0.y);
-  xs.sum32[1] = __uint_as_float(u0.z);
-  xs.sum16[0] = __uint_as_float(u0.w);
-  xs.sum16[1] = __uint_as_float(u1.x);
-  xs.sum16[2] = __uint_as_float(u1.y);
-  xs.sum16[3] = __uint_as_float(u1.z);
+  if (q == 0) {
+    q6[3 * 16 + c * 2] = 0;
+    q6[3 * 16 + c * 2 + 1] = 0;
+  }
 }
 
-__device__ __forceinline__ int dot16(const uint32_t *wq, const uint32_t *xp) {
-  int s = 0;
+// ---------------------------------------------------------------- MMA units
+// Per-lane output columns n = 2t, 2t+1: plane weight (65536, 256, 1; 0 when unused) and token.
+__device__ __forceinline__ float plane_weight(int n, int ncols) {
+  if (n >= ncols) return 0.f;
+  const int p = n % 3;
+  return p == 0 ? 65536.0f : (p == 1 ? 256.0f : 1.0f);
+}
+
+// Q4_K (tiled records; matrix m's records of the stage at `stage + m * mstride`): this lane's share
+// of rows g and g+8 for block b (record lb of the stage), v[m][row][token], summed over the four t
+// lanes by the caller.  Chunk c = sub-block c; even sub-blocks are the low nibbles of bytes
+// 32(c/2) + [0,32), odd ones the high nibbles (quants.rs:181-208).  High nibbles stay in place
+// (16 q) and the low-nibble sums are scaled by 16 to match, so d/16 is applied at the end.
+template <int NMAT, int T>
+__device__ __forceinline__ void unit_q4k(const uint8_t *__restrict__ stage, int mstride, int lb, int b,
+                                         const XSmem &X, int g, int t, float (&v)[NMAT][2][T]) {
+  constexpr int NP = 3 * T;
+  const uint32_t keep = g < NP ? 0xFFFFFFFFu : 0u;
+  const int P = g < NP ? g : 0;
+  uint32_t bf[8][2];
 #pragma unroll
-  for (int w = 0; w < 4; ++w) s = dp4a_us(wq[w], xp[w], s);
-  return s;
-}
-
-__device__ __forceinline__ float combine_planes(int ia, int ib, int ic) {
-  return (float(ia) * 65536.0f + float(ib) * 256.0f) + float(ic);
-}
-
-__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t b) {  // (a & mask) | b
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(b));
-  return r;
-}
-
-// ---------------------------------------------------------------- per-row slice dots
-// Q4_K (GGUF layout): adds this thread's 64-element dot to acc[t] for every token.
-template <int T>
-__device__ __forceinline__ void q4k_slice(const uint8_t *__restrict__ row, int blk, int j,
-                                          const XSlice (&xs)[T], float (&acc)[T]) {
-  const uint8_t *bp = row + blk * BLOCK_Q4_K;
-  const uint4 hd = lds128(bp);
-  const uint4 q0 = lds128(bp + 16 + j * 32), q1 = lds128(bp + 32 + j * 32);
-  const float d = h2f_bits(uint16_t(hd.x & 0xFFFF));
-  const float dmin = h2f_bits(uint16_t(hd.x >> 16));
-  // get_scale_min_k4 for sub-blocks 2j (A) and 2j+1 (B), quants.rs:252-261; the two bytes of
-  // each of the three scale words sit side by side, so extract them as a 16-bit pair.
-  int scA, mA, scB, mB;
-  {
-    const uint32_t sel = (j & 1) ? 0x4342u : 0x4140u;  // bytes (2j&3, 2j&3+1) -> 16-bit lanes
-    const uint32_t x0 = __byte_perm(hd.y, 0u, sel), x1 = __byte_perm(hd.z, 0u, sel), x2 = __byte_perm(hd.w, 0u, sel);
-    uint32_t sc, mn;
-    if (j < 2) {
-      sc = x0 & 0x003F003Fu;
-      mn = x1 & 0x003F003Fu;
-    } else {
-      sc = (x2 & 0x000F000Fu) | ((x0 >> 2) & 0x00300030u);
-      mn = ((x2 >> 4) & 0x000F000Fu) | ((x1 >> 2) & 0x00300030u);
+  for (int cp = 0; cp < 4; ++cp) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(X.frag + (((b * 4 + cp) * NP + P) * 4 + t) * 4);
+    bf[2 * cp][0] = w.x & keep;
+    bf[2 * cp][1] = w.y & keep;
+    bf[2 * cp + 1][0] = w.z & keep;
+    bf[2 * cp + 1][1] = w.w & keep;
+  }
+  const int n0 = 2 * t, n1 = 2 * t + 1, tk0 = n0 / 3 < T ? n0 / 3 : T - 1, tk1 = n1 / 3 < T ? n1 / 3 : T - 1;
+  const float W0 = plane_weight(n0, NP) * X.scale[b * T + tk0];
+  const float W1 = plane_weight(n1, NP) * X.scale[b * T + tk1];
+  float S[T][2];
+#pragma unroll
+  for (int k = 0; k < T; ++k) {
+    const float2 s = *reinterpret_cast<const float2 *>(X.sum32 + (b * T + k) * 8 + 2 * t);
+    S[k][0] = s.x;
+    S[k][1] = s.y;
+  }
+  const uint32_t msel0 = 0x4440u | uint32_t(2 * (t & 1)), msel1 = msel0 + 1;
+#pragma unroll
+  for (int m = 0; m < NMAT; ++m) {
+    const uint8_t *rec = stage + m * mstride + lb * REC_Q4_K;
+    const uint4 hg = lds128(rec + 16 * g), hh = lds128(rec + 16 * (g + 8));
+    const uint8_t *qg = rec + 256 + 128 * g, *qh8 = qg + 8 * 128;  // rows g, g+8: same chunk swizzle
+    // get_scale_min_k4 (quants.rs:252-261), four 6-bit values per word: sub-blocks 0-3, 4-7
+    const uint32_t scg03 = hg.y & 0x3F3F3F3Fu, sch03 = hh.y & 0x3F3F3F3Fu;
+    const uint32_t scg47 = lop_and_or(hg.w, 0x0F0F0F0Fu, (hg.y >> 2) & 0x30303030u);
+    const uint32_t sch47 = lop_and_or(hh.w, 0x0F0F0F0Fu, (hh.y >> 2) & 0x30303030u);
+    // mins of sub-blocks 2t, 2t+1 (this lane's share of the min term)
+    const uint32_t mg = t < 2 ? (hg.z & 0x3F3F3F3Fu) : lop_and_or(hg.w >> 4, 0x0F0F0F0Fu, (hg.z >> 2) & 0x30303030u);
+    const uint32_t mh = t < 2 ? (hh.z & 0x3F3F3F3Fu) : lop_and_or(hh.w >> 4, 0x0F0F0F0Fu, (hh.z >> 2) & 0x30303030u);
+    int ae[4] = {0, 0, 0, 0}, ao[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // bytes 32j + 4t (chunk 2j) and 32j + 16 + 4t (chunk 2j + 1) of the row's quants
+      const int o0 = (((2 * j) ^ (g & 7)) << 4) + 4 * t, o1 = (((2 * j + 1) ^ (g & 7)) << 4) + 4 * t;
+      const uint32_t w0g = lds32(qg + o0), w1g = lds32(qg + o1), w0h = lds32(qh8 + o0), w1h = lds32(qh8 + o1);
+      const uint32_t swg = j < 2 ? scg03 : scg47, swh = j < 2 ? sch03 : sch47;
+      const uint32_t se = 0x4440u | uint32_t((2 * j) & 3), so = se + 1;
+      int d[4];
+      mma_u8s8(d, w0g & 0x0F0F0F0Fu, w0h & 0x0F0F0F0Fu, w1g & 0x0F0F0F0Fu, w1h & 0x0F0F0F0Fu, bf[2 * j][0],
+               bf[2 * j][1], 0, 0, 0, 0);
+      const int sge = prmt0(swg, se), she = prmt0(swh, se);
+      ae[0] += sge * d[0];
+      ae[1] += sge * d[1];
+      ae[2] += she * d[2];
+      ae[3] += she * d[3];
+      mma_u8s8(d, w0g & 0xF0F0F0F0u, w0h & 0xF0F0F0F0u, w1g & 0xF0F0F0F0u, w1h & 0xF0F0F0F0u, bf[2 * j + 1][0],
+               bf[2 * j + 1][1], 0, 0, 0, 0);
+      const int sgo = prmt0(swg, so), sho = prmt0(swh, so);
+      ao[0] += sgo * d[0];
+      ao[1] += sgo * d[1];
+      ao[2] += sho * d[2];
+      ao[3] += sho * d[3];
     }
-    scA = int(sc & 0xFFFF);
-    scB = int(sc >> 16);
-    mA = int(mn & 0xFFFF);
-    mB = int(mn >> 16);
-  }
-  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  uint32_t lo[8], hi[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    lo[k] = w[k] & 0x0F0F0F0Fu;
-    hi[k] = (w[k] >> 4) & 0x0F0F0F0Fu;
-  }
-  const float fmA = float(mA), fmB = float(mB);
+    for (int i = 0; i < 2; ++i) {
+      const uint4 &h = i ? hh : hg;
+      const uint32_t mw = i ? mh : mg;
+      const float d16 = h2f_bits(uint16_t(h.x & 0xFFFF)) * 0.0625f;
+      const float dmin = h2f_bits(uint16_t(h.x >> 16));
+      const float m0 = float(prmt0(mw, msel0)), m1 = float(prmt0(mw, msel1));
+      const float F0 = float(ae[2 * i] * 16 + ao[2 * i]) * W0;
+      const float F1 = float(ae[2 * i + 1] * 16 + ao[2 * i + 1]) * W1;
 #pragma unroll
-  for (int t = 0; t < T; ++t) {
-    int I[3];
-#pragma unroll
-    for (int p = 0; p < 3; ++p)
-      I[p] = scA * (dot16(lo, xs[t].p[p][0]) + dot16(lo + 4, xs[t].p[p][0] + 4)) +
-             scB * (dot16(hi, xs[t].p[p][1]) + dot16(hi + 4, xs[t].p[p][1] + 4));
-    const float f = combine_planes(I[0], I[1], I[2]);
-    acc[t] += d * (xs[t].scale * f) - dmin * (fmA * xs[t].sum32[0] + fmB * xs[t].sum32[1]);
+      for (int k = 0; k < T; ++k) {
+        const float f = (tk0 == k ? F0 : 0.f) + (tk1 == k ? F1 : 0.f);
+        v[m][i][k] = d16 * f - dmin * (m0 * S[k][0] + m1 * S[k][1]);
+      }
+    }
   }
 }
 
-// Q6_K (device SoA layout per row: ql[nb][128] | qh[nb][64] | sc[nb][16] | d[nb] f16).
-// Slice j covers elements j*64..j*64+63 = 128-half n = j/2, quarter groups g = 2(j&1), 2(j&1)+1.
-template <int T>
-__device__ __forceinline__ void q6k_slice(const uint8_t *__restrict__ row, int nb, int blk, int j,
-                                          const XSlice (&xs)[T], float (&acc)[T]) {
-  const int n = j >> 1, jj = j & 1;
-  const uint8_t *ql = row + blk * 128 + n * 64;
-  const uint8_t *qh = row + nb * 128 + blk * 64 + n * 32;
-  const uint32_t scw = *reinterpret_cast<const uint32_t *>(row + nb * 192 + blk * 16 + n * 8 + 4 * jj);
-  const uint16_t dbits = *reinterpret_cast<const uint16_t *>(row + nb * 208 + blk * 2);
-  const uint4 a0 = lds128(ql), a1 = lds128(ql + 16), b0 = lds128(ql + 32), b1 = lds128(ql + 48);
-  const uint4 h0 = lds128(qh), h1 = lds128(qh + 16);
-  const int sA0 = int(int8_t(scw & 0xFF)), sA1 = int(int8_t((scw >> 8) & 0xFF));
-  const int sB0 = int(int8_t((scw >> 16) & 0xFF)), sB1 = int(int8_t(scw >> 24));
-  const float d = h2f_bits(dbits);
-  const int sh = 4 * jj;
-  const uint32_t qa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-  const uint32_t qb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-  const uint32_t qhw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-  uint32_t uA[8], uB[8];
+// Q6_K (tiled records, as unit_q4k).  Chunk c = 4n + q covers elements 128n + 32q + l, l in [0,32):
+// q6 = ((ql[64n + 32(q&1) + l] >> 4(q>>1)) & 15) | (((qh[32n + l] >> 2q) & 3) << 4), scale group
+// 2c + l/16 (quants.rs:210-249).  The B columns are masked per group (columns 0-2: elements
+// l < 16, columns 3-5: l >= 16) so that each output column sees one scale group.
+template <int NMAT, int T>
+__device__ __forceinline__ void unit_q6k(const uint8_t *__restrict__ stage, int mstride, int lb, int b,
+                                         const XSmem &X, int g, int t, float (&v)[NMAT][2][T]) {
+  constexpr int NP = 3 * T;
+  const uint32_t keep0 = g < 3 ? 0xFFFFFFFFu : 0u, keep1 = (g >= 3 && g < 6) ? 0xFFFFFFFFu : 0u;
+  const int gp = g < 6 ? g % 3 : 0;
+  // output columns of this lane: n = 2t + k -> scale group parity p_k (columns >= 6 are zero)
+  const int n0 = 2 * t, n1 = 2 * t + 1;
+  const uint32_t p0 = n0 >= 3 ? 1u : 0u, p1 = n1 >= 3 ? 1u : 0u;
+  const uint32_t se0 = sext_sel(p0), se1 = sext_sel(p1), so0 = sext_sel(2u + p0), so1 = sext_sel(2u + p1);
+  float W0[T], W1[T];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    // 2 high bits of group g sit at bits 2g..2g+1 of each qh byte; move them to bits 4..5
-    const uint32_t hA = ((qhw[k] >> sh) << 4) & 0x30303030u;
-    const uint32_t hB = ((qhw[k] >> (sh + 2)) << 4) & 0x30303030u;
-    uA[k] = lop_and_or(qa[k] >> sh, 0x0F0F0F0Fu, hA);
-    uB[k] = lop_and_or(qb[k] >> sh, 0x0F0F0F0Fu, hB);
+  for (int k = 0; k < T; ++k) {
+    const float xs = X.scale[b * T + k];
+    W0[k] = plane_weight(n0, 6) * xs;
+    W1[k] = plane_weight(n1, 6) * xs;
   }
+  const int *q6c = X.q6c + (b * T) * 64 + t * 16;
 #pragma unroll
-  for (int t = 0; t < T; ++t) {
-    int I[3];
+  for (int m = 0; m < NMAT; ++m) {
+    const uint8_t *rec = stage + m * mstride + lb * REC_Q6_K;
+    const uint4 scg = lds128(rec + 3072 + 16 * g), sch = lds128(rec + 3072 + 16 * (g + 8));
+    const float dg = h2f_bits(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * g));
+    const float dh = h2f_bits(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * (g + 8)));
+    const int sw_l = g & 7, sw_h = (g >> 1) & 3;  // chunk swizzles of ql / qh (rows g and g+8 alike)
+    int acc[T][4];
 #pragma unroll
-    for (int p = 0; p < 3; ++p)
-      I[p] = sA0 * dot16(uA, xs[t].p[p][0]) + sA1 * dot16(uA + 4, xs[t].p[p][0] + 4) +
-             sB0 * dot16(uB, xs[t].p[p][1]) + sB1 * dot16(uB + 4, xs[t].p[p][1] + 4);
-    const float f = combine_planes(I[0], I[1], I[2]);
-    // sum (u - 32) * sc * x = sc * (sum u x - 32 sum x), per 16-element scale group
-    const float corr = float(sA0) * xs[t].sum16[0] + float(sA1) * xs[t].sum16[1] + float(sB0) * xs[t].sum16[2] +
-                       float(sB1) * xs[t].sum16[3];
-    acc[t] += d * (xs[t].scale * f - 32.0f * corr);
+    for (int k = 0; k < T; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      // ql bytes 64n + 32qq + 16k + 4t (chunk 4n + 2qq + k), qh bytes 32n + 16k + 4t (chunk 2n + k)
+      const uint8_t *lg = rec + 128 * g + 4 * t, *lh = lg + 8 * 128;
+      const uint8_t *hg_ = rec + 2048 + 64 * g + 4 * t, *hh_ = hg_ + 8 * 64;
+      uint32_t Lg[2][2], Lh[2][2], Hg[2], Hh[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+          const int ol = ((4 * n + 2 * qq + k) ^ sw_l) << 4;
+          Lg[qq][k] = lds32(lg + ol);
+          Lh[qq][k] = lds32(lh + ol);
+        }
+        const int oh = ((2 * n + k) ^ sw_h) << 4;
+        Hg[k] = lds32(hg_ + oh);
+        Hh[k] = lds32(hh_ + oh);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int c = 4 * n + q;
+        uint32_t ug[2], uh[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const uint32_t lwg = Lg[q & 1][k], lwh = Lh[q & 1][k];
+          if (q == 0) {
+            ug[k] = lop_and_or(lwg, 0x0F0F0F0Fu, (Hg[k] << 4) & 0x30303030u);
+            uh[k] = lop_and_or(lwh, 0x0F0F0F0Fu, (Hh[k] << 4) & 0x30303030u);
+          } else if (q == 1) {
+            ug[k] = lop_and_or(lwg, 0x0F0F0F0Fu, (Hg[k] << 2) & 0x30303030u);
+            uh[k] = lop_and_or(lwh, 0x0F0F0F0Fu, (Hh[k] << 2) & 0x30303030u);
+          } else if (q == 2) {
+            ug[k] = lop_and_or(lwg >> 4, 0x0F0F0F0Fu, Hg[k] & 0x30303030u);
+            uh[k] = lop_and_or(lwh >> 4, 0x0F0F0F0Fu, Hh[k] & 0x30303030u);
+          } else {
+            ug[k] = lop_and_or(lwg >> 4, 0x0F0F0F0Fu, (Hg[k] >> 2) & 0x30303030u);
+            uh[k] = lop_and_or(lwh >> 4, 0x0F0F0F0Fu, (Hh[k] >> 2) & 0x30303030u);
+          }
+        }
+        const uint32_t swg = (c >> 1) == 0 ? scg.x : (c >> 1) == 1 ? scg.y : (c >> 1) == 2 ? scg.z : scg.w;
+        const uint32_t swh = (c >> 1) == 0 ? sch.x : (c >> 1) == 1 ? sch.y : (c >> 1) == 2 ? sch.z : sch.w;
+        const uint32_t s0 = (c & 1) ? so0 : se0, s1 = (c & 1) ? so1 : se1;
+        const int sg0 = prmt0(swg, s0), sg1 = prmt0(swg, s1), sh0 = prmt0(swh, s0), sh1 = prmt0(swh, s1);
+#pragma unroll
+        for (int k = 0; k < T; ++k) {
+          const uint4 w =
+              *reinterpret_cast<const uint4 *>(X.frag + (((b * 4 + (c >> 1)) * NP + 3 * k + gp) * 4 + t) * 4);
+          const uint32_t b0 = ((c & 1) ? w.z : w.x) & keep0, b1 = ((c & 1) ? w.w : w.y) & keep1;
+          const int2 co = *reinterpret_cast<const int2 *>(q6c + k * 64 + c * 2);
+          int d[4];
+          mma_u8s8(d, ug[0], uh[0], ug[1], uh[1], b0, b1, co.x, co.y, co.x, co.y);
+          acc[k][0] += sg0 * d[0];
+          acc[k][1] += sg1 * d[1];
+          acc[k][2] += sh0 * d[2];
+          acc[k][3] += sh1 * d[3];
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < T; ++k) {
+      v[m][0][k] = dg * (float(acc[k][0]) * W0[k] + float(acc[k][1]) * W1[k]);
+      v[m][1][k] = dh * (float(acc[k][2]) * W0[k] + float(acc[k][3]) * W1[k]);
+    }
   }
-}
-
-__device__ __forceinline__ float gelu_tanh_mul(float v, float u) {
-  // real_math.rs:79-85
-  const float k = 0.7978845608028654f;
-  const float inner = k * (v + 0.044715f * v * v * v);
-  return 0.5f * v * (1.0f + tanhf(inner)) * u;
 }
 
 // ---------------------------------------------------------------- kernel
-constexpr int MAX_SEG = 3;
-
-struct QGemvArgs {
-  GemvSeg seg[MAX_SEG];
-  int nseg;
-  int64_t total_rows;
-  int nb;
-  int groups;
-  int nstage;
-  int stage_bytes;
-  int rps_max;
-  int rcap;       // rows whose block partials the CTA can hold before it must finalize
-  int red_bytes;  // bytes of the partials buffer (also holds the activation slice records)
-  GemvPrologue pro;
-  unsigned *err;
+struct GemvSegK {
+  const uint8_t *w[2];
+  float *y;
+  int rows;
+  int tile0;  // first global tile of the segment
+  int type;
+  int rec;  // record bytes (REC_Q4_K / REC_Q6_K)
+  int nbs;  // blocks per stage at most (a matrix's records of a stage: nbs * rec bytes)
+  int ldy;
 };
 
-// Segments let one launch cover several matrices with the same K (q, k and v of a layer):
-// the CTAs split the concatenated row space evenly and each stage stays inside one segment.
+struct QGemvArgs {
+  GemvSegK seg[GEMV_MAX_SEG];
+  int nseg;
+  int nb;
+  int units;      // tiles * nb
+  int uq, ur;     // CTA c owns units [c*uq + min(c, ur), ...), uq + (c < ur) of them
+  int nstage;     // ring slots
+  int stage_bytes;
+  int red_off, x_off, ring_off;  // dynamic shared-memory offsets
+  GemvPrologue pro;
+  unsigned *err;
+  unsigned *cnt;  // per CTA boundary: arrivals of the two CTAs sharing a tile
+  float *part;    // per CTA boundary: GEMV_SPLIT_SLOT floats of partial row sums
+};
+
+// The tiles a CTA touches, in processing order: the tiles it shares with its neighbours come first
+// (its last tile, then its first) so that their partial sums are published early, then the tiles
+// it owns alone, ascending.
+struct CtaTiles {
+  int u0, u1, tf, tl, np, count;
+  bool fs, ls;  // first tile shared with CTA cta-1 / last tile shared with CTA cta+1
+  __device__ __forceinline__ void init(int u0_, int u1_, int nb) {
+    u0 = u0_;
+    u1 = u1_;
+    tf = u0 / nb;
+    tl = (u1 - 1) / nb;
+    fs = u0 != tf * nb;
+    ls = u1 != (tl + 1) * nb;
+    np = (fs ? 1 : 0) + (ls ? 1 : 0);
+    count = tl - tf + 1;
+  }
+  __device__ __forceinline__ int tile(int i) const {
+    if (i < np) return (ls && i == 0) ? tl : tf;
+    return tf + (fs ? 1 : 0) + (i - np);
+  }
+};
+
+// Stage = one tile's rows over a block range [b0, b0 + nbs) of the CTA's units.
+struct GemvStage {
+  int lt;   // processing index of the tile within the CTA
+  int tau;  // global tile
+  int r0;   // first row of the tile within its segment
+  int ks;   // CTA-local index of the stage's first unit
+  int sg, b0, nbs, nr;
+};
+
+__device__ __forceinline__ int seg_of_tile(const QGemvArgs &a, int tau) {
+  int sg = 0;
+  while (sg + 1 < a.nseg && tau >= a.seg[sg + 1].tile0) ++sg;
+  return sg;
+}
+
+// Cursor over the CTA's stages (the producer and every consumer warp walk the same sequence).
+struct StageWalk {
+  int i, b, hi, tau, sg, ku;
+  __device__ __forceinline__ void set_tile(const QGemvArgs &a, const CtaTiles &ct) {
+    tau = ct.tile(i);
+    const int base = tau * a.nb;
+    b = ct.u0 > base ? ct.u0 - base : 0;
+    hi = ct.u1 - base < a.nb ? ct.u1 - base : a.nb;
+    sg = seg_of_tile(a, tau);
+  }
+  __device__ __forceinline__ void init(const QGemvArgs &a, const CtaTiles &ct) {
+    i = 0;
+    ku = 0;
+    set_tile(a, ct);
+  }
+  __device__ __forceinline__ bool more(const CtaTiles &ct) const { return i < ct.count; }
+  __device__ __forceinline__ void next(const QGemvArgs &a, const CtaTiles &ct, GemvStage &s) {
+    const GemvSegK &S = a.seg[sg];
+    s.lt = i;
+    s.tau = tau;
+    s.b0 = b;
+    s.sg = sg;
+    s.ks = ku;
+    const int n = S.nbs < hi - b ? S.nbs : hi - b;
+    s.nbs = n;
+    s.r0 = (tau - S.tile0) * GEMV_TILE;
+    s.nr = S.rows - s.r0 < GEMV_TILE ? S.rows - s.r0 : GEMV_TILE;
+    ku += n;
+    b += n;
+    if (b == hi && ++i < ct.count) set_tile(a, ct);
+  }
+};
+
+// Called by a warp after each unit of a shared tile (processing index lt < np).  The warp that
+// completes the CTA's part of the tile sums its rows over the CTA's blocks, publishes the partial
+// sums for the neighbour, and, if the neighbour's part is already published, writes the outputs:
+// lower part (blocks from 0) + upper part, in that order whichever CTA finishes second.
 template <int NMAT, int T>
-__global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGemvArgs a) {
+__device__ __forceinline__ void finish_shared(const QGemvArgs &a, const CtaTiles &ct, int lt, int tau, int cta,
+                                           const float *red, int *s_done, int lane) {
+  const int nb = a.nb;
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) {
+    __threadfence_block();
+    old = atomicAdd(&s_done[lt], 1);
+  }
+  old = __shfl_sync(0xFFFFFFFFu, old, 0);
+  const int base = tau * nb;
+  const int lo = ct.u0 > base ? ct.u0 - base : 0, hi = ct.u1 - base < nb ? ct.u1 - base : nb;
+  if (old != hi - lo - 1) return;
+  __syncwarp();
+  __threadfence_block();
+  const bool upper = ct.fs && tau == ct.tf;  // blocks [lo, nb) here, [0, lo) in CTA cta-1
+  const int bslot = upper ? cta - 1 : cta;
+  float *mine = a.part + bslot * GEMV_SPLIT_SLOT + (upper ? GEMV_SPLIT_SLOT / 2 : 0);
+  const float *other = a.part + bslot * GEMV_SPLIT_SLOT + (upper ? 0 : GEMV_SPLIT_SLOT / 2);
+  const int row = lane & 15, kk = lane >> 4;
+  float vm[NMAT];
+  if (kk < T) {
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+      const float *p = red + (((lt * GEMV_TILE + row) * NMAT + m) * T + kk) * nb;
+      float sum = 0.f;
+      for (int bb = lo; bb < hi; ++bb) sum += p[bb];
+      vm[m] = sum;
+      mine[(row * NMAT + m) * T + kk] = sum;
+    }
+  }
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    __threadfence();  // this warp's partials, then the arrival
+    last = atomicAdd(&a.cnt[bslot], 1u) == 1u;
+    if (last) {
+      a.cnt[bslot] = 0;  // both parts are in: reset for the next launch
+      __threadfence();
+    }
+  }
+  last = __shfl_sync(0xFFFFFFFFu, last, 0);
+  __syncwarp();
+  if (!last || kk >= T) return;
+  const GemvSegK &S = a.seg[seg_of_tile(a, tau)];
+  const int r = (tau - S.tile0) * GEMV_TILE + row;
+  if (r >= S.rows) return;
+  float w[NMAT];
+#pragma unroll
+  for (int m = 0; m < NMAT; ++m) {
+    const float o = __ldcg(other + (row * NMAT + m) * T + kk);
+    w[m] = upper ? o + vm[m] : vm[m] + o;
+  }
+  S.y[int64_t(kk) * S.ldy + r] = NMAT == 2 ? gelu_tanh_mul(w[0], w[NMAT - 1]) : w[0];
+}
+
+// Segments let one launch cover several matrices with the same K (q, k and v of a layer).
+template <int NMAT, int T>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float pro_red[GEMV_MAX_T][GEMV_MAX_THREADS / 32];
-  const int tid = threadIdx.x;
-  const int S = a.nb * SLICES_PER_BLOCK;
-  const int g = tid / S, s = tid % S;
-  const int blk = s >> 2, j = s & 3;
-  const int lane = tid & 31;
-  const int K = a.nb * QK_K;
-
-  const int64_t r_begin = a.total_rows * blockIdx.x / gridDim.x;
-  const int64_t r_end = a.total_rows * (blockIdx.x + 1) / gridDim.x;
-
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-  float *red = reinterpret_cast<float *>(smem + 128);  // [rcap][NMAT][T][nb] block partials
-  uint8_t *stages = smem + 128 + a.red_bytes;
-
-  // stage at global row `pos`: segment, first local row, row count
-  auto stage_at = [&](int64_t pos, int &sg, int64_t &local0, int &nr) {
-    int64_t base = 0;
-    sg = 0;
-    while (sg + 1 < a.nseg && pos >= base + a.seg[sg].rows) base += a.seg[sg++].rows;
-    local0 = pos - base;
-    int64_t n = a.seg[sg].rps;
-    if (r_end - pos < n) n = r_end - pos;
-    if (a.seg[sg].rows - local0 < n) n = a.seg[sg].rows - local0;
-    nr = int(n);
-  };
-  // Producer cursor: every thread tracks it (it is deterministic) so that refills are a uniform
-  // decision; only thread 0 issues the copies.
-  int64_t ppos = r_begin;
-  int pit = 0;
-  auto issue_next = [&]() {
-    int sg, nr;
-    int64_t l0;
-    stage_at(ppos, sg, l0, nr);
-    if (tid == 0) {
-      const GemvSeg &G = a.seg[sg];
-      const int slot = pit % a.nstage;
-      const uint32_t bytes = uint32_t(nr) * G.row_bytes;
-      mbar_arrive_expect_tx(&bars[slot], bytes * NMAT);
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m)
-        bulk_g2s(stages + slot * a.stage_bytes + m * G.rps * G.row_bytes, G.w[m] + l0 * G.row_bytes, bytes,
-                 &bars[slot]);
-    }
-    ppos += nr;
-    ++pit;
-  };
-  // Writes the outputs of CTA-relative rows [c0, c1) from their block partials.
-  auto finalize = [&](int c0, int c1) {
-    for (int idx = tid; idx < (c1 - c0) * T; idx += blockDim.x) {
-      const int pr = idx / T, t = idx % T;
-      int sg, nr;
-      int64_t l0;
-      stage_at(r_begin + c0 + pr, sg, l0, nr);
-      float v[NMAT];
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        const float *p = red + ((pr * NMAT + m) * T + t) * a.nb;
-        float sum = 0.f;
-        for (int b = 0; b < a.nb; ++b) sum += p[b];
-        v[m] = sum;
-      }
-      a.seg[sg].y[int64_t(t) * a.seg[sg].ldy + l0] = NMAT == 2 ? gelu_tanh_mul(v[0], v[NMAT - 1]) : v[0];
-    }
-  };
+  __shared__ float pro_red[GEMV_MAX_T][GEMV_CONSUMERS];
+  __shared__ int s_done[2];  // finished units of the shared tiles
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = a.nb, K = nb * QK_K;
+  const int cta = int(blockIdx.x);
+  CtaTiles ct;
+  {
+    const int u0 = cta * a.uq + (cta < a.ur ? cta : a.ur);
+    ct.init(u0, u0 + a.uq + (cta < a.ur ? 1 : 0), nb);
+  }
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem), *empty = full + GEMV_MAX_STAGES;
+  float *red = reinterpret_cast<float *>(smem + a.red_off);  // [local tile][16][NMAT][T][nb]
+  const XSmem X = x_view(smem + a.x_off, nb, T);
+  uint8_t *ring = smem + a.ring_off;
 
   if (tid == 0) {
-    for (int i = 0; i < a.nstage; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < a.nstage; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], GEMV_CONSUMERS);
+    }
     fence_mbar_init();
+    s_done[0] = s_done[1] = 0;
   }
-  // Weights never depend on the previous kernel: stream them before the dependency wait so their
-  // fetch overlaps the producer's tail (programmatic dependent launch).  Every thread advances
-  // the cursor; thread 0 (which initialised the barriers just above) issues the copies.
-  while (pit < a.nstage && ppos < r_end) issue_next();
+  __syncthreads();
+
+  if (warp == GEMV_CONSUMERS) {
+    // ---- producer: weights never depend on the previous kernel, so no dependency wait here
+    StageWalk wk;
+    wk.init(a, ct);
+    for (int s = 0; wk.more(ct); ++s) {
+      GemvStage st;
+      wk.next(a, ct, st);
+      const int slot = s % a.nstage;
+      if (s >= a.nstage) {
+        if (lane == 0) mbar_wait_bounded(&empty[slot], uint32_t((s / a.nstage) - 1) & 1u, a.err);
+        __syncwarp();
+      }
+      const GemvSegK &S = a.seg[st.sg];
+      // the stage's records of each matrix: one contiguous range
+      const uint32_t bytes = uint32_t(st.nbs) * uint32_t(S.rec);
+      const int64_t first = int64_t(st.tau - S.tile0) * nb + st.b0;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[slot], bytes * NMAT);
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+          bulk_g2s(ring + size_t(slot) * a.stage_bytes + m * S.nbs * S.rec, S.w[m] + first * S.rec, bytes, &full[slot]);
+      }
+      __syncwarp();
+    }
+    return;
+  }
+
+  // ---- consumers
   pdl_wait();
   pdl_launch_dependents();
 
-  // ---- activations, computed once per CTA.  Unit u = (token t, 256-block b) belongs to warp
-  // u % nwarps and lane l holds its elements 8l..8l+7, so every global access is a coalesced
-  // 1 KB piece of a row.  The optional fused residual add + RMSNorm passes run first; the last
-  // pass writes each 64-element slice's digit planes and sums into a shared-memory record
-  // (aliasing the row-partials buffer), from which every thread loads its own slice.
-  XSlice xs[T];
+  // Activations, computed once per CTA.  Unit (token t, 256-block b) belongs to warp
+  // (t*nb + b) % 15 and lane l holds its elements 8l..8l+7, so every global access is a coalesced
+  // 1 KB piece of a row.  The optional fused residual add + RMSNorm passes run first.
   {
     const GemvPrologue &P = a.pro;
-    uint32_t *xrec = reinterpret_cast<uint32_t *>(red);
-    const int nwarps = int(blockDim.x) >> 5, warp = tid >> 5;
-    const int units = T * a.nb;
+    const int units = T * nb;
     float s1[T], s2[T];
 #pragma unroll
     for (int t = 0; t < T; ++t) s1[t] = s2[t] = 1.0f;
@@ -398,8 +666,8 @@ __global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGe
       float part[T];
 #pragma unroll
       for (int t = 0; t < T; ++t) part[t] = 0.f;
-      for (int u = warp; u < units; u += nwarps) {
-        const int t = u / a.nb, b = u % a.nb;
+      for (int u = warp; u < units; u += GEMV_CONSUMERS) {
+        const int t = u / nb, b = u % nb;
         float v[8];
         value8(t, b, step, v);
         float q = 0.f;
@@ -413,14 +681,14 @@ __global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGe
         const float w = warp_sum(part[t]);
         if (lane == 0) pro_red[t][warp] = w;
       }
-      __syncthreads();
+      consumer_bar();
 #pragma unroll
       for (int t = 0; t < T; ++t) {
         float sum = 0.f;
-        for (int w = 0; w < nwarps; ++w) sum += pro_red[t][w];
+        for (int w = 0; w < GEMV_CONSUMERS; ++w) sum += pro_red[t][w];
         out[t] = sum;
       }
-      __syncthreads();
+      consumer_bar();
     };
     if (P.mode != 0) {
       float tot[T];
@@ -429,74 +697,83 @@ __global__ void __launch_bounds__(GemvCfg<T>::THREADS, 1) qgemv_kernel(const QGe
 #pragma unroll
         for (int t = 0; t < T; ++t) s1[t] = 1.0f / sqrtf(tot[t] / float(K) + P.eps);
       }
-      if (P.mode == 2 && (P.w_next || (P.resid_out && blockIdx.x == 0))) {
-        cta_sumsq(1, P.resid_out && blockIdx.x == 0, tot);
+      if (P.mode == 2 && (P.w_next || (P.resid_out && cta == 0))) {
+        cta_sumsq(1, P.resid_out && cta == 0, tot);
 #pragma unroll
         for (int t = 0; t < T; ++t) s2[t] = 1.0f / sqrtf(tot[t] / float(K) + P.eps);
       }
     }
-    for (int u = warp; u < units; u += nwarps) {
-      const int t = u / a.nb, b = u % a.nb;
+    for (int u = warp; u < units; u += GEMV_CONSUMERS) {
+      const int t = u / nb, b = u % nb;
       float v[8];
       value8(t, b, 2, v);
-      quantize8(v, lane, xrec + ((t * a.nb + b) * SLICES_PER_BLOCK + (lane >> 3)) * XREC_WORDS);
+      emit_block<T>(v, lane, b, t, X);
     }
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < T; ++t) load_slice(xrec + ((t * a.nb + blk) * SLICES_PER_BLOCK + j) * XREC_WORDS, xs[t]);
   }
-  __syncthreads();  // slices loaded (the records alias the partials) and barrier inits visible
+  consumer_bar();
 
-  const unsigned seg = 0xFu << (lane & 28);
-  int64_t pos = r_begin;
-  int pend0 = 0;  // CTA-relative row held in red[0]
-  for (int it = 0; pos < r_end; ++it) {
-    int sg, nr;
-    int64_t l0;
-    stage_at(pos, sg, l0, nr);
-    const int crow = int(pos - r_begin);
-    if (crow + nr - pend0 > a.rcap) {  // partial buffer full: emit the pending rows first
-      __syncthreads();
-      finalize(pend0, crow);
-      __syncthreads();
-      pend0 = crow;
-    }
-    const GemvSeg &G = a.seg[sg];
-    const int slot = it % a.nstage;
-    mbar_wait_bounded(&bars[slot], (it / a.nstage) & 1, a.err);
-    const uint8_t *st = stages + slot * a.stage_bytes;
-    const bool q4 = G.type == T_Q4_K;
-    for (int lr = g; lr < nr; lr += a.groups) {
-      float acc[NMAT][T];
+  // ---- units: CTA-local unit k (stage order, block fastest) belongs to consumer warp k % 15
+  const int g = lane >> 2, t = lane & 3;
+  {
+    StageWalk wk;
+    wk.init(a, ct);
+    int k = warp;  // next CTA-local unit of this warp
+    for (int slot = 0, phase = 0; wk.more(ct);) {
+      GemvStage st;
+      wk.next(a, ct, st);
+      if (k < st.ks + st.nbs) {
+        mbar_wait_bounded(&full[slot], uint32_t(phase), a.err);
+        const GemvSegK &S = a.seg[st.sg];
+        const uint8_t *tile = ring + size_t(slot) * a.stage_bytes;
+        for (; k < st.ks + st.nbs; k += GEMV_CONSUMERS) {
+          const int b = st.b0 + (k - st.ks);
+          float v[NMAT][2][T];
+          if (S.type == T_Q4_K)
+            unit_q4k<NMAT, T>(tile, S.nbs * S.rec, b - st.b0, b, X, g, t, v);
+          else
+            unit_q6k<NMAT, T>(tile, S.nbs * S.rec, b - st.b0, b, X, g, t, v);
 #pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
+          for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-        for (int t = 0; t < T; ++t) acc[m][t] = 0.f;
-        const uint8_t *row = st + (m * G.rps + lr) * G.row_bytes;
-        if (q4)
-          q4k_slice<T>(row, blk, j, xs, acc[m]);
-        else
-          q6k_slice<T>(row, a.nb, blk, j, xs, acc[m]);
-      }
-      float *rd = red + (crow - pend0 + lr) * NMAT * T * a.nb;
+            for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          float v = acc[m][t];
-          v += __shfl_xor_sync(seg, v, 1);
-          v += __shfl_xor_sync(seg, v, 2);
-          if ((s & 3) == 0) rd[(m * T + t) * a.nb + blk] = v;
+              for (int kk = 0; kk < T; ++kk) {
+                float x = v[m][i][kk];
+                x += __shfl_xor_sync(0xFFFFFFFFu, x, 1);
+                x += __shfl_xor_sync(0xFFFFFFFFu, x, 2);
+                if (t == 0) red[(((st.lt * GEMV_TILE + g + 8 * i) * NMAT + m) * T + kk) * nb + b] = x;
+              }
+          if (st.lt < ct.np) finish_shared<NMAT, T>(a, ct, st.lt, st.tau, cta, red, s_done, lane);
         }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&empty[slot]);
+      if (++slot == a.nstage) {
+        slot = 0;
+        phase ^= 1;
+      }
     }
-    if (ppos < r_end) {  // this slot is needed again: wait until every thread is done with it
-      __syncthreads();
-      issue_next();
-    }
-    pos += nr;
   }
-  __syncthreads();
-  finalize(pend0, int(r_end - r_begin));
+  if (ct.count == ct.np) return;
+  consumer_bar();
+
+  // ---- tiles owned alone: row sums over all blocks in block order
+  for (int item = tid; item < (ct.count - ct.np) * GEMV_TILE * T; item += GEMV_CONSUMERS * 32) {
+    const int kk = item % T, row = (item / T) % GEMV_TILE, lt = ct.np + item / (T * GEMV_TILE);
+    const int tau = ct.tile(lt);
+    const GemvSegK &S = a.seg[seg_of_tile(a, tau)];
+    const int r = (tau - S.tile0) * GEMV_TILE + row;
+    if (r >= S.rows) continue;
+    float vm[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+      const float *p = red + (((lt * GEMV_TILE + row) * NMAT + m) * T + kk) * nb;
+      float sum = 0.f;
+      for (int bb = 0; bb < nb; ++bb) sum += p[bb];
+      vm[m] = sum;
+    }
+    S.y[int64_t(kk) * S.ldy + r] = NMAT == 2 ? gelu_tanh_mul(vm[0], vm[NMAT - 1]) : vm[0];
+  }
 }
 
 // ---------------------------------------------------------------- float-weight GEMV
@@ -584,22 +861,35 @@ __global__ void dequant_kernel(int type, const uint8_t *__restrict__ w, int64_t 
   }
 }
 
-// GGUF Q6_K rows -> device SoA rows (see file header).
-__global__ void repack_q6k_kernel(const uint8_t *__restrict__ src, int64_t rows, int nb, int dst_row_bytes,
-                                  uint8_t *__restrict__ dst) {
-  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (b >= rows * nb) return;
-  const int64_t r = b / nb;
-  const int k = int(b % nb);
-  const uint8_t *s = src + b * BLOCK_Q6_K;
-  uint8_t *row = dst + r * dst_row_bytes;
-  for (int i = 0; i < 128; ++i) row[k * 128 + i] = s[i];
-  for (int i = 0; i < 64; ++i) row[nb * 128 + k * 64 + i] = s[128 + i];
-  for (int i = 0; i < 16; ++i) row[nb * 192 + k * 16 + i] = s[192 + i];
-  row[nb * 208 + 2 * k] = s[208];
-  row[nb * 208 + 2 * k + 1] = s[209];
-  if (k == 0)
-    for (int i = nb * 210; i < dst_row_bytes; ++i) row[i] = 0;
+// GGUF Q4_K / Q6_K rows -> tiled device records (common.cuh).  One thread per (tile, block, row of
+// the tile); rows past the end of the tensor are zero.
+__global__ void repack_kquant_kernel(int type, const uint8_t *__restrict__ src, int64_t rows, int nb,
+                                     uint8_t *__restrict__ dst) {
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t ntiles = (rows + KQ_TILE - 1) / KQ_TILE;
+  if (gid >= ntiles * nb * KQ_TILE) return;
+  const int r = int(gid % KQ_TILE);
+  const int64_t rec = gid / KQ_TILE;  // tile * nb + block
+  const int b = int(rec % nb);
+  const int64_t row = (rec / nb) * KQ_TILE + r;
+  const bool valid = row < rows;
+  if (type == T_Q4_K) {
+    const uint8_t *s = src + (row * nb + b) * BLOCK_Q4_K;
+    uint8_t *o = dst + rec * REC_Q4_K;
+    for (int i = 0; i < 16; ++i) o[16 * r + i] = valid ? s[i] : 0;
+    for (int j = 0; j < 8; ++j)
+      for (int i = 0; i < 16; ++i) o[256 + 128 * r + 16 * (j ^ (r & 7)) + i] = valid ? s[16 + 16 * j + i] : 0;
+  } else {
+    const uint8_t *s = src + (row * nb + b) * BLOCK_Q6_K;
+    uint8_t *o = dst + rec * REC_Q6_K;
+    for (int j = 0; j < 8; ++j)
+      for (int i = 0; i < 16; ++i) o[128 * r + 16 * (j ^ (r & 7)) + i] = valid ? s[16 * j + i] : 0;
+    for (int j = 0; j < 4; ++j)
+      for (int i = 0; i < 16; ++i) o[2048 + 64 * r + 16 * (j ^ ((r >> 1) & 3)) + i] = valid ? s[128 + 16 * j + i] : 0;
+    for (int i = 0; i < 16; ++i) o[3072 + 16 * r + i] = valid ? s[192 + i] : 0;
+    o[3328 + 2 * r] = valid ? s[208] : 0;
+    o[3329 + 2 * r] = valid ? s[209] : 0;
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -610,14 +900,21 @@ int device_row_bytes(int type, int64_t K) {
     case T_F16:
     case T_BF16: return int(K * 2);
     case T_Q4_K: return K % QK_K ? -1 : int(K / QK_K * BLOCK_Q4_K);
-    case T_Q6_K: return K % QK_K ? -1 : int((K / QK_K * BLOCK_Q6_K + 15) / 16 * 16);
+    case T_Q6_K: return K % QK_K ? -1 : int(K / QK_K * BLOCK_Q6_K);
   }
   return -1;
 }
 
-int gguf_row_bytes(int type, int64_t K) {
-  if (type == T_Q6_K) return K % QK_K ? -1 : int(K / QK_K * BLOCK_Q6_K);
-  return device_row_bytes(type, K);
+int gguf_row_bytes(int type, int64_t K) { return device_row_bytes(type, K); }
+
+int64_t device_tensor_bytes(int type, int64_t rows, int64_t K) {
+  if (rows < 0) return -1;
+  if (type == T_Q4_K || type == T_Q6_K) {
+    if (K <= 0 || K % QK_K) return -1;
+    return (rows + KQ_TILE - 1) / KQ_TILE * (K / QK_K) * kquant_rec_bytes(type);
+  }
+  const int rb = device_row_bytes(type, K);
+  return rb < 0 ? -1 : int64_t(rb) * rows;
 }
 
 // Address of this module's device error word on the current device (cached per device).
@@ -632,74 +929,122 @@ unsigned *device_error_ptr() {
   return cache[dev];
 }
 
+
 constexpr int GEMV_STAGE_TARGET = 24 * 1024;
+constexpr int GEMV_SMEM_BUDGET = 227 * 1024 - 1024;  // dynamic shared memory (static use is < 1 KB)
+constexpr int GEMV_RED_TARGET = 32 * 1024;
+
+size_t gemv_split_bytes(int max_ctas) {
+  return size_t(max_ctas) * sizeof(unsigned) + size_t(max_ctas) * GEMV_SPLIT_SLOT * sizeof(float) + 256;
+}
+
+GemvSplit gemv_split_view(void *base, int max_ctas) {
+  GemvSplit s;
+  s.cnt = static_cast<unsigned *>(base);
+  const size_t off = (size_t(max_ctas) * sizeof(unsigned) + 255) / 256 * 256;
+  s.part = reinterpret_cast<float *>(static_cast<char *>(base) + off);
+  s.max_ctas = max_ctas;
+  return s;
+}
+
+static GemvSplit default_split() {
+  static GemvSplit cache[64] = {};
+  GemvSplit none = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return none;
+  if (!cache[dev].cnt) {
+    void *c = nullptr, *p = nullptr;
+    if (cudaGetSymbolAddress(&c, g_gemv_cnt) != cudaSuccess || cudaGetSymbolAddress(&p, g_gemv_part) != cudaSuccess)
+      return none;
+    cache[dev].cnt = static_cast<unsigned *>(c);
+    cache[dev].part = static_cast<float *>(p);
+    cache[dev].max_ctas = GEMV_DEFAULT_SPLIT_CTAS;
+  }
+  return cache[dev];
+}
 
 template <int NMAT, int T>
-static cudaError_t launch_qgemv_t(QGemvArgs a, cudaStream_t st) {
+static cudaError_t launch_qgemv_t(QGemvArgs a, const GemvSplit &sp, cudaStream_t st) {
   auto kern = qgemv_kernel<NMAT, T>;
-  constexpr int THREADS = GemvCfg<T>::THREADS;
-  const int S = a.nb * SLICES_PER_BLOCK;
-  a.groups = THREADS / S;
-  if (a.groups < 1) return cudaErrorInvalidValue;
-  a.stage_bytes = 0;
-  a.rps_max = 0;
+  const int nb = a.nb;
+  int64_t tiles = 0;
+  int stage_bytes = 0;
+  for (int i = 0; i < a.nseg; ++i)
+    if (a.seg[i].rows <= 0) return cudaErrorInvalidValue;
   for (int i = 0; i < a.nseg; ++i) {
-    GemvSeg &sg = a.seg[i];
-    // rows per stage: a multiple of the row-group count so every group has the same rows
-    int rps = (GEMV_STAGE_TARGET / (sg.row_bytes * NMAT) + a.groups / 2) / a.groups * a.groups;
-    if (rps < a.groups) rps = a.groups;
-    sg.rps = rps;
-    if (rps * sg.row_bytes * NMAT > a.stage_bytes) a.stage_bytes = rps * sg.row_bytes * NMAT;
-    if (rps > a.rps_max) a.rps_max = rps;
+    GemvSegK &S = a.seg[i];
+    S.tile0 = int(tiles);
+    tiles += (S.rows + GEMV_TILE - 1) / GEMV_TILE;
+    int nbs = GEMV_STAGE_TARGET / (NMAT * S.rec);
+    if (nbs < 1) nbs = 1;
+    if (nbs > nb) nbs = nb;
+    S.nbs = nbs;
+    if (NMAT * nbs * S.rec > stage_bytes) stage_bytes = NMAT * nbs * S.rec;
   }
-  int64_t ctas = (a.total_rows + a.groups - 1) / a.groups;
-  if (ctas > num_sms()) ctas = num_sms();
-  // hold every row of the CTA's slab when that fits (one finalize at the end), else rps_max rows
-  const int per_row = NMAT * T * a.nb * 4;
-  const int rows_per_cta = int((a.total_rows + ctas - 1) / ctas);
-  a.rcap = rows_per_cta * per_row <= 32 * 1024 ? rows_per_cta : a.rps_max;
-  if (a.rcap < a.rps_max) a.rcap = a.rps_max;
-  const int budget = 200 * 1024;  // one CTA per SM (the register file is full)
-  int red_bytes = a.rcap * per_row;
-  const int rec_bytes = T * a.nb * SLICES_PER_BLOCK * XREC_WORDS * 4;
-  if (rec_bytes > red_bytes) red_bytes = rec_bytes;
-  red_bytes = (red_bytes + 127) / 128 * 128;
-  a.red_bytes = red_bytes;
-  int nst = (budget - 128 - red_bytes) / a.stage_bytes;
-  if (nst > 8) nst = 8;
+  if (tiles * nb >= (int64_t(1) << 30)) return cudaErrorInvalidValue;
+  a.units = int(tiles * nb);
+  a.stage_bytes = stage_bytes;
+  // Grid: every CTA holds at least one tile's worth of units (a tile is then shared by at most
+  // two CTAs) and touches at most lt_cap tiles (the partial-sum buffer).
+  const int64_t tile_red = int64_t(GEMV_TILE) * NMAT * T * nb * 4;
+  int64_t lt_cap = GEMV_RED_TARGET / tile_red;
+  if (lt_cap < 3) lt_cap = 3;
+  int64_t G = tiles < num_sms() ? tiles : num_sms();
+  const int64_t g_min = (tiles + lt_cap - 3) / (lt_cap - 2);
+  if (G < g_min) G = g_min;
+  if (G > sp.max_ctas || !sp.cnt || !sp.part) return cudaErrorInvalidValue;
+  a.uq = int(a.units / G);
+  a.ur = int(a.units % G);
+  const int64_t max_units = (a.units + G - 1) / G;
+  const int64_t lt_max = (max_units + nb - 1) / nb + 1;
+  const int red_bytes = int((lt_max * tile_red + 127) / 128 * 128);
+  a.red_off = 256;  // barriers: full[12], empty[12]
+  a.x_off = a.red_off + red_bytes;
+  a.ring_off = a.x_off + (gemv_x_bytes(nb, T) + 127) / 128 * 128;
+  int nst = (GEMV_SMEM_BUDGET - a.ring_off) / stage_bytes;
+  if (nst > GEMV_MAX_STAGES) nst = GEMV_MAX_STAGES;
   if (nst < 1) return cudaErrorInvalidValue;
   a.nstage = nst;
-  const size_t smem = 128 + red_bytes + size_t(nst) * a.stage_bytes;
+  a.cnt = sp.cnt;
+  a.part = sp.part;
+  const size_t smem = size_t(a.ring_off) + size_t(nst) * stage_bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, dim3(unsigned(ctas)), dim3(a.groups * S), smem, st, a);
+  return launch_pdl(kern, dim3(unsigned(G)), dim3(GEMV_THREADS), smem, st, a);
 }
 
 template <int NMAT>
-static cudaError_t launch_qgemv_n(const QGemvArgs &a, int T, cudaStream_t st) {
+static cudaError_t launch_qgemv_n(const QGemvArgs &a, int T, const GemvSplit &sp, cudaStream_t st) {
   switch (T) {
-    case 1: return launch_qgemv_t<NMAT, 1>(a, st);
-    default: return launch_qgemv_t<NMAT, 2>(a, st);
+    case 1: return launch_qgemv_t<NMAT, 1>(a, sp, st);
+    default: return launch_qgemv_t<NMAT, 2>(a, sp, st);
   }
 }
 
 cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvPrologue pro, int64_t n_tok,
-                       cudaStream_t st) {
+                       cudaStream_t st, const GemvSplit *split) {
   if (n_tok <= 0) return cudaSuccess;
-  if (nseg < 1 || nseg > MAX_SEG || (nmat != 1 && nmat != 2)) return cudaErrorInvalidValue;
-  if (K % QK_K || K / QK_K * SLICES_PER_BLOCK > 320) return cudaErrorInvalidValue;
+  if (nseg < 1 || nseg > GEMV_MAX_SEG || (nmat != 1 && nmat != 2)) return cudaErrorInvalidValue;
+  if (K % QK_K || K / QK_K > 64) return cudaErrorInvalidValue;
+  const GemvSplit sp = split ? *split : default_split();
   QGemvArgs a = {};
   a.nseg = nseg;
   a.nb = int(K / QK_K);
   a.err = device_error_ptr();
   a.pro = pro;
   for (int i = 0; i < nseg; ++i) {
-    GemvSeg sg = segs[i];
+    const GemvSeg &sg = segs[i];
     if (sg.type != T_Q4_K && sg.type != T_Q6_K) return cudaErrorInvalidValue;
-    if (!sg.w[0] || (nmat == 2 && !sg.w[1]) || sg.rows <= 0) return cudaErrorInvalidValue;
-    sg.row_bytes = device_row_bytes(sg.type, K);
-    a.seg[i] = sg;
-    a.total_rows += sg.rows;
+    if (!sg.w[0] || (nmat == 2 && !sg.w[1]) || sg.rows <= 0 || sg.rows >= (int64_t(1) << 30))
+      return cudaErrorInvalidValue;
+    GemvSegK &S = a.seg[i];
+    S.w[0] = sg.w[0];
+    S.w[1] = sg.w[1];
+    S.y = sg.y;
+    S.rows = int(sg.rows);
+    S.type = sg.type;
+    S.rec = kquant_rec_bytes(sg.type);
+    S.ldy = sg.ldy;
   }
   for (int64_t t0 = 0; t0 < n_tok; t0 += GEMV_MAX_T) {
     const int T = int(n_tok - t0 < GEMV_MAX_T ? n_tok - t0 : GEMV_MAX_T);
@@ -709,7 +1054,7 @@ cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvP
     if (c.pro.resid_in) c.pro.resid_in += t0 * K;
     if (c.pro.resid_out) c.pro.resid_out += t0 * K;
     for (int i = 0; i < nseg; ++i) c.seg[i].y += t0 * c.seg[i].ldy;
-    const cudaError_t e = nmat == 2 ? launch_qgemv_n<2>(c, T, st) : launch_qgemv_n<1>(c, T, st);
+    const cudaError_t e = nmat == 2 ? launch_qgemv_n<2>(c, T, sp, st) : launch_qgemv_n<1>(c, T, sp, st);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -761,13 +1106,13 @@ cudaError_t dequantize(int type, const void *w, int64_t n_rows, int64_t K, float
 }
 
 cudaError_t prepare_weights(int type, const void *gguf, int64_t rows, int64_t K, void *dst, cudaStream_t st) {
-  if (type == T_Q6_K) {
-    if (K % QK_K) return cudaErrorInvalidValue;
+  if (type == T_Q4_K || type == T_Q6_K) {
+    if (K <= 0 || K % QK_K) return cudaErrorInvalidValue;
     const int nb = int(K / QK_K);
-    const int64_t nblk = rows * nb;
-    if (nblk == 0) return cudaSuccess;
-    repack_q6k_kernel<<<unsigned((nblk + 127) / 128), 128, 0, st>>>(
-        static_cast<const uint8_t *>(gguf), rows, nb, device_row_bytes(type, K), static_cast<uint8_t *>(dst));
+    const int64_t threads = (rows + KQ_TILE - 1) / KQ_TILE * nb * KQ_TILE;
+    if (threads == 0) return cudaSuccess;
+    repack_kquant_kernel<<<unsigned((threads + 255) / 256), 256, 0, st>>>(type, static_cast<const uint8_t *>(gguf),
+                                                                           rows, nb, static_cast<uint8_t *>(dst));
     return cudaGetLastError();
   }
   const int rb = device_row_bytes(type, K);

@@ -43,7 +43,9 @@ cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_
 unsigned *device_error_ptr();
 
 // ---- weights (gemv.cu)
-int device_row_bytes(int type, int64_t K);  // bytes per row in the device layout
+int device_row_bytes(int type, int64_t K);  // bytes per row (K-quants: of the GGUF row; their device
+                                            // layout is tiled, see common.cuh)
+int64_t device_tensor_bytes(int type, int64_t rows, int64_t K);  // bytes of `rows` rows in the device layout
 int gguf_row_bytes(int type, int64_t K);
 cudaError_t prepare_weights(int type, const void *gguf, int64_t rows, int64_t K, void *dst, cudaStream_t st);
 cudaError_t dequantize(int type, const void *w_gguf, int64_t n_rows, int64_t K, float *out, cudaStream_t st);
@@ -57,8 +59,6 @@ struct GemvSeg {
   float *y;             // output rows [T][ldy]
   int64_t rows;
   int type;             // T_Q4_K or T_Q6_K
-  int row_bytes;        // filled by the launcher
-  int rps;              // rows per stage, filled by the launcher
   int ldy;
 };
 // How the launch forms x:  mode 0: x given;  mode 1: x = rms_norm(a) * w_next;
@@ -71,9 +71,20 @@ struct GemvPrologue {
   const float *w_post, *scale, *w_next;
   float eps;
 };
+// Boundary buffers of the GEMV: a 16-row tile cut between two CTAs is summed by the second CTA
+// to arrive.  cnt must start zeroed (each launch leaves it zeroed); launches that run at the same
+// time on one device need separate buffers.  max_ctas bounds the grid.
+struct GemvSplit {
+  unsigned *cnt;
+  float *part;
+  int max_ctas;
+};
+size_t gemv_split_bytes(int max_ctas);
+GemvSplit gemv_split_view(void *base, int max_ctas);  // base: gemv_split_bytes(max_ctas) bytes
 // K-quant GEMV over 1..3 segments (nmat = 2: every segment is a gate/up pair with GeGLU).
+// split == nullptr uses the module's own buffers (shared by every caller on the device).
 cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvPrologue pro, int64_t n_tok,
-                       cudaStream_t st);
+                       cudaStream_t st, const GemvSplit *split = nullptr);
 
 // ---- elementwise / norms / attention (ops.cu)
 // out[t] = rms_norm(x[t]) * w   (real_math.rs:30-47)

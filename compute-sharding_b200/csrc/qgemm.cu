@@ -50,7 +50,7 @@ constexpr int QG_RST = 2;        // raw-block ring slots
 constexpr int QG_THREADS = 352;
 constexpr int QG_A_BYTES = QG_M * 128;  // one A tile: 128 rows x 64 fp16
 constexpr int QG_A_SLOT = 2 * QG_A_BYTES;  // one A ring slot: Q4_K two chunks, Q6_K one chunk's two tiles
-constexpr int QG_RAW_BYTES = QG_M * 208;  // largest raw block of 128 rows (Q6_K ql+qh+sc)
+constexpr int QG_RAW_BYTES = (QG_M / KQ_TILE) * REC_Q6_K;  // one block of 128 rows: 8 tiled records
 constexpr int QG_MAX_NB = 64;    // K <= 16384
 constexpr int QG_META = 9;       // per (token, block): s and 8 sub-block sums
 constexpr int QG_MAX_SEG = 3;
@@ -61,7 +61,7 @@ __host__ __device__ constexpr int qg_b_slots(int tn) {
 }
 
 struct QGemmSeg {
-  CUtensorMap map[4];  // Q4_K: [0] blocks; Q6_K: [0] ql, [1] qh, [2] scales, [3] d of all blocks
+  CUtensorMap map[4];  // K-quants: [0] tiled records; fp16: [0] rows
   float *y;
   int64_t ldy;
   int rows;
@@ -95,6 +95,21 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
                "r"(x), "r"(y)
+               : "memory");
+}
+
+// K-quant records of 8 consecutive 16-row tiles for one block: map [tile][block][chunk][bytes]
+__device__ __forceinline__ void tma_load_rec(void *dst, const CUtensorMap *map, int block, int tile, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(block), "r"(tile), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_rec(const CUtensorMap *map, int block, int tile) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(0), "r"(0), "r"(block), "r"(tile)
                : "memory");
 }
 
@@ -214,13 +229,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   uint8_t *sA = smem;                                  // [2][QG_A_SLOT]
   uint8_t *sB = sA + QG_AST * QG_A_BYTES;              // [BST][B_BYTES]
   uint8_t *sRaw = sB + BST * B_BYTES;                  // [QG_RST][QG_RAW_BYTES]
-  uint8_t *sD = sRaw + QG_RST * QG_RAW_BYTES;          // Q6_K d of all blocks: [128][<= 128 B]
-  float *sBm = reinterpret_cast<float *>(sD + QG_M * 128);  // [4][9][TN]
+  float *sBm = reinterpret_cast<float *>(sRaw + QG_RST * QG_RAW_BYTES);  // [4][9][TN]
   float *sRm = sBm + 4 * QG_META * TN;                 // [2][128][10]
   uint64_t *bars = reinterpret_cast<uint64_t *>(sRm + 2 * QG_M * 10);
   uint64_t *a_full = bars, *a_empty = bars + 4, *b_full = bars + 8, *b_empty = bars + 24;
   uint64_t *raw_full = bars + 40, *raw_empty = bars + 42, *acc_full = bars + 44, *acc_empty = bars + 46;
-  uint64_t *bm_full = bars + 48, *bm_empty = bars + 52, *rm_full = bars + 56, *d_full = bars + 58;
+  uint64_t *bm_full = bars + 48, *bm_empty = bars + 52, *rm_full = bars + 56;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 59);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -237,8 +251,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
   const int nbl = int(int64_t(nb) * (blockIdx.z + 1) / gridDim.z) - kbeg;
   const bool q6 = S.type == T_Q6_K;
   const bool f16 = S.type == T_F16;  // fp16 weights (the tied embedding): A tiles come straight from TMA
-  const int raw_bytes = q6 ? QG_M * 208 : QG_M * BLOCK_Q4_K;
-  const int dbox = (2 * nb + 15) / 16 * 16;
+  const int raw_bytes = (QG_M / KQ_TILE) * kquant_rec_bytes(S.type);
   // A ring: 2 slots of 32 KB, one MMA step each: Q4_K two 64-element chunks, Q6_K one chunk as its
   // two tiles (16*sh*(q-32) and sl*(q-32))
   const int spb = q6 ? 4 : 2;   // MMA steps (8 MMAs, one barrier handoff each) per 256-element block
@@ -262,7 +275,6 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       mbar_init(&acc_empty[i], 8);
       mbar_init(&rm_full[i], 4);
     }
-    mbar_init(d_full, 1);
     fence_mbar_init();
   }
   if (warp == 0) {  // TMEM for two accumulators of N fp32 columns
@@ -278,35 +290,17 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
 
   auto prefetch_raw_l2 = [&](int kb) {
     if (kb >= nbl) return;
-    const int kg = kbeg + kb;
-    if (!q6) {
-      tma_prefetch_2d(&S.map[0], kg * BLOCK_Q4_K, row0);
-    } else {
-      tma_prefetch_2d(&S.map[0], kg * 128, row0);
-      tma_prefetch_2d(&S.map[1], nb * 128 + kg * 64, row0);
-      tma_prefetch_2d(&S.map[2], nb * 192 + kg * 16, row0);
-    }
+    tma_prefetch_rec(&S.map[0], kbeg + kb, row0 / KQ_TILE);
   };
+  // one block of the 128-row tile: the tiled records of its 8 16-row tiles, [8][record]
   auto issue_raw = [&](int kb) {
     const int rs = kb & 1;
     prefetch_raw_l2(kb + QG_RST);
-    uint8_t *dst = sRaw + rs * QG_RAW_BYTES;
     mbar_arrive_expect_tx(&raw_full[rs], uint32_t(raw_bytes));
-    const int kg = kbeg + kb;
-    if (!q6) {
-      tma_load_2d(dst, &S.map[0], kg * BLOCK_Q4_K, row0, &raw_full[rs]);
-    } else {
-      tma_load_2d(dst, &S.map[0], kg * 128, row0, &raw_full[rs]);                       // ql [128][128]
-      tma_load_2d(dst + QG_M * 128, &S.map[1], nb * 128 + kg * 64, row0, &raw_full[rs]);  // qh [128][64]
-      tma_load_2d(dst + QG_M * 192, &S.map[2], nb * 192 + kg * 16, row0, &raw_full[rs]); // sc [128][16]
-    }
+    tma_load_rec(sRaw + rs * QG_RAW_BYTES, &S.map[0], kbeg + kb, row0 / KQ_TILE, &raw_full[rs]);
   };
   // weights never depend on the previous kernel: start them before the dependency wait
   if (warp == 8 && lane == 0) {
-    if (q6) {
-      mbar_arrive_expect_tx(d_full, uint32_t(QG_M * dbox));
-      tma_load_2d(sD, &S.map[3], nb * 208, row0, d_full);
-    }
     if (!f16)
       for (int kb = 0; kb < nbl && kb < QG_RST; ++kb) issue_raw(kb);
   }
@@ -448,16 +442,18 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
       }
     };
 
-    if (q6) mbar_wait_bounded(d_full, 0, a.err);
     if (f16 && epi)
       for (int kb = 0; kb + 1 < nbl; ++kb) epilogue(kb);  // no dequant work: the epilogue only
     for (int kb = 0; kb < (f16 ? 0 : nbl); ++kb) {
       const int rs = kb & 1, ph = (kb >> 1) & 1;
       mbar_wait_bounded(&raw_full[rs], ph, a.err);
       const uint8_t *raw = sRaw + rs * QG_RAW_BYTES;
+      // row r of the 128-row tile: record r/16, row rr = r%16 of it (chunk swizzles: common.cuh)
+      const int rr = r & (KQ_TILE - 1);
+      const uint8_t *rec = raw + (r / KQ_TILE) * (q6 ? REC_Q6_K : REC_Q4_K);
       uint32_t scw[4];  // Q4_K: sc of sub-blocks 0-3 / 4-7 as bytes (scw[0], scw[1]); Q6_K: 16 int8 scales
       if (!q6) {
-        const uint4 hd = *reinterpret_cast<const uint4 *>(raw + r * BLOCK_Q4_K);
+        const uint4 hd = *reinterpret_cast<const uint4 *>(rec + 16 * rr);
         // get_scale_min_k4 (quants.rs:252-261) for sub-blocks 0..7
         scw[0] = hd.y & 0x3F3F3F3Fu;
         scw[1] = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
@@ -479,14 +475,14 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
           if (lane == 0) mbar_arrive(&rm_full[kb & 1]);
         }
       } else {
-        const uint4 sv = *reinterpret_cast<const uint4 *>(raw + QG_M * 192 + r * 16);
+        const uint4 sv = *reinterpret_cast<const uint4 *>(rec + 3072 + 16 * rr);
         scw[0] = sv.x;
         scw[1] = sv.y;
         scw[2] = sv.z;
         scw[3] = sv.w;
         if (part == 0) {
           warp_wait(&acc_empty[kb & 1], ph ^ 1, a.err);
-          sRm[((kb & 1) * QG_M + r) * 10] = h2f_bits(*reinterpret_cast<const uint16_t *>(sD + r * dbox + (kbeg + kb) * 2));
+          sRm[((kb & 1) * QG_M + r) * 10] = h2f_bits(*reinterpret_cast<const uint16_t *>(rec + 3328 + 2 * rr));
           __syncwarp();
           if (lane == 0) mbar_arrive(&rm_full[kb & 1]);
         }
@@ -501,7 +497,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
           // chunk c = elements 64c..64c+63: low nibbles of qs[32c..32c+31] (sub-block 2c) are
           // elements 0-31, high nibbles (sub-block 2c+1) elements 32-63.  This thread: bytes
           // 16*part..16*part+15, i.e. pieces 2part, 2part+1 of each half.
-          const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * BLOCK_Q4_K + 16 + 32 * c + 16 * part);
+          const uint4 w = *reinterpret_cast<const uint4 *>(rec + 256 + 128 * rr + 16 * ((2 * c + part) ^ (rr & 7)));
           const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -530,12 +526,14 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const __grid_const
           // thread: l = 16*part..16*part+15 of both.  sc*(q-32) = 16*sh*(q-32) + sl*(q-32) with
           // sc = 16*sh + sl, sl in [0, 15]: both products are exact in fp16 and go to the two A tiles.
           const int n = c >> 1, odd = c & 1;
-          const uint4 qhv = *reinterpret_cast<const uint4 *>(raw + QG_M * 128 + r * 64 + 32 * n + 16 * part);
+          const uint4 qhv =
+              *reinterpret_cast<const uint4 *>(rec + 2048 + 64 * rr + 16 * ((2 * n + part) ^ ((rr >> 1) & 3)));
           const uint32_t hwv[4] = {qhv.x, qhv.y, qhv.z, qhv.w};
           const __half2 c1056 = __half2half2(__ushort_as_half(0x6420u));  // 1056.0
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const uint4 qlv = *reinterpret_cast<const uint4 *>(raw + r * 128 + 64 * n + 32 * h + 16 * part);
+            const uint4 qlv =
+                *reinterpret_cast<const uint4 *>(rec + 128 * rr + 16 * ((4 * n + 2 * h + part) ^ (rr & 7)));
             const uint32_t lwv[4] = {qlv.x, qlv.y, qlv.z, qlv.w};
             const int shift_l = odd ? 4 : 0;
             const int shift_h = 2 * (2 * odd + h);
@@ -774,15 +772,20 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2D uint8 view [rows][row_bytes] of a weight tensor, box = box_x bytes x 128 rows
-static bool make_map(CUtensorMap *m, const void *base, int64_t row_bytes, int64_t rows, int box_x) {
+// Tiled K-quant records as a 4D uint8 view [tile][block][rec/row_x][row_x] (row_x = 256 B for Q4_K,
+// 240 B for Q6_K), box = one block's records of 8 tiles (128 weight rows); tiles past the end read
+// as zeros.
+static bool make_map_rec(CUtensorMap *m, const void *base, int type, int64_t rows, int nb) {
   auto fn = encode_fn();
   if (!fn) return false;
-  const cuuint64_t dims[2] = {cuuint64_t(row_bytes), cuuint64_t(rows)};
-  const cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
-  const cuuint32_t box[2] = {cuuint32_t(box_x), cuuint32_t(QG_M)};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+  const int rec = kquant_rec_bytes(type);
+  const int row_x = type == T_Q4_K ? 256 : 240;
+  const cuuint64_t ntiles = cuuint64_t((rows + KQ_TILE - 1) / KQ_TILE);
+  const cuuint64_t dims[4] = {cuuint64_t(row_x), cuuint64_t(rec / row_x), cuuint64_t(nb), ntiles};
+  const cuuint64_t strides[3] = {cuuint64_t(row_x), cuuint64_t(rec), cuuint64_t(rec) * nb};
+  const cuuint32_t box[4] = {cuuint32_t(row_x), cuuint32_t(rec / row_x), 1, cuuint32_t(QG_M / KQ_TILE)};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -825,17 +828,8 @@ static bool weight_maps(int type, const void *w, int64_t rows, int64_t K, CUtens
   if (it == cache.end()) {
     MapSet s;
     memset(&s, 0, sizeof(s));
-    const int64_t rb = device_row_bytes(type, K);
     const int nb = int(K / QK_K);
-    bool ok;
-    if (type == T_F16) {
-      ok = make_map_f16(&s.map[0], w, K, rows);
-    } else if (type == T_Q4_K) {
-      ok = make_map(&s.map[0], w, rb, rows, BLOCK_Q4_K);
-    } else {
-      ok = make_map(&s.map[0], w, rb, rows, 128) && make_map(&s.map[1], w, rb, rows, 64) &&
-           make_map(&s.map[2], w, rb, rows, 16) && make_map(&s.map[3], w, rb, rows, (2 * nb + 15) / 16 * 16);
-    }
+    const bool ok = type == T_F16 ? make_map_f16(&s.map[0], w, K, rows) : make_map_rec(&s.map[0], w, type, rows, nb);
     if (!ok) return false;
     it = cache.emplace(key, s).first;
   }
@@ -845,7 +839,7 @@ static bool weight_maps(int type, const void *w, int64_t rows, int64_t K, CUtens
 
 static size_t qgemm_smem(int TN) {
   return 1024 + size_t(QG_AST) * QG_A_BYTES + size_t(qg_b_slots(TN)) * 2 * TN * 128 + size_t(QG_RST) * QG_RAW_BYTES +
-         QG_M * 128 + 4 * QG_META * TN * 4 + 2 * QG_M * 10 * 4 + 60 * 8;
+         4 * QG_META * TN * 4 + 2 * QG_M * 10 * 4 + 60 * 8;
 }
 
 // Token-tile width: the largest of 64/32/16/8 that still gives every SM a CTA, else 8.

@@ -270,6 +270,8 @@ struct sfc_stage {
   SeqInfo *seq_dev = nullptr;
   void *scratch = nullptr;
   unsigned *attn_counters = nullptr;  // decode attention split counters, [max_batch][n_kv], kept zero
+  void *gemv_split_mem = nullptr;     // GEMV tile-boundary counters (kept zero) and partial sums
+  GemvSplit gemv_split = {};
   // tensor-core GEMM path for 8+ rows (K-quant stages): operand-B staging and the up-projection
   bool gemm_ok = false;
   void *gemm_scratch = nullptr;
@@ -372,10 +374,10 @@ int64_t gguf_tensor_bytes(int type, const std::vector<int64_t> &dims) {
 }
 
 int64_t device_tensor_bytes(int type, const std::vector<int64_t> &dims) {
+  if (dims.empty()) return -1;
   int64_t rows = 1;
   for (size_t i = 1; i < dims.size(); ++i) rows *= dims[i];
-  const int rb = device_row_bytes(type, dims[0]);
-  return rb < 0 ? -1 : rb * rows;
+  return ::sfc::device_tensor_bytes(type, rows, dims[0]);
 }
 
 int apply_options(sfc_stage *h, const sfc_options *o) {
@@ -556,7 +558,7 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
       SFC_CUDA(cudaMemcpy(dt->dev, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice));
       continue;
     }
-    const bool needs_repack = ht->type == T_Q6_K;
+    const bool needs_repack = ht->type == T_Q4_K || ht->type == T_Q6_K;  // tiled device layout
     if (ht->synthetic) {
       if (!needs_repack) {
         SFC_CUDA(synth_tensor(ht->type, ht->key, dt->rows, dt->in_dim, ht->sigma, ht->mean, dt->dev, h->stream));
@@ -636,6 +638,10 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   h->logit_scratch = logits_scratch_bytes(T);
   if ((rc = alloc(&h->scratch, int64_t(std::max(h->attn_scratch, h->logit_scratch))))) return rc;
   if ((rc = alloc((void **)&h->attn_counters, T * ap.n_kv * 4))) return rc;
+  constexpr int kGemvSplitCtas = 1024;
+  if ((rc = alloc(&h->gemv_split_mem, int64_t(gemv_split_bytes(kGemvSplitCtas))))) return rc;
+  h->gemv_split = gemv_split_view(h->gemv_split_mem, kGemvSplitCtas);
+  SFC_CUDA(cudaMemset(h->gemv_split_mem, 0, gemv_split_bytes(kGemvSplitCtas)));
   if (h->fused && T >= QGEMM_MIN_TOKENS) {
     bool ok = true;
     for (const Layer &L : h->layers)
@@ -681,7 +687,7 @@ void destroy_stage(sfc_stage *h) {
   for (void *p : {(void *)h->resid, (void *)h->resid2, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
-                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
+                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemv_split_mem, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
                   (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores, (void *)h->logit_scores,
                   h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
@@ -863,7 +869,7 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
     }
     const GemvSeg qkv[3] = {seg_of(L.q, nullptr, h->q, h->q_dim), seg_of(L.k, nullptr, h->k, h->k_dim),
                             seg_of(L.v, nullptr, h->v, h->k_dim)};
-    if ((e = gemv_fused(qkv, 3, 1, H, pro, T, st))) return e;
+    if ((e = gemv_fused(qkv, 3, 1, H, pro, T, st, &h->gemv_split))) return e;
     const AttnParams ap = attn_params(h, L);
     const KVLayer kv = kv_layer(h, li);
     if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
@@ -871,7 +877,7 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
     GemvPrologue po = {};
     po.mode = 0;
     po.x = h->att;
-    if ((e = gemv_fused(&o, 1, 1, h->q_dim, po, T, st))) return e;
+    if ((e = gemv_fused(&o, 1, 1, h->q_dim, po, T, st, &h->gemv_split))) return e;
     GemvPrologue pf = {};
     pf.mode = 2;
     pf.eps = h->eps;
@@ -882,12 +888,12 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
     pf.w_next = F32P(L.ffn_norm);
     std::swap(cur, other);
     const GemvSeg gu = seg_of(L.gate, L.up, h->act, h->ffn);
-    if ((e = gemv_fused(&gu, 1, 2, H, pf, T, st))) return e;
+    if ((e = gemv_fused(&gu, 1, 2, H, pf, T, st, &h->gemv_split))) return e;
     const GemvSeg d = seg_of(L.down, nullptr, h->proj, H);
     GemvPrologue pd = {};
     pd.mode = 0;
     pd.x = h->act;
-    if ((e = gemv_fused(&d, 1, 1, h->ffn, pd, T, st))) return e;
+    if ((e = gemv_fused(&d, 1, 1, h->ffn, pd, T, st, &h->gemv_split))) return e;
   }
   const Layer &Z = h->layers.back();
   if ((e = add_norm(cur, h->proj, F32P(Z.post_ffw), F32P(Z.scale), 0, nullptr, nullptr, T, H, h->eps, st))) return e;

@@ -18,7 +18,7 @@ import argparse
 import numpy as np
 import torch
 
-from . import Q4_K, CudaStageBackend, ModelShape, lib, synth_tensor
+from . import Q4_K, CudaStageBackend, ModelShape, lib, prepare_weights, synth_tensor
 
 
 def run_decode(steps: int, ctx: int, batch: int):
@@ -48,7 +48,7 @@ def run_gemv(launches: int, tokens: int = 1):
     rows, k = 10240, 2560
     wbytes = rows * (k // 256) * 144
     copies = int(np.ceil(2 * (126 << 20) / wbytes)) + 2
-    ws = [synth_tensor(Q4_K, 1, f"gemv.{i}", rows, k, 0.02) for i in range(copies)]
+    ws = [prepare_weights(Q4_K, synth_tensor(Q4_K, 1, f"gemv.{i}", rows, k, 0.02), rows, k) for i in range(copies)]
     x = torch.randn(tokens, k, device=dev)
     y = torch.empty(tokens, rows, device=dev)
     st = torch.cuda.current_stream().cuda_stream

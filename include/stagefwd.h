@@ -52,8 +52,10 @@ int64_t sfc_kernel_launches(void);
 
 /* ------------------------------------------------------------------ kernel-level API
  * Device pointers, caller's stream.  Weights for sfc_matmul* must be in the device layout
- * produced by sfc_prepare_weights (identical to GGUF for F32/F16/BF16/Q4_K; Q6_K rows are
- * re-laid out field-by-field so every field is 16-byte aligned).                        */
+ * produced by sfc_prepare_weights: identical to GGUF for F32/F16/BF16; Q4_K and Q6_K rows are
+ * grouped in tiles of 16 (zero-padded) with one contiguous record per (tile, 256-element block)
+ * holding the 16 rows' scales and quants field by field, so a tile's run of blocks is a single
+ * bulk copy for the GEMV and a single tensor copy for the GEMM.                          */
 
 /* Bytes of `rows` rows in the device layout. <0 on unsupported type/shape. */
 int64_t sfc_weight_device_bytes(int ggml_type, int64_t rows, int64_t in_dim);

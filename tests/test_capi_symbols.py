@@ -41,8 +41,12 @@ def test_host_validation_without_gpu():
     assert b"unsupported ggml type 13" in sf.lib.sfc_last_error()
     assert sf.lib.sfc_matmul(12, None, 4, 100, None, 1, None, None) == -1
     assert sf.lib.sfc_dequantize_rows(1, None, 1, 256, None, None) == -1
-    assert sf.lib.sfc_weight_device_bytes(14, 10, 2560) == 10 * 2112
-    assert sf.lib.sfc_weight_device_bytes(12, 10, 2560) == 10 * 1440
+    # K-quants: tiles of 16 rows (zero-padded), one record per (tile, 256-block): Q6_K 3360 B, Q4_K 2304 B
+    assert sf.lib.sfc_weight_device_bytes(14, 10, 2560) == 1 * 10 * 3360
+    assert sf.lib.sfc_weight_device_bytes(14, 32, 2560) == 2 * 10 * 3360
+    assert sf.lib.sfc_weight_device_bytes(12, 10, 2560) == 1 * 10 * 2304
+    assert sf.lib.sfc_weight_device_bytes(12, 17, 512) == 2 * 2 * 2304
+    assert sf.lib.sfc_weight_device_bytes(1, 10, 2560) == 10 * 2560 * 2
 
 
 def test_stage_open_rejects_bad_index_name(tmp_path):
