@@ -17,7 +17,9 @@
 //  * Warp w takes keys 4w..4w+3 of every 32-key tile: lane l holds dims 8l..8l+7, scores are
 //    warp sums, and one online-softmax update per 4 keys.  Warps merge in a fixed order.
 //  * Splits write (max, sum, acc) partials; the last CTA of a (sequence, kv head) to finish
-//    (atomic counter) merges them in split order — deterministic, and no combine launch.
+//    (atomic counter) merges them in split order — deterministic, and no combine launch.  The merge
+//    stages every split's (max, sum) in shared memory at once and folds the partial vectors with
+//    the split loop unrolled, so its L2 reads overlap instead of queueing one latency per split.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -30,7 +32,8 @@ constexpr int DA_WARPS = 8;
 constexpr int DA_THREADS = DA_WARPS * 32;
 constexpr int DA_MAXG = 4;  // query heads per kv head handled here (registers hold q and acc per head)
 constexpr int DA_MAX_HD = 256;
-constexpr int DA_MIN_CHUNK = 32;  // keys per split at least
+constexpr int DA_MIN_CHUNK = 64;  // keys per split at least
+constexpr int DA_MAX_SPLIT = 32;  // key splits per (sequence, kv head) at most
 constexpr int DA_STAGES = 3;
 constexpr int DA_TILE_BYTES = 32 * DA_MAX_HD * 2;  // K or V of one tile: 32 fp16 keys (16 f32 keys)
 
@@ -79,6 +82,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   __shared__ float s_red[DA_MAXG + 2][DA_WARPS];
   __shared__ float s_m[DA_WARPS][DA_MAXG], s_l[DA_WARPS][DA_MAXG];
   __shared__ unsigned s_last;
+  __shared__ float s_f[DA_MAXG][DA_MAX_SPLIT];  // merge weights exp(m_s - M) / L per head and split
 
   const int t = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -338,20 +342,34 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   if (!s_last) return;
   __threadfence();
   // last split of this (sequence, kv head): merge all partials in split order
+  const float *pbase = part + (int64_t(t) * p.n_heads + kvh * G) * n_split * (hd + 2);
+  if (tid < G * n_eff) {  // (max, sum) of every split, loaded in parallel
+    const int g = tid / n_eff, sp = tid % n_eff;
+    s_f[g][sp] = __ldcg(pbase + (g * n_split + sp) * (hd + 2));
+    s_vec[g][sp] = __ldcg(pbase + (g * n_split + sp) * (hd + 2) + 1);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float mm = -INFINITY;
+    for (int sp = 0; sp < n_eff; ++sp) mm = fmaxf(mm, s_f[tid][sp]);
+    float ll = 0.f;
+    for (int sp = 0; sp < n_eff; ++sp) {
+      const float ms = s_f[tid][sp];
+      const float f = ms == -INFINITY ? 0.f : expf(ms - mm);
+      s_f[tid][sp] = f;
+      ll += s_vec[tid][sp] * f;
+    }
+    const float inv = ll > 0.f ? 1.0f / ll : 0.f;
+    for (int sp = 0; sp < n_eff; ++sp) s_f[tid][sp] *= inv;
+  }
+  __syncthreads();
   for (int idx = tid; idx < G * hd; idx += DA_THREADS) {
     const int g = idx / hd, d = idx % hd;
-    const float *pp = part + (int64_t(t) * p.n_heads + kvh * G + g) * n_split * (hd + 2);
-    float mm = -INFINITY;
-    for (int s = 0; s < n_eff; ++s) mm = fmaxf(mm, __ldcg(pp + s * (hd + 2)));
-    float ll = 0.f, a = 0.f;
-    for (int s = 0; s < n_eff; ++s) {
-      const float ms = __ldcg(pp + s * (hd + 2));
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - mm);
-      ll += __ldcg(pp + s * (hd + 2) + 1) * f;
-      a += __ldcg(pp + s * (hd + 2) + 2 + d) * f;
-    }
-    out[int64_t(t) * p.n_heads * hd + (kvh * G + g) * hd + d] = ll > 0.f ? a / ll : 0.f;
+    const float *pp = pbase + g * n_split * (hd + 2) + 2 + d;
+    float a = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < n_eff; ++sp) a += s_f[g][sp] * __ldcg(pp + sp * (hd + 2));
+    out[int64_t(t) * p.n_heads * hd + (kvh * G + g) * hd + d] = a;
   }
   if (tid == 0) counters[t * p.n_kv + kvh] = 0u;  // ready for the next launch
 }
@@ -363,7 +381,7 @@ int decode_attention_splits(int64_t n_seq, const AttnParams &p, int64_t max_keys
   if (want < by_len) want = by_len;
   const int64_t cap = (max_keys + DA_MIN_CHUNK - 1) / DA_MIN_CHUNK;
   if (want > cap) want = cap;
-  if (want > 128) want = 128;
+  if (want > DA_MAX_SPLIT) want = DA_MAX_SPLIT;
   if (want < 1) want = 1;
   return int(want);
 }

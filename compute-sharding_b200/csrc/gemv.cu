@@ -26,6 +26,7 @@
 //    carries -32 x (digit sums), so the MMA returns the exact sum of (q - 32) x digits.
 #include <cuda_runtime.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -33,8 +34,10 @@
 namespace sfc {
 
 constexpr int GEMV_TILE = 16;       // weight rows per MMA tile
-constexpr int GEMV_CONSUMERS = 15;  // consumer warps per CTA (plus one producer warp: 512 threads)
-constexpr int GEMV_THREADS = (GEMV_CONSUMERS + 1) * 32;
+// Consumer warps per CTA (plus one producer warp): 15 (512 threads, one CTA per SM) or 7 (256
+// threads and at most half the shared memory, so the next launch's CTA fits beside this one and
+// streams its weights while this one computes).
+constexpr int GEMV_CW_WIDE = 15, GEMV_CW_HALF = 7;
 constexpr int GEMV_MAX_T = 2;
 constexpr int GEMV_MAX_STAGES = 12;
 constexpr int GEMV_MAX_SEG = 3;
@@ -102,8 +105,9 @@ __device__ __forceinline__ void mbar_arrive_cta(uint64_t *bar) {
 }
 
 // Barrier of the consumer warps only (the producer warp never joins).
+template <int CW>
 __device__ __forceinline__ void consumer_bar() {
-  asm volatile("bar.sync 1, %0;" ::"n"(GEMV_CONSUMERS * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
 }
 
 __device__ __forceinline__ float gelu_tanh_mul(float v, float u) {
@@ -423,8 +427,9 @@ struct QGemvArgs {
   int units;      // tiles * nb
   int uq, ur;     // CTA c owns units [c*uq + min(c, ur), ...), uq + (c < ur) of them
   int nstage;     // ring slots
+  int max_stages; // stage-table entries per CTA
   int stage_bytes;
-  int red_off, x_off, ring_off;  // dynamic shared-memory offsets
+  int red_off, x_off, ring_off, tab_off;  // dynamic shared-memory offsets
   GemvPrologue pro;
   unsigned *err;
   unsigned *cnt;  // per CTA boundary: arrivals of the two CTAs sharing a tile
@@ -563,11 +568,14 @@ __device__ __forceinline__ void finish_shared(const QGemvArgs &a, const CtaTiles
 }
 
 // Segments let one launch cover several matrices with the same K (q, k and v of a layer).
-template <int NMAT, int T>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs a) {
+// TYPE: the weight type of every segment (T_Q4_K / T_Q6_K), or 0 for a mix (checked per unit).
+template <int NMAT, int T, int TYPE, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, CW == GEMV_CW_HALF ? 2 : 1) qgemv_kernel(const QGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float pro_red[GEMV_MAX_T][GEMV_CONSUMERS];
-  __shared__ int s_done[2];  // finished units of the shared tiles
+  __shared__ float pro_red[GEMV_MAX_T][16];
+  __shared__ int s_tdone[2];                 // finished units of the shared tiles
+  __shared__ int s_sdone[GEMV_MAX_STAGES];  // finished units of the stage in each ring slot
+  __shared__ int s_nstages;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nb = a.nb, K = nb * QK_K;
   const int cta = int(blockIdx.x);
@@ -580,40 +588,49 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs 
   float *red = reinterpret_cast<float *>(smem + a.red_off);  // [local tile][16][NMAT][T][nb]
   const XSmem X = x_view(smem + a.x_off, nb, T);
   uint8_t *ring = smem + a.ring_off;
+  GemvStage *tab = reinterpret_cast<GemvStage *>(smem + a.tab_off);  // the CTA's stages in order
 
   if (tid == 0) {
     for (int i = 0; i < a.nstage; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], GEMV_CONSUMERS);
+      mbar_init(&empty[i], 1);  // arrived by the warp that finishes the stage's last unit
+      s_sdone[i] = 0;
     }
     fence_mbar_init();
-    s_done[0] = s_done[1] = 0;
-  }
-  __syncthreads();
-
-  if (warp == GEMV_CONSUMERS) {
-    // ---- producer: weights never depend on the previous kernel, so no dependency wait here
+    s_tdone[0] = s_tdone[1] = 0;
     StageWalk wk;
     wk.init(a, ct);
-    for (int s = 0; wk.more(ct); ++s) {
-      GemvStage st;
-      wk.next(a, ct, st);
-      const int slot = s % a.nstage;
-      if (s >= a.nstage) {
-        if (lane == 0) mbar_wait_bounded(&empty[slot], uint32_t((s / a.nstage) - 1) & 1u, a.err);
+    int n = 0;
+    while (wk.more(ct) && n < a.max_stages) wk.next(a, ct, tab[n++]);
+    if (wk.more(ct) && a.err) atomicExch(a.err, DEV_BAD_ARG);
+    s_nstages = n;
+  }
+  __syncthreads();
+  const int nstages = s_nstages;
+
+  if (warp == CW) {
+    // ---- producer: weights never depend on the previous kernel, so no dependency wait here
+    for (int s = 0, slot = 0, ph = 0; s < nstages; ++s) {
+      if (s >= a.nstage) {  // wait for the slot's previous stage to be consumed
+        if (lane == 0) mbar_wait_bounded(&empty[slot], uint32_t(ph ^ 1), a.err);
         __syncwarp();
       }
-      const GemvSegK &S = a.seg[st.sg];
-      // the stage's records of each matrix: one contiguous range
-      const uint32_t bytes = uint32_t(st.nbs) * uint32_t(S.rec);
-      const int64_t first = int64_t(st.tau - S.tile0) * nb + st.b0;
       if (lane == 0) {
+        const GemvStage st = tab[s];
+        const GemvSegK &S = a.seg[st.sg];
+        // the stage's records of each matrix: one contiguous range
+        const uint32_t bytes = uint32_t(st.nbs) * uint32_t(S.rec);
+        const int64_t first = int64_t(st.tau - S.tile0) * nb + st.b0;
         mbar_arrive_expect_tx(&full[slot], bytes * NMAT);
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
           bulk_g2s(ring + size_t(slot) * a.stage_bytes + m * S.nbs * S.rec, S.w[m] + first * S.rec, bytes, &full[slot]);
       }
       __syncwarp();
+      if (++slot == a.nstage) {
+        slot = 0;
+        ph ^= 1;
+      }
     }
     return;
   }
@@ -623,7 +640,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs 
   pdl_launch_dependents();
 
   // Activations, computed once per CTA.  Unit (token t, 256-block b) belongs to warp
-  // (t*nb + b) % 15 and lane l holds its elements 8l..8l+7, so every global access is a coalesced
+  // (t*nb + b) % CW and lane l holds its elements 8l..8l+7, so every global access is a coalesced
   // 1 KB piece of a row.  The optional fused residual add + RMSNorm passes run first.
   {
     const GemvPrologue &P = a.pro;
@@ -666,7 +683,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs 
       float part[T];
 #pragma unroll
       for (int t = 0; t < T; ++t) part[t] = 0.f;
-      for (int u = warp; u < units; u += GEMV_CONSUMERS) {
+      for (int u = warp; u < units; u += CW) {
         const int t = u / nb, b = u % nb;
         float v[8];
         value8(t, b, step, v);
@@ -681,14 +698,14 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs 
         const float w = warp_sum(part[t]);
         if (lane == 0) pro_red[t][warp] = w;
       }
-      consumer_bar();
+      consumer_bar<CW>();
 #pragma unroll
       for (int t = 0; t < T; ++t) {
         float sum = 0.f;
-        for (int w = 0; w < GEMV_CONSUMERS; ++w) sum += pro_red[t][w];
+        for (int w = 0; w < CW; ++w) sum += pro_red[t][w];
         out[t] = sum;
       }
-      consumer_bar();
+      consumer_bar<CW>();
     };
     if (P.mode != 0) {
       float tot[T];
@@ -703,62 +720,64 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) qgemv_kernel(const QGemvArgs 
         for (int t = 0; t < T; ++t) s2[t] = 1.0f / sqrtf(tot[t] / float(K) + P.eps);
       }
     }
-    for (int u = warp; u < units; u += GEMV_CONSUMERS) {
+    for (int u = warp; u < units; u += CW) {
       const int t = u / nb, b = u % nb;
       float v[8];
       value8(t, b, 2, v);
       emit_block<T>(v, lane, b, t, X);
     }
   }
-  consumer_bar();
+  consumer_bar<CW>();
 
-  // ---- units: CTA-local unit k (stage order, block fastest) belongs to consumer warp k % 15
+  // ---- units: CTA-local unit k (stage order, block fastest) belongs to consumer warp k % CW
   const int g = lane >> 2, t = lane & 3;
-  {
-    StageWalk wk;
-    wk.init(a, ct);
-    int k = warp;  // next CTA-local unit of this warp
-    for (int slot = 0, phase = 0; wk.more(ct);) {
-      GemvStage st;
-      wk.next(a, ct, st);
-      if (k < st.ks + st.nbs) {
-        mbar_wait_bounded(&full[slot], uint32_t(phase), a.err);
-        const GemvSegK &S = a.seg[st.sg];
-        const uint8_t *tile = ring + size_t(slot) * a.stage_bytes;
-        for (; k < st.ks + st.nbs; k += GEMV_CONSUMERS) {
-          const int b = st.b0 + (k - st.ks);
-          float v[NMAT][2][T];
-          if (S.type == T_Q4_K)
-            unit_q4k<NMAT, T>(tile, S.nbs * S.rec, b - st.b0, b, X, g, t, v);
-          else
-            unit_q6k<NMAT, T>(tile, S.nbs * S.rec, b - st.b0, b, X, g, t, v);
-#pragma unroll
-          for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-              for (int kk = 0; kk < T; ++kk) {
-                float x = v[m][i][kk];
-                x += __shfl_xor_sync(0xFFFFFFFFu, x, 1);
-                x += __shfl_xor_sync(0xFFFFFFFFu, x, 2);
-                if (t == 0) red[(((st.lt * GEMV_TILE + g + 8 * i) * NMAT + m) * T + kk) * nb + b] = x;
-              }
-          if (st.lt < ct.np) finish_shared<NMAT, T>(a, ct, st.lt, st.tau, cta, red, s_done, lane);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cta(&empty[slot]);
+  const int total = ct.u1 - ct.u0;
+  for (int k = warp, si = 0, slot = 0, phase = 0; k < total; k += CW) {
+    while (k >= tab[si].ks + tab[si].nbs) {
+      ++si;
       if (++slot == a.nstage) {
         slot = 0;
         phase ^= 1;
       }
     }
+    const GemvStage st = tab[si];
+    mbar_wait_bounded(&full[slot], uint32_t(phase), a.err);
+    const GemvSegK &S = a.seg[st.sg];
+    const uint8_t *tile = ring + size_t(slot) * a.stage_bytes;
+    const int b = st.b0 + (k - st.ks);
+    float v[NMAT][2][T];
+    if (TYPE == T_Q4_K || (TYPE == 0 && S.type == T_Q4_K))
+      unit_q4k<NMAT, T>(tile, S.nbs * S.rec, b - st.b0, b, X, g, t, v);
+    else
+      unit_q6k<NMAT, T>(tile, S.nbs * S.rec, b - st.b0, b, X, g, t, v);
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int kk = 0; kk < T; ++kk) {
+          float x = v[m][i][kk];
+          x += __shfl_xor_sync(0xFFFFFFFFu, x, 1);
+          x += __shfl_xor_sync(0xFFFFFFFFu, x, 2);
+          if (t == 0) red[(((st.lt * GEMV_TILE + g + 8 * i) * NMAT + m) * T + kk) * nb + b] = x;
+        }
+    // release the ring slot once every unit of its stage is done (its reads precede the count)
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&s_sdone[slot], 1) == st.nbs - 1) {
+        s_sdone[slot] = 0;
+        __threadfence_block();
+        mbar_arrive_cta(&empty[slot]);
+      }
+    }
+    if (st.lt < ct.np) finish_shared<NMAT, T>(a, ct, st.lt, st.tau, cta, red, s_tdone, lane);
   }
   if (ct.count == ct.np) return;
-  consumer_bar();
+  consumer_bar<CW>();
 
   // ---- tiles owned alone: row sums over all blocks in block order
-  for (int item = tid; item < (ct.count - ct.np) * GEMV_TILE * T; item += GEMV_CONSUMERS * 32) {
+  for (int item = tid; item < (ct.count - ct.np) * GEMV_TILE * T; item += CW * 32) {
     const int kk = item % T, row = (item / T) % GEMV_TILE, lt = ct.np + item / (T * GEMV_TILE);
     const int tau = ct.tile(lt);
     const GemvSegK &S = a.seg[seg_of_tile(a, tau)];
@@ -931,7 +950,17 @@ unsigned *device_error_ptr() {
 
 
 constexpr int GEMV_STAGE_TARGET = 24 * 1024;
-constexpr int GEMV_SMEM_BUDGET = 227 * 1024 - 1024;  // dynamic shared memory (static use is < 1 KB)
+constexpr int GEMV_SMEM_WIDE = 227 * 1024 - 1024;  // dynamic shared memory (static use is < 1 KB)
+constexpr int GEMV_SMEM_HALF = 112 * 1024 - 512;   // two CTAs per SM
+
+// Launch shape: SFC_GEMV_HALF=1 selects the two-CTAs-per-SM configuration.
+static bool gemv_half_ctas() {
+  static const int v = [] {
+    const char *e = getenv("SFC_GEMV_HALF");
+    return e && e[0] == '1' ? 1 : 0;
+  }();
+  return v != 0;
+}
 constexpr int GEMV_RED_TARGET = 32 * 1024;
 
 size_t gemv_split_bytes(int max_ctas) {
@@ -963,12 +992,13 @@ static GemvSplit default_split() {
   return cache[dev];
 }
 
-template <int NMAT, int T>
+template <int NMAT, int T, int TYPE, int CW>
 static cudaError_t launch_qgemv_t(QGemvArgs a, const GemvSplit &sp, cudaStream_t st) {
-  auto kern = qgemv_kernel<NMAT, T>;
+  auto kern = qgemv_kernel<NMAT, T, TYPE, CW>;
+  const int budget = CW == GEMV_CW_HALF ? GEMV_SMEM_HALF : GEMV_SMEM_WIDE;
   const int nb = a.nb;
   int64_t tiles = 0;
-  int stage_bytes = 0;
+  int stage_bytes = 0, nbs_min = nb;
   for (int i = 0; i < a.nseg; ++i)
     if (a.seg[i].rows <= 0) return cudaErrorInvalidValue;
   for (int i = 0; i < a.nseg; ++i) {
@@ -979,6 +1009,7 @@ static cudaError_t launch_qgemv_t(QGemvArgs a, const GemvSplit &sp, cudaStream_t
     if (nbs < 1) nbs = 1;
     if (nbs > nb) nbs = nb;
     S.nbs = nbs;
+    if (nbs < nbs_min) nbs_min = nbs;
     if (NMAT * nbs * S.rec > stage_bytes) stage_bytes = NMAT * nbs * S.rec;
   }
   if (tiles * nb >= (int64_t(1) << 30)) return cudaErrorInvalidValue;
@@ -997,28 +1028,45 @@ static cudaError_t launch_qgemv_t(QGemvArgs a, const GemvSplit &sp, cudaStream_t
   a.ur = int(a.units % G);
   const int64_t max_units = (a.units + G - 1) / G;
   const int64_t lt_max = (max_units + nb - 1) / nb + 1;
+  a.max_stages = int(max_units / nbs_min + lt_max + 1);
   const int red_bytes = int((lt_max * tile_red + 127) / 128 * 128);
   a.red_off = 256;  // barriers: full[12], empty[12]
-  a.x_off = a.red_off + red_bytes;
+  a.tab_off = a.red_off + red_bytes;
+  a.x_off = a.tab_off + (a.max_stages * int(sizeof(GemvStage)) + 127) / 128 * 128;
   a.ring_off = a.x_off + (gemv_x_bytes(nb, T) + 127) / 128 * 128;
-  int nst = (GEMV_SMEM_BUDGET - a.ring_off) / stage_bytes;
+  int nst = (budget - a.ring_off) / stage_bytes;
   if (nst > GEMV_MAX_STAGES) nst = GEMV_MAX_STAGES;
-  if (nst < 1) return cudaErrorInvalidValue;
+  if (nst < 2) return cudaErrorInvalidValue;
   a.nstage = nst;
   a.cnt = sp.cnt;
   a.part = sp.part;
   const size_t smem = size_t(a.ring_off) + size_t(nst) * stage_bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, dim3(unsigned(G)), dim3(GEMV_THREADS), smem, st, a);
+  return launch_pdl(kern, dim3(unsigned(G)), dim3((CW + 1) * 32), smem, st, a);
+}
+
+template <int NMAT, int T, int TYPE>
+static cudaError_t launch_qgemv_cw(const QGemvArgs &a, const GemvSplit &sp, cudaStream_t st) {
+  // the half-SM shape needs two ring slots beside the activations (not the case for 2 tokens at
+  // K = 10240): otherwise, and by default, one CTA per SM
+  if (gemv_half_ctas() && launch_qgemv_t<NMAT, T, TYPE, GEMV_CW_HALF>(a, sp, st) == cudaSuccess) return cudaSuccess;
+  return launch_qgemv_t<NMAT, T, TYPE, GEMV_CW_WIDE>(a, sp, st);
 }
 
 template <int NMAT>
 static cudaError_t launch_qgemv_n(const QGemvArgs &a, int T, const GemvSplit &sp, cudaStream_t st) {
-  switch (T) {
-    case 1: return launch_qgemv_t<NMAT, 1>(a, sp, st);
-    default: return launch_qgemv_t<NMAT, 2>(a, sp, st);
+  int type = a.seg[0].type;
+  for (int i = 1; i < a.nseg; ++i)
+    if (a.seg[i].type != type) type = 0;
+  if (T == 1) {
+    if (type == T_Q4_K) return launch_qgemv_cw<NMAT, 1, T_Q4_K>(a, sp, st);
+    if (type == T_Q6_K) return launch_qgemv_cw<NMAT, 1, T_Q6_K>(a, sp, st);
+    return launch_qgemv_cw<NMAT, 1, 0>(a, sp, st);
   }
+  if (type == T_Q4_K) return launch_qgemv_cw<NMAT, 2, T_Q4_K>(a, sp, st);
+  if (type == T_Q6_K) return launch_qgemv_cw<NMAT, 2, T_Q6_K>(a, sp, st);
+  return launch_qgemv_cw<NMAT, 2, 0>(a, sp, st);
 }
 
 cudaError_t gemv_fused(const GemvSeg *segs, int nseg, int nmat, int64_t K, GemvPrologue pro, int64_t n_tok,
