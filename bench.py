@@ -35,7 +35,7 @@ LAYER_WEIGHT_BYTES = 60_518_400
 EMBD_BYTES = VOCAB * HIDDEN * 2
 # dram__bytes_read.sum + dram__bytes_write.sum of one qgemv_kernel<1,1> launch on that shape, from
 # the ncu capture summarised in profiles/qgemv_q4k_10240x2560_1tok.md
-GEMV_DRAM_BYTES = 14_804_992
+GEMV_DRAM_BYTES = 14_810_368
 
 
 def bs1_config(world: int = 1) -> dict:
@@ -191,7 +191,7 @@ def gemv_roofline(sf, torch, hbm_peak):
     dur_s = e0.elapsed_time(e1) / 1e3 / n
     achieved = GEMV_BYTES / dur_s / 1e9
     del g
-    return {"kernel": "qgemv_kernel<1,1> (Q4_K 10240x2560, 1 token, weights cycled over > 2x L2)", "bound": "hbm",
+    return {"kernel": "qgemv_kernel<1,1,Q4_K,15> (Q4_K 10240x2560, 1 token, weights cycled over > 2x L2)", "bound": "hbm",
             "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
             "us_per_launch": dur_s * 1e6, "launches_timed": n, "bytes_per_launch": GEMV_BYTES,
             "traffic": GEMV_DRAM_BYTES}
