@@ -71,16 +71,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == GEMV_CW_HALF ? 2 : 1) qge
     }
     fence_mbar_init();
     s_tdone[0] = s_tdone[1] = 0;
-    s_nstages = build_stage_table(a, ct, tab);
   }
   __syncthreads();
 
   if (warp == CW) {  // producer: weights never depend on the previous kernel, so no dependency wait
-    RingPos rp = {0, 0};
-    int issued = 0;
-    produce_stages<NMAT>(a, tab, s_nstages, ring, full, empty, rp, issued, lane);
+    produce_walk<NMAT>(a, ct, ring, full, empty, lane);
     return;
   }
+  if (tid == 0) s_nstages = build_stage_table(a, ct, tab);  // the consumers' copy of the same walk
+  consumer_bar<CW>();
   pdl_wait();
   pdl_launch_dependents();
   build_x<T, CW>(a.pro, a.nb, cta, X, pro_red, warp, lane);

@@ -590,6 +590,36 @@ __device__ __forceinline__ void produce_stages(const QGemvArgs &a, const GemvSta
   }
 }
 
+// Producer warp of a one-projection launch: walks the CTA's stages itself (the same walk that fills
+// the consumers' table) so the first copies leave without waiting for the table.
+template <int NMAT>
+__device__ __forceinline__ void produce_walk(const QGemvArgs &a, const CtaTiles &ct, uint8_t *ring, uint64_t *full,
+                                             uint64_t *empty, int lane) {
+  StageWalk wk;
+  wk.init(a, ct);
+  RingPos rp = {0, 0};
+  for (int s = 0; wk.more(ct) && s < a.max_stages; ++s) {
+    GemvStage st;
+    wk.next(a, ct, st);
+    if (s >= a.nstage) {  // wait for the slot's previous stage to be consumed
+      if (lane == 0) mbar_wait_bounded(&empty[rp.slot], uint32_t(rp.phase ^ 1), a.err);
+      __syncwarp();
+    }
+    if (lane == 0) {
+      const GemvSegK &S = a.seg[st.sg];
+      const uint32_t bytes = uint32_t(st.nbs) * uint32_t(S.rec);
+      const int64_t first = int64_t(st.tau - S.tile0) * a.nb + st.b0;
+      mbar_arrive_expect_tx(&full[rp.slot], bytes * NMAT);
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+        bulk_g2s(ring + size_t(rp.slot) * a.stage_bytes + m * S.nbs * S.rec, S.w[m] + first * S.rec, bytes,
+                 &full[rp.slot]);
+    }
+    __syncwarp();
+    rp.advance(a.nstage);
+  }
+}
+
 // Activations of T tokens into the CTA's image X (consumer warps; ends with a consumer barrier).
 // Unit (token t, 256-block b) belongs to warp (t*nb + b) % CW and lane l holds its elements
 // 8l..8l+7, so every global access is a coalesced 1 KB piece of a row.  The optional fused
