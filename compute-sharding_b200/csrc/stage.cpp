@@ -907,7 +907,7 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
       in.hidden = H;
       in.q_dim = h->q_dim;
       in.ffn = h->ffn;
-      in.max_keys = max_keys;
+      in.max_keys = h->max_ctx;  // the split count is fixed per stage (the decode graph is captured once)
       in.q = h->q;
       in.k = h->k;
       in.v = h->v;
