@@ -1,12 +1,12 @@
 // noalloc.cu — logits + softcap + argmax for callers that cannot allocate device memory.
 //
 // sfc_logits_argmax keeps its per-CTA partial results in a scratch buffer that it allocates
-// with cudaMalloc the first time it needs one.  Some callers cannot let a library do that: code
-// running while a CUDA graph is being captured (allocation is not a capturable operation), and
+// with cudaMalloc the first time it needs one.  Some callers cannot let a library do that:
 // serving processes whose device memory is reserved up front by their own allocator or budget,
 // where a stray cudaMalloc either fails or fragments the reservation (and synchronizes the
-// device).  sfc_logits_argmax_noalloc computes the same result with its scratch in a fixed
-// array that belongs to this library and is sized at load time.
+// device), and hosts that hand the library only the buffers they own.  sfc_logits_argmax_noalloc
+// computes the same result with its scratch in a fixed array that belongs to this library and is
+// sized at load time.
 #include <cuda_runtime.h>
 
 #include <mutex>

@@ -99,9 +99,9 @@ int sfc_logits_argmax(int ggml_type, const void *w_dev, int64_t vocab, int64_t d
 int sfc_sample_temperature(const float *scores_dev, int64_t n, int64_t vocab, float temperature, uint64_t seed,
                            int64_t *tokens_dev, void *stream);
 
-/* Same computation as sfc_logits_argmax, for callers that cannot allocate device memory (code
- * running under CUDA graph capture, processes whose device memory belongs to their own
- * allocator).  No counterpart in the reference.  It allocates nothing: its per-CTA partials live
+/* Same computation as sfc_logits_argmax, for callers that cannot allocate device memory
+ * (serving processes whose device memory is reserved up front and owned by their own allocator,
+ * so a cudaMalloc inside the library would fail or fragment it).  No counterpart in the reference.  It allocates nothing: its per-CTA partials live
  * in a fixed 64 KiB array inside the library (enough for GPUs with up to 512 SMs; larger needs
  * return SFC_E_NOMEM).  The first call on each device looks up that array's device address, so
  * make it before any stream capture.  All calls share the array: calls whose kernels overlap on

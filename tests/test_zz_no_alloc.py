@@ -1,7 +1,6 @@
 """GPU: the allocation-free logits entry point (sfc_logits_argmax_noalloc) gives the same result as
-sfc_logits_argmax.  It exists for callers that cannot have the library call cudaMalloc: work being
-captured into a CUDA graph, and serving processes whose device memory is owned by their own
-allocator.  Collected last so that a run stopping at the first failure has already run every
+sfc_logits_argmax.  It exists for callers that cannot have the library call cudaMalloc: serving
+processes whose device memory is reserved up front and owned by their own allocator.  Collected last so that a run stopping at the first failure has already run every
 other test; it must also pass alone in a fresh process."""
 import ctypes
 
