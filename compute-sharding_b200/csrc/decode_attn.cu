@@ -71,7 +71,7 @@ __device__ __forceinline__ void load_row8(const uint8_t *p, bool kv32, float (&v
 template <int G, bool KV32>
 __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
     const float *__restrict__ qr, const float *__restrict__ kr, const float *__restrict__ vr, int q_ld, int kv_ld,
-    float *__restrict__ out, KVLayer kv, const SeqInfo *__restrict__ seqs, AttnParams p, int n_split,
+    float *__restrict__ out, KVLayer kv, const SeqInfo *__restrict__ seqs, AttnParams p, int n_split, int min_chunk,
     float *__restrict__ part, unsigned *__restrict__ counters, unsigned *err) {
   constexpr int ESZ = KV32 ? 4 : 2;
   constexpr int TK = DA_TILE_BYTES / (DA_MAX_HD * ESZ);  // keys per tile
@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   const int w0 = p.window > 0 ? max(0, limit - p.window) : 0;
   const int span = limit - w0;
   int chunk = (span + n_split - 1) / n_split;
-  if (chunk < DA_MIN_CHUNK) chunk = DA_MIN_CHUNK;
+  if (chunk < min_chunk) chunk = min_chunk;  // min_chunk >= DA_MIN_CHUNK
   const int n_eff = (span + chunk - 1) / chunk;
   if (split >= n_eff) return;  // this sequence needs fewer splits (uniform over the CTA)
   const int k_begin = w0 + split * chunk, k_end = min(limit, k_begin + chunk);
@@ -386,6 +386,25 @@ int decode_attention_splits(int64_t n_seq, const AttnParams &p, int64_t max_keys
   return int(want);
 }
 
+// Keys per split at least, for a batch of sum_keys keys in total: every CTA pays a fixed cost
+// (head norms, RoPE, the warp merge, the partials and the last-CTA merge) that a split of a few
+// tiles does not amortise, so large batches spread their keys over about DA_CTAS_PER_SM CTAs per
+// SM instead of giving every sequence the split count of the longest one.  A sequence then takes
+// max(ceil(span / n_split), min_chunk) keys per split; n_split bounds the grid and the partials.
+constexpr int DA_CTAS_PER_SM = 4;  // measured at 64 sequences: 2 and 8 were slower
+static void decode_attention_plan(int64_t n_seq, const AttnParams &p, int64_t max_keys, int64_t sum_keys, int *ns,
+                                  int *min_chunk) {
+  *ns = decode_attention_splits(n_seq, p, max_keys);
+  *min_chunk = DA_MIN_CHUNK;
+  if (sum_keys <= 0) return;
+  const int64_t target = int64_t(DA_CTAS_PER_SM) * num_sms();
+  const int64_t c = (sum_keys * p.n_kv + target - 1) / target;
+  if (c <= DA_MIN_CHUNK) return;
+  *min_chunk = int(c < (int64_t(1) << 30) ? c : (int64_t(1) << 30));
+  const int64_t need = (max_keys + *min_chunk - 1) / *min_chunk;
+  if (need < *ns) *ns = int(need < 1 ? 1 : need);
+}
+
 size_t decode_attention_scratch_bytes(int64_t n_seq, const AttnParams &p, int64_t max_keys) {
   const int ns = decode_attention_splits(n_seq, p, max_keys);
   return size_t(n_seq) * p.n_heads * ns * (p.head_dim + 2) * sizeof(float);
@@ -398,17 +417,19 @@ bool decode_attention_supported(const AttnParams &p) {
 }
 
 cudaError_t decode_attention(const float *q, const float *k, const float *v, int q_ld, int kv_ld, float *out,
-                             KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, const AttnParams &p,
-                             void *scratch, size_t scratch_bytes, unsigned *counters, cudaStream_t st) {
+                             KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, int64_t sum_keys,
+                             const AttnParams &p, void *scratch, size_t scratch_bytes, unsigned *counters,
+                             cudaStream_t st) {
   if (n_seq <= 0) return cudaSuccess;
   if (!decode_attention_supported(p) || !counters) return cudaErrorInvalidValue;
-  const int ns = decode_attention_splits(n_seq, p, max_keys);
+  int ns = 1, min_chunk = DA_MIN_CHUNK;
+  decode_attention_plan(n_seq, p, max_keys, sum_keys, &ns, &min_chunk);
   if (scratch_bytes < decode_attention_scratch_bytes(n_seq, p, max_keys)) return cudaErrorInvalidValue;
   const size_t smem = size_t(DA_STAGES) * 2 * DA_TILE_BYTES;
   const dim3 grid(unsigned(n_seq), unsigned(p.n_kv), unsigned(ns));
   const int G = p.n_heads / p.n_kv;
   void (*kern)(const float *, const float *, const float *, int, int, float *, KVLayer, const SeqInfo *, AttnParams,
-               int, float *, unsigned *, unsigned *) = nullptr;
+               int, int, float *, unsigned *, unsigned *) = nullptr;
   switch (G) {
     case 1: kern = p.kv_f32 ? decode_attention_kernel<1, true> : decode_attention_kernel<1, false>; break;
     case 2: kern = p.kv_f32 ? decode_attention_kernel<2, true> : decode_attention_kernel<2, false>; break;
@@ -417,7 +438,7 @@ cudaError_t decode_attention(const float *q, const float *k, const float *v, int
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, grid, dim3(DA_THREADS), smem, st, q, k, v, q_ld, kv_ld, out, kv, seqs, p, ns,
+  return launch_pdl(kern, grid, dim3(DA_THREADS), smem, st, q, k, v, q_ld, kv_ld, out, kv, seqs, p, ns, min_chunk,
                     static_cast<float *>(scratch), counters, device_error_ptr());
 }
 

@@ -173,12 +173,14 @@ constexpr int64_t QGEMM_MIN_TOKENS = 8;
 
 // Decode step (one new token per sequence, row t = sequence t): q/k/v head norms + RoPE, KV
 // append and attention in one launch (decode_attn.cu).  counters: n_seq * n_kv words, zero
-// before the first launch; every launch leaves them zero.
+// before the first launch; every launch leaves them zero.  sum_keys: the batch's keys summed over
+// its sequences (new ones included), or 0; it only sets how many keys a split takes at least.
 bool decode_attention_supported(const AttnParams &p);
 size_t decode_attention_scratch_bytes(int64_t n_seq, const AttnParams &p, int64_t max_keys);
 cudaError_t decode_attention(const float *q, const float *k, const float *v, int q_ld, int kv_ld, float *out,
-                             KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, const AttnParams &p,
-                             void *scratch, size_t scratch_bytes, unsigned *counters, cudaStream_t st);
+                             KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, int64_t sum_keys,
+                             const AttnParams &p, void *scratch, size_t scratch_bytes, unsigned *counters,
+                             cudaStream_t st);
 // One decoder layer of a one-token, one-sequence decode step as a single cooperative launch
 // (decode_layer.cu): q/k/v projections with the fused residual + RMSNorm prologue, attention,
 // o projection, gate/up + GeGLU, down.  bar: two words, zero before the first launch (each launch

@@ -270,6 +270,7 @@ struct sfc_stage {
   SeqInfo *seq_dev = nullptr;
   void *scratch = nullptr;
   unsigned *attn_counters = nullptr;  // decode attention split counters, [max_batch][n_kv], kept zero
+  int64_t attn_sum_keys = 0;  // keys of the eager batch being run (0: graph capture, fixed splits)
   void *gemv_split_mem = nullptr;     // GEMV tile-boundary counters (kept zero) and partial sums
   GemvSplit gemv_split = {};
   // one-token decode as one launch per layer (decode_layer.cu): grid-barrier words, kept valid
@@ -780,8 +781,8 @@ GemvSeg seg_of(const DevTensor *w, const DevTensor *w2, float *y, int64_t ldy) {
 cudaError_t layer_attention(sfc_stage *h, const AttnParams &ap, const KVLayer &kv, int64_t T, int64_t max_keys,
                             bool decode, cudaStream_t st) {
   if (decode && !h->tree_active && decode_attention_supported(ap))
-    return decode_attention(h->q, h->k, h->v, h->q_dim, h->k_dim, h->att, kv, h->seq_dev, T, max_keys, ap,
-                            h->scratch, h->attn_scratch, h->attn_counters, st);
+    return decode_attention(h->q, h->k, h->v, h->q_dim, h->k_dim, h->att, kv, h->seq_dev, T, max_keys,
+                            h->attn_sum_keys, ap, h->scratch, h->attn_scratch, h->attn_counters, st);
   const bool tr = h->tree_active;
   cudaError_t e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev,
                            tr ? h->tree_rope_dev : nullptr, T, ap, st);
@@ -1000,7 +1001,7 @@ struct SeqReq {
 // `in_dev` rows for other stages.  Output stays in h->resid.
 int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t *ids, bool ids_on_device,
                   const float *in_dev, cudaStream_t st) {
-  int64_t T = 0, max_keys = 1;
+  int64_t T = 0, max_keys = 1, sum_keys = 0;
   for (auto &s : seqs) {
     SFC_REQUIRE(s.n > 0, "empty sequence in batch");
     if (s.s->len + s.n > h->max_ctx) {
@@ -1009,6 +1010,7 @@ int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t 
     }
     T += s.n;
     max_keys = std::max<int64_t>(max_keys, s.s->len + s.n);
+    sum_keys += s.s->len + s.n;
   }
   SFC_REQUIRE(T <= h->max_batch, "batch of %lld rows exceeds max_batch_tokens %d", (long long)T, h->max_batch);
   int ri;
@@ -1046,7 +1048,10 @@ int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t 
     SFC_CUDA(cudaMemcpyAsync(h->resid, in_dev, size_t(T) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
   }
   h->ring.release(ri, st);
-  SFC_CUDA(run_layers(h, T, max_keys, T == int64_t(seqs.size()), st));
+  h->attn_sum_keys = sum_keys;
+  const cudaError_t lerr = run_layers(h, T, max_keys, T == int64_t(seqs.size()), st);
+  h->attn_sum_keys = 0;
+  SFC_CUDA(lerr);
   for (auto &s : seqs) s.s->len += s.n;
   return SFC_OK;
 }
