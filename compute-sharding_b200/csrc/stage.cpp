@@ -16,170 +16,19 @@
 
 #include <algorithm>
 #include <map>
+#include <set>
 #include <memory>
 #include <string>
 #include <unordered_map>
 #include <vector>
 
 #include "capi_common.h"
+#include "gguf.h"
+#include "json.h"
 #include "common.cuh"
 #include "kernels.h"
 
 namespace sfc {
-
-// ------------------------------------------------------------------ minimal JSON reader
-struct Json {
-  enum Kind { Null, Bool, Num, Str, Arr, Obj } kind = Null;
-  double num = 0;
-  bool b = false;
-  std::string str;
-  std::vector<Json> arr;
-  std::vector<std::pair<std::string, Json>> obj;
-  const Json *get(const char *k) const {
-    for (auto &kv : obj)
-      if (kv.first == k) return &kv.second;
-    return nullptr;
-  }
-};
-
-struct JsonParser {
-  const char *p, *e;
-  bool ok = true;
-  void ws() {
-    while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
-  }
-  bool lit(const char *s) {
-    size_t n = strlen(s);
-    if (size_t(e - p) >= n && !memcmp(p, s, n)) {
-      p += n;
-      return true;
-    }
-    return false;
-  }
-  std::string string() {
-    std::string out;
-    ++p;  // opening quote
-    while (p < e && *p != '"') {
-      if (*p == '\\' && p + 1 < e) {
-        ++p;
-        switch (*p) {
-          case 'n': out += '\n'; break;
-          case 't': out += '\t'; break;
-          case 'r': out += '\r'; break;
-          case 'b': out += '\b'; break;
-          case 'f': out += '\f'; break;
-          case 'u': {  // keep ASCII, replace others
-            if (e - p >= 5) {
-              unsigned v = unsigned(strtoul(std::string(p + 1, p + 5).c_str(), nullptr, 16));
-              out += v < 128 ? char(v) : '?';
-              p += 4;
-            }
-            break;
-          }
-          default: out += *p;
-        }
-        ++p;
-      } else {
-        out += *p++;
-      }
-    }
-    if (p >= e) ok = false;
-    ++p;
-    return out;
-  }
-  Json value() {
-    Json j;
-    ws();
-    if (p >= e) {
-      ok = false;
-      return j;
-    }
-    if (*p == '{') {
-      j.kind = Json::Obj;
-      ++p;
-      ws();
-      if (p < e && *p == '}') {
-        ++p;
-        return j;
-      }
-      while (ok) {
-        ws();
-        if (p >= e || *p != '"') {
-          ok = false;
-          break;
-        }
-        std::string k = string();
-        ws();
-        if (p >= e || *p != ':') {
-          ok = false;
-          break;
-        }
-        ++p;
-        j.obj.emplace_back(k, value());
-        ws();
-        if (p < e && *p == ',') {
-          ++p;
-          continue;
-        }
-        if (p < e && *p == '}') {
-          ++p;
-          break;
-        }
-        ok = false;
-      }
-    } else if (*p == '[') {
-      j.kind = Json::Arr;
-      ++p;
-      ws();
-      if (p < e && *p == ']') {
-        ++p;
-        return j;
-      }
-      while (ok) {
-        j.arr.push_back(value());
-        ws();
-        if (p < e && *p == ',') {
-          ++p;
-          continue;
-        }
-        if (p < e && *p == ']') {
-          ++p;
-          break;
-        }
-        ok = false;
-      }
-    } else if (*p == '"') {
-      j.kind = Json::Str;
-      j.str = string();
-    } else if (lit("true")) {
-      j.kind = Json::Bool;
-      j.b = true;
-    } else if (lit("false")) {
-      j.kind = Json::Bool;
-    } else if (lit("null")) {
-      j.kind = Json::Null;
-    } else {
-      char *end = nullptr;
-      j.num = strtod(p, &end);
-      if (end == p) ok = false;
-      j.kind = Json::Num;
-      p = end;
-    }
-    return j;
-  }
-};
-
-static bool read_file(const std::string &path, std::string &out) {
-  FILE *f = fopen(path.c_str(), "rb");
-  if (!f) return false;
-  fseek(f, 0, SEEK_END);
-  long n = ftell(f);
-  fseek(f, 0, SEEK_SET);
-  out.resize(size_t(n));
-  size_t got = n > 0 ? fread(&out[0], 1, size_t(n), f) : 0;
-  fclose(f);
-  return got == size_t(n);
-}
 
 // ------------------------------------------------------------------ stage
 struct DevTensor {
@@ -1218,6 +1067,67 @@ int sfc_stage_open(const char *index_json_path, const sfc_layout *layout, const 
     set_error("Packed tensor coverage %lld does not match total_bytes %lld", (long long)expected,
               (long long)pack.size());
     return SFC_E_IO;
+  }
+  rc = build_stage(h.get(), hts);
+  if (rc) {
+    destroy_stage(h.release());
+    return rc;
+  }
+  *out = h.release();
+  return SFC_OK;
+}
+
+int sfc_stage_open_gguf(const char *gguf_path, const sfc_layout *layout, const sfc_options *opts, int device,
+                        sfc_stage **out) {
+  clear_error();
+  SFC_REQUIRE(gguf_path && layout && out, "null argument");
+  std::unique_ptr<sfc_stage> h;
+  int rc = new_stage(layout, opts, device, out, h);
+  if (rc) return rc;
+  GgufFile f;  // mapped until this call returns (build_stage finishes its uploads first)
+  std::string err;
+  if (!f.bytes.map_file(gguf_path, err) || !f.parse(err)) {
+    set_error("%s", err.c_str());
+    return SFC_E_IO;
+  }
+  // The tensors a runtime plan gives this stage (gguf.rs:560-616): its layers, the positional and
+  // shared auxiliary tensors, the embedding on the head (and on a tail without output.weight, whose
+  // logits use the tied embedding, real_forward.rs:803-816) and output* on the tail.
+  const bool head = layout->is_head != 0, tail = layout->is_tail != 0;
+  const bool has_output = f.find("output.weight") >= 0;
+  std::vector<HostTensor> hts;
+  std::set<std::string> seen;
+  for (size_t k = 0; k < f.tensors.size(); ++k) {
+    const GgufTensorInfo &t = f.tensors[k];
+    bool take = false;
+    switch (f.role[k]) {
+      case ROLE_LAYER: take = f.layer[k] >= int64_t(layout->start_layer) && f.layer[k] <= int64_t(layout->end_layer); break;
+      case ROLE_PROMPT_INGRESS: take = head || (tail && !has_output); break;
+      case ROLE_POSITIONAL:
+      case ROLE_SHARED_AUX: take = true; break;
+      case ROLE_TAIL_ONLY: take = tail; break;
+      default: take = false;
+    }
+    if (!take || !seen.insert(t.name).second) continue;  // a repeated name: the first one, as lookups find
+    HostTensor ht;
+    ht.name = t.name;
+    ht.type = int(t.type);
+    for (uint64_t d : t.dims) {
+      SFC_REQUIRE(d < (uint64_t(1) << 40), "tensor %s: dimension %llu too large", t.name.c_str(),
+                  (unsigned long long)d);
+      ht.dims.push_back(int64_t(d));
+    }
+    const int64_t gb = gguf_tensor_bytes(ht.type, ht.dims);
+    const uint64_t off = f.data_offset + t.offset;
+    if (gb >= 0) {
+      SFC_REQUIRE(uint64_t(gb) <= f.byte_len[k], "tensor %s: %lld bytes implied by its dims but %llu before the next tensor",
+                  t.name.c_str(), (long long)gb, (unsigned long long)f.byte_len[k]);
+      SFC_REQUIRE(off <= f.file_size && uint64_t(gb) <= f.file_size - off, "tensor %s runs past the end of %s",
+                  t.name.c_str(), gguf_path);
+    }
+    ht.data = f.bytes.data + (off <= f.file_size ? off : 0);
+    ht.bytes = gb >= 0 ? gb : int64_t(f.byte_len[k]);  // an unsupported type fails in build_stage
+    hts.push_back(ht);
   }
   rc = build_stage(h.get(), hts);
   if (rc) {

@@ -84,6 +84,8 @@ _sig("sfc_synth_tensor", _I, _I, _U64, ctypes.c_char_p, _I64, _I64, _F, _F, _P, 
 _sig("sfc_stage_open", _I, ctypes.c_char_p, ctypes.POINTER(Layout), ctypes.POINTER(Options), _I, ctypes.POINTER(_P))
 _sig("sfc_stage_open_synthetic", _I, ctypes.POINTER(SynthSpec), ctypes.POINTER(Layout), ctypes.POINTER(Options), _I,
      ctypes.POINTER(_P))
+_sig("sfc_stage_open_gguf", _I, ctypes.c_char_p, ctypes.POINTER(Layout), ctypes.POINTER(Options), _I,
+     ctypes.POINTER(_P))
 _sig("sfc_stage_close", _I, _P)
 _sig("sfc_stage_get_info", _I, _P, ctypes.POINTER(StageInfo))
 _sig("sfc_begin_token_ids", _I, _P, ctypes.c_char_p, _P, _I64, _P)
@@ -269,11 +271,16 @@ class CudaStageBackend:
     """StageForwardBackend on B200 (RealGemmaBackend semantics, real_forward.rs:112-2411)."""
 
     def __init__(self, index_path: str | os.PathLike | None = None, *, synthetic: ModelShape | None = None,
-                 device: int = 0, rope_theta: float = 0.0, logit_softcap: float = 0.0, kv_f32: bool = False,
-                 max_ctx: int = 4096, max_sessions: int = 64, max_batch_tokens: int = 512):
-        if (index_path is None) == (synthetic is None):
-            raise ValueError("give exactly one of index_path or synthetic")
+                 gguf_path: str | os.PathLike | None = None, device: int = 0, rope_theta: float = 0.0,
+                 logit_softcap: float = 0.0, kv_f32: bool = False, max_ctx: int = 4096, max_sessions: int = 64,
+                 max_batch_tokens: int = 512):
+        """Weights from a packed stage (`<stage>.index.json`, RealGemmaBackend::new), from a GGUF
+        file directly (`gguf_path`: the layout's layers and the stage's head/tail tensors), or
+        generated on the device (`synthetic`)."""
+        if sum(x is not None for x in (index_path, synthetic, gguf_path)) != 1:
+            raise ValueError("give exactly one of index_path, gguf_path or synthetic")
         self.index_path = None if index_path is None else str(index_path)
+        self.gguf_path = None if gguf_path is None else os.fspath(gguf_path)
         self.synthetic = synthetic
         self.device = device
         self.options = Options(rope_theta, logit_softcap, 0.0, int(kv_f32), max_ctx, max_sessions, max_batch_tokens)
@@ -290,6 +297,9 @@ class CudaStageBackend:
             spec = self.synthetic.spec()
             rc = _lib.sfc_stage_open_synthetic(ctypes.byref(spec), ctypes.byref(self._layout),
                                                ctypes.byref(self.options), self.device, ctypes.byref(h))
+        elif self.gguf_path is not None:
+            rc = _lib.sfc_stage_open_gguf(os.fsencode(self.gguf_path), ctypes.byref(self._layout),
+                                          ctypes.byref(self.options), self.device, ctypes.byref(h))
         else:
             rc = _lib.sfc_stage_open(self.index_path.encode(), ctypes.byref(self._layout), ctypes.byref(self.options),
                                      self.device, ctypes.byref(h))

@@ -37,6 +37,7 @@ enum {
   SFC_E_IO = -3,       /* pack / index file error */
   SFC_E_NOMEM = -4,    /* device allocation failed or a fixed capacity is exceeded */
   SFC_E_DEVICE = -5,   /* a kernel reported a device-side error (bounded wait expired, bad id) */
+  SFC_ABSENT = 1,      /* a query found no such key / tensor / split (not an error) */
 };
 
 /* ------------------------------------------------------------------ misc */
@@ -233,6 +234,93 @@ typedef struct {
   int64_t kernels; /* kernels launched by the timed region (graph replays included) */
 } sfc_profile;
 int sfc_last_profile(sfc_stage *h, sfc_profile *out);
+
+/* ------------------------------------------------------------------ GGUF shards, splits, packs
+ * The reference's on-disk path: GgufFile (crates/stage-forward-lab/src/gguf.rs:138-365), the shard
+ * manifest bundle (plan_for_splits / build_manifest / write_bundle, gguf.rs:366-751), the runtime
+ * bundle loader and the stage pack writer (LoadedRuntimeBundle / StageResidencyAdapter,
+ * lib.rs:3283-3613).  Files written here have the reference's names, layout and JSON field order. */
+
+typedef struct sfc_gguf sfc_gguf;
+
+/* TensorRole (gguf.rs:49-57), from classify_tensor_role (gguf.rs:753-786) */
+enum {
+  SFC_ROLE_LAYER = 0,          /* blk.<n>.* */
+  SFC_ROLE_PROMPT_INGRESS = 1, /* token_embd.weight */
+  SFC_ROLE_POSITIONAL = 2,     /* rope_freqs.weight */
+  SFC_ROLE_SHARED_AUX = 3,     /* per_layer_token_embd / per_layer_model_proj / per_layer_proj_norm */
+  SFC_ROLE_TAIL_ONLY = 4,      /* output* */
+  SFC_ROLE_UNKNOWN_GLOBAL = 5,
+};
+
+typedef struct {
+  uint32_t version;
+  uint64_t tensor_count, metadata_count, file_size_bytes, tensor_data_offset;
+  int64_t layer_count;          /* inferred_layer_count (gguf.rs:235-247); -1 if none */
+  int64_t hidden_size;          /* <arch>.embedding_length for gemma4 / gemma / llama; -1 if absent */
+  int64_t feed_forward_length;  /* <arch>.feed_forward_length; -1 if absent */
+  int64_t attention_head_count; /* <arch>.attention.head_count; -1 if absent */
+  const char *architecture;     /* general.architecture if a string, else NULL (valid while open) */
+} sfc_gguf_info;
+
+typedef struct {
+  const char *name;       /* valid while the handle is open */
+  uint32_t n_dims;
+  const uint64_t *dims;   /* [n_dims], GGUF order (dims[0] = elements per row) */
+  uint32_t ggml_type;
+  uint64_t offset;        /* relative to the tensor data section */
+  uint64_t file_offset;   /* tensor_file_offset (gguf.rs:345-350) */
+  uint64_t byte_len;      /* tensor_byte_len (gguf.rs:331-343): distance to the next tensor by offset */
+  int32_t role;           /* SFC_ROLE_* */
+  int64_t layer;          /* layer index for SFC_ROLE_LAYER, else -1 */
+} sfc_gguf_tensor;
+
+/* StageSplit (gguf.rs:42-47) */
+typedef struct {
+  uint32_t stage_index, start_layer, end_layer;
+} sfc_stage_split;
+
+/* GgufFile::parse_file / parse_bytes (gguf.rs:139-210): versions 1 (32-bit counts) and 2/3; the
+ * tensor data starts at general.alignment (u32/u64, default 32).  Malformed files return
+ * SFC_E_IO with the reason.  open maps the file read-only and keeps it mapped until close. */
+int sfc_gguf_open(const char *path, sfc_gguf **out);
+int sfc_gguf_parse(const void *bytes, uint64_t n, sfc_gguf **out);
+int sfc_gguf_close(sfc_gguf *g);
+int sfc_gguf_get_info(const sfc_gguf *g, sfc_gguf_info *info);
+int sfc_gguf_get_tensor(const sfc_gguf *g, uint64_t index, sfc_gguf_tensor *out);
+/* First tensor with that name; SFC_ABSENT if none. */
+int sfc_gguf_find_tensor(const sfc_gguf *g, const char *name, uint64_t *index);
+/* Metadata keys in sorted order (the reference keeps a BTreeMap; a repeated key keeps its last value). */
+int sfc_gguf_metadata_key(const sfc_gguf *g, uint64_t index, const char **key, uint32_t *value_type);
+/* metadata_string (gguf.rs:249-251 with metadata_value_to_string :800-823): any value as text, floats
+ * in Rust's shortest round-trip form without exponent, arrays as "[a, b]".  Writes at most cap-1
+ * bytes and a NUL; *len = the full length.  SFC_ABSENT if the key is missing. */
+int sfc_gguf_metadata_string(const sfc_gguf *g, const char *key, char *buf, uint64_t cap, uint64_t *len);
+/* metadata_u32 (gguf.rs:279-287): u32, or u64 / i32 / i64 values that fit; else SFC_ABSENT. */
+int sfc_gguf_metadata_u32(const sfc_gguf *g, const char *key, uint32_t *value);
+/* block_indices (gguf.rs:219-233): sorted distinct n of blk.<n>.*; *n = count, first cap written. */
+int sfc_gguf_block_indices(const sfc_gguf *g, uint32_t *out, uint64_t cap, uint64_t *n);
+/* suggest_even_stage_split (gguf.rs:307-329): out[stages]; the first (layers % stages) stages take
+ * one extra layer.  SFC_ABSENT when stages is 0, exceeds the layer count, or no count is known. */
+int sfc_gguf_even_split(const sfc_gguf *g, uint32_t stages, sfc_stage_split *out);
+/* plan_for_splits + write_bundle (gguf.rs:366-400, :636-751): model-shard-manifest.json,
+ * stage-N.json and its six tensor lists, runtime-stage-N.json, -required.txt, -optional.txt and
+ * -slices.json in out_dir (created). */
+int sfc_gguf_write_bundle(const sfc_gguf *g, const sfc_stage_split *splits, uint32_t n_splits, const char *out_dir);
+/* StageResidencyAdapter::load + pack_required_tensors / pack_all_tensors (lib.rs:3424-3613): checks
+ * the bundle against itself and the GGUF, then writes stage-N-required.pack and
+ * stage-N-required.index.json (N = stage_index + 1) into out_dir; include_optional adds the
+ * stage's optional tensors (the tied embedding on non-head stages).  The index path is copied to
+ * index_path (cap bytes, NUL included) when cap > 0. */
+int sfc_pack_stage(const char *bundle_dir, const char *gguf_path, uint32_t stage_index, int include_optional,
+                   const char *out_dir, char *index_path, uint64_t cap);
+/* A stage straight from a GGUF file (no pack): the layout's layers start..end plus, as the
+ * runtime plan would give it, rope_freqs and the shared auxiliaries, token_embd on the head (and on
+ * the tail when the file has no output.weight: tied logits) and output* on the tail.  Tensors are
+ * read at the size their dimensions imply, straight from the mapped file.  Otherwise as
+ * sfc_stage_open. */
+int sfc_stage_open_gguf(const char *gguf_path, const sfc_layout *layout, const sfc_options *opts, int device,
+                        sfc_stage **out);
 
 #ifdef __cplusplus
 }
