@@ -97,8 +97,10 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   const int n_eff = (span + chunk - 1) / chunk;
   if (split >= n_eff) return;  // this sequence needs fewer splits (uniform over the CTA)
   const int k_begin = w0 + split * chunk, k_end = min(limit, k_begin + chunk);
-  const int k_old_end = min(k_end, pos);  // keys already in the cache
-  const bool owner = k_end == limit;      // this split holds the new key
+  // keys already in the cache: all of them when another layer's cache is read (kv_shared: that
+  // layer appended this step's key earlier in the forward)
+  const int k_old_end = p.kv_shared ? k_end : min(k_end, pos);
+  const bool owner = k_end == limit && !p.kv_shared;  // this split computes and appends the new key
   const int n_old = max(0, k_old_end - k_begin);
   const int n_tiles = (n_old + TK - 1) / TK;
 

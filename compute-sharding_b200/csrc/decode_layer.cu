@@ -629,6 +629,7 @@ size_t decode_layer_scratch_bytes(const AttnParams &ap, int64_t max_keys) {
 
 cudaError_t decode_layer(const DecodeLayerIn &in, cudaStream_t st) {
   const AttnParams &ap = in.ap;
+  if (ap.kv_shared) return cudaErrorNotSupported;  // the attention item appends the layer's own k/v
   if (!decode_layer_supported(ap) || !in.bar || !in.split || !in.split->cnt || !in.split->part) return cudaErrorInvalidValue;
   DecodeLayerArgs d = {};
   DecodeLayerPlanIn pi = {};

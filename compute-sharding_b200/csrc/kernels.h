@@ -110,6 +110,8 @@ struct AttnParams {
   int n_freqs;
   const float *q_norm, *k_norm;  // may be null
   int window;          // <= 0: none
+  int kv_shared;       // 1: the layer attends over another layer's cache, already holding this step's
+                       // positions; it has no k/v of its own and appends nothing
 };
 
 // One sequence of the current batch.  Its cache for a layer lives in slot `slot` of that

@@ -231,8 +231,10 @@ cudaError_t qkv_post(float *q, const float *k, const float *v, int q_ld, int kv_
                      cudaStream_t st) {
   if (n_tok <= 0) return cudaSuccess;
   if (p.head_dim > 1024) return cudaErrorInvalidValue;
-  return launch_pdl(qkv_post_kernel, dim3(unsigned(n_tok), unsigned(p.n_heads + 2 * p.n_kv)), dim3(256), 0, st, q, k,
-                    v, q_ld, kv_ld, kv, seqs, tok_seq, rope_pos, p);
+  // a layer reading another layer's cache (kv_shared) normalises and rotates only its q heads
+  const unsigned heads = unsigned(p.n_heads + (p.kv_shared ? 0 : 2 * p.n_kv));
+  return launch_pdl(qkv_post_kernel, dim3(unsigned(n_tok), heads), dim3(256), 0, st, q, k, v, q_ld, kv_ld, kv, seqs,
+                    tok_seq, rope_pos, p);
 }
 
 // ---------------------------------------------------------------- attention

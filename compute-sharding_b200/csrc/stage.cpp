@@ -44,6 +44,14 @@ struct Layer {
   DevTensor *attn_norm = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *q_norm = nullptr, *k_norm = nullptr,
             *o = nullptr, *post_attn = nullptr, *ffn_norm = nullptr, *gate = nullptr, *up = nullptr,
             *down = nullptr, *post_ffw = nullptr, *scale = nullptr;
+  // attention schedule (LayerAttentionConfig, real_forward.rs:1407-1457); zeros: the stage's defaults
+  float theta = 0.f;     // RoPE base
+  int rotary_dim = 0;    // rotated dims (0: head_dim)
+  int proportional = 0;  // inv_freq over head_dim instead of rotary_dim
+  int window = 0;        // sliding window in keys
+  int kv_source = -1;    // index in sfc_stage::layers of the layer whose cache this one attends over
+  int slab = 0;          // KV cache slab (its own, or its source's)
+  bool own_kv() const { return kv_source < 0; }
 };
 
 struct Session {
@@ -111,6 +119,8 @@ struct sfc_stage {
   // activations
   float *resid2 = nullptr;  // residual ping-pong partner for the fused GEMV prologues
   bool fused = false;       // every layer matrix is a K-quant the fused GEMV handles
+  bool rope_unit = false;   // RoPE without packed frequencies (every scale 1): the Gemma-4 e4b rule
+  int kv_slabs = 0;         // KV cache slabs (layers that read another layer's cache hold none)
   float *resid = nullptr, *xn = nullptr, *proj = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
         *act = nullptr, *hn = nullptr, *score_dev = nullptr;
   uint32_t *ids_dev = nullptr;
@@ -338,22 +348,56 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
     SFC_REQUIRE(h->n_heads % h->n_kv == 0 && h->n_heads / h->n_kv <= 8, "unsupported GQA grouping %d/%d",
                 h->n_heads, h->n_kv);
     SFC_REQUIRE(hd <= 256, "head_dim %d > 256 unsupported", hd);
+    // Gemma-4 e4b attention schedule (layer_attention_config_for_layout, real_forward.rs:1407-1457):
+    // layers 5, 11, 17, .. are global (base 1e6, proportional RoPE over head_dim/4 dims), the others
+    // slide over 512 keys (base 1e4); from layer 24 on a layer attends over the cache of layer 23
+    // (global) or 22 (sliding) instead of its own.  The packed rope_freqs are not used for this
+    // model; RoPE still runs, every frequency scale 1 (real_forward.rs:158-160, :2287-2297).
+    if (h->model_id.find("gemma-4-e4b") != std::string::npos && h->hidden == 2560 && (hd == 256 || hd == 512)) {
+      h->rope_unit = true;
+      for (auto &L : h->layers) {
+        const bool global = L.index % 6 == 5;
+        L.theta = global ? 1000000.0f : 10000.0f;
+        L.rotary_dim = global ? hd / 4 : hd;
+        L.proportional = global ? 1 : 0;
+        L.window = global ? 0 : 512;
+        if (L.index < 24) continue;
+        const int src = global ? 23 : 22;
+        // validate_stage_split_constraints (real_forward.rs:1459-1481)
+        if (src < int(h->start_layer) || src > int(h->end_layer)) {
+          set_error("real_forward stage %s (layers %u-%u) is unsupported for %s: layer %d requires shared KV from "
+                    "layer %d outside this stage; current contract keeps shared-KV caches stage-local",
+                    h->stage_id.c_str(), h->start_layer, h->end_layer, h->model_id.c_str(), L.index, src);
+          return SFC_E_INVALID;
+        }
+        for (size_t j = 0; j < h->layers.size(); ++j)
+          if (h->layers[j].index == src) L.kv_source = int(j);
+        SFC_REQUIRE(L.kv_source >= 0, "layer %d reads the KV of layer %d, whose tensors this stage lacks", L.index,
+                    src);
+      }
+    }
     for (auto &L : h->layers) {
-      SFC_REQUIRE(L.q && L.k && L.v && L.o && L.gate && L.up && L.down, "layer %d is incomplete", L.index);
+      if (!L.own_kv()) {  // its k/v projections are not used (real_forward.rs:1561-1592): any or none
+        L.k = nullptr;
+        L.v = nullptr;
+        L.k_norm = nullptr;
+      }
+      SFC_REQUIRE(L.q && (!L.own_kv() || (L.k && L.v)) && L.o && L.gate && L.up && L.down, "layer %d is incomplete",
+                  L.index);
       for (DevTensor *t : {L.q_norm, L.k_norm})
         SFC_REQUIRE(!t || t->in_dim == hd, "%s has %lld elements but head_dim is %d", t->name.c_str(),
                     (long long)t->in_dim, hd);
       for (DevTensor *t : {L.attn_norm, L.post_attn, L.ffn_norm, L.post_ffw})
         SFC_REQUIRE(!t || t->in_dim == h->hidden, "%s has %lld elements but hidden is %d", t->name.c_str(),
                     (long long)t->in_dim, h->hidden);
-      SFC_REQUIRE(L.q->dims[0] == h->hidden && L.q->rows == h->q_dim && L.k->rows == h->k_dim &&
-                      L.v->rows == h->k_dim && L.o->dims[0] == h->q_dim && L.o->rows == h->hidden &&
+      SFC_REQUIRE(L.q->dims[0] == h->hidden && L.q->rows == h->q_dim && (!L.k || L.k->rows == h->k_dim) &&
+                      (!L.v || L.v->rows == h->k_dim) && L.o->dims[0] == h->q_dim && L.o->rows == h->hidden &&
                       L.gate->dims[0] == h->hidden && L.gate->rows == h->ffn && L.up->rows == h->ffn &&
                       L.down->dims[0] == h->ffn && L.down->rows == h->hidden,
                   "layer %d shapes differ from layer %d", L.index, h->layers.front().index);
       SFC_REQUIRE(L.gate->type == L.up->type, "layer %d: gate/up types differ", L.index);
       for (DevTensor *t : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
-        SFC_REQUIRE((t->type != T_Q4_K && t->type != T_Q6_K) || t->in_dim <= 10240,
+        SFC_REQUIRE(!t || (t->type != T_Q4_K && t->type != T_Q6_K) || t->in_dim <= 10240,
                     "%s: K-quant rows of %lld elements exceed the GEMV limit 10240", t->name.c_str(),
                     (long long)t->in_dim);
     }
@@ -365,7 +409,14 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
              h->hidden <= 10240 && h->q_dim <= 10240 && h->ffn <= 10240;
   for (auto &L : h->layers)
     for (DevTensor *t : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
-      if (t->type != T_Q4_K && t->type != T_Q6_K) h->fused = false;
+      if (t && t->type != T_Q4_K && t->type != T_Q6_K) h->fused = false;
+  {  // KV slabs: one per layer with its own cache; readers of another layer's cache share its slab
+    int slabs = 0;
+    for (auto &L : h->layers) L.slab = L.own_kv() ? slabs++ : -1;
+    for (auto &L : h->layers)
+      if (!L.own_kv()) L.slab = h->layers[size_t(L.kv_source)].slab;
+    h->kv_slabs = slabs;
+  }
   if (h->output_norm)
     SFC_REQUIRE(h->output_norm->in_dim == h->hidden, "output_norm.weight has %lld elements but hidden is %d",
                 (long long)h->output_norm->in_dim, h->hidden);
@@ -443,7 +494,7 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   // KV cache
   const int64_t elt = h->kv_f32 ? 4 : 2;
   h->kv_slot_stride = 2 * int64_t(h->n_kv) * h->max_ctx * h->head_dim;
-  h->kv_bytes = int64_t(h->layers.size()) * h->max_sessions * h->kv_slot_stride * elt;
+  h->kv_bytes = int64_t(h->kv_slabs) * h->max_sessions * h->kv_slot_stride * elt;
   if (h->kv_bytes > 0) {
     if (cudaMalloc(&h->kv_arena, size_t(h->kv_bytes)) != cudaSuccess) {
       set_error("cannot allocate %lld bytes of KV cache (max_ctx %d x %d sessions)", (long long)h->kv_bytes,
@@ -502,16 +553,19 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
     // one-token decode through the layer kernel: K-quant projections, supported attention shape
     const char *env = getenv("SFC_DECODE_LAYER");
     bool ok = h->fused && decode_layer_supported(ap) && env && env[0] == '1';
-    for (const Layer &L : h->layers)
+    for (const Layer &L : h->layers) {
+      ok = ok && L.own_kv();  // the layer kernel appends every layer's own k/v
       for (const DevTensor *w : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
         ok = ok && w && (w->type == T_Q4_K || w->type == T_Q6_K);
+    }
     h->layer_kernel = ok;
   }
   if (h->fused && T >= QGEMM_MIN_TOKENS) {
     bool ok = true;
     for (const Layer &L : h->layers)
       for (const DevTensor *w : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
-        ok = ok && w && qgemm_supported(w->type, w->in_dim) && reinterpret_cast<uintptr_t>(w->dev) % 16 == 0;
+        ok = ok && (w ? qgemm_supported(w->type, w->in_dim) && reinterpret_cast<uintptr_t>(w->dev) % 16 == 0
+                      : (w == L.k || w == L.v) && !L.own_kv());
     if (ok) {
       size_t gb = 0;
       for (int64_t K : {int64_t(H), int64_t(h->q_dim), int64_t(h->ffn)}) gb = std::max(gb, qgemm_scratch_bytes(T, K));
@@ -588,7 +642,7 @@ int session_for(sfc_stage *h, const std::string &id, bool restart, Session **out
 KVLayer kv_layer(sfc_stage *h, size_t li) {
   KVLayer kv;
   const int64_t elt = h->kv_f32 ? 4 : 2;
-  kv.base = static_cast<char *>(h->kv_arena) + int64_t(li) * h->max_sessions * h->kv_slot_stride * elt;
+  kv.base = static_cast<char *>(h->kv_arena) + int64_t(h->layers[li].slab) * h->max_sessions * h->kv_slot_stride * elt;
   kv.slot_stride = h->kv_slot_stride;
   return kv;
 }
@@ -601,14 +655,20 @@ AttnParams attn_params(sfc_stage *h, const Layer &L) {
   p.kv_f32 = h->kv_f32;
   p.max_ctx = h->max_ctx;
   p.eps = h->eps;
-  p.rope_theta = h->theta;
-  p.rotary_dim = h->head_dim;
-  p.proportional = 0;
-  p.rope_freqs = h->rope_freqs ? static_cast<const float *>(h->rope_freqs->dev) : nullptr;
-  p.n_freqs = h->rope_freqs ? int(h->rope_freqs->in_dim) : 0;
+  p.rope_theta = L.theta > 0.f ? L.theta : h->theta;
+  p.rotary_dim = L.rotary_dim > 0 ? L.rotary_dim : h->head_dim;
+  p.proportional = L.proportional;
+  if (h->rope_unit) {  // RoPE on, no frequency table: the kernels read rope_freqs[i] only for i < n_freqs = 0
+    p.rope_freqs = static_cast<const float *>(h->resid);
+    p.n_freqs = 0;
+  } else {
+    p.rope_freqs = h->rope_freqs ? static_cast<const float *>(h->rope_freqs->dev) : nullptr;
+    p.n_freqs = h->rope_freqs ? int(h->rope_freqs->in_dim) : 0;
+  }
   p.q_norm = L.q_norm ? static_cast<const float *>(L.q_norm->dev) : nullptr;
   p.k_norm = L.k_norm ? static_cast<const float *>(L.k_norm->dev) : nullptr;
-  p.window = 0;
+  p.window = L.window;
+  p.kv_shared = L.own_kv() ? 0 : 1;
   return p;
 }
 
@@ -671,10 +731,12 @@ cudaError_t run_layers_gemm(sfc_stage *h, int64_t T, int64_t max_keys, bool deco
       pro.scale = F32P(P.scale);
       std::swap(cur, other);
     }
-    const QGemmOut qkv[3] = {{L.q->type, L.q->dev, L.q->rows, h->q, h->q_dim},
-                             {L.k->type, L.k->dev, L.k->rows, h->k, h->k_dim},
-                             {L.v->type, L.v->dev, L.v->rows, h->v, h->k_dim}};
-    if ((e = qgemm(qkv, 3, H, pro, T, gs, gsb, st))) return e;
+    QGemmOut qkv[3] = {{L.q->type, L.q->dev, L.q->rows, h->q, h->q_dim}, {}, {}};
+    if (L.own_kv()) {  // a layer reading another layer's cache projects q only
+      qkv[1] = {L.k->type, L.k->dev, L.k->rows, h->k, h->k_dim};
+      qkv[2] = {L.v->type, L.v->dev, L.v->rows, h->v, h->k_dim};
+    }
+    if ((e = qgemm(qkv, L.own_kv() ? 3 : 1, H, pro, T, gs, gsb, st))) return e;
     const AttnParams ap = attn_params(h, L);
     const KVLayer kv = kv_layer(h, li);
     if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
@@ -732,11 +794,15 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
       pro.scale = F32P(P.scale);
       std::swap(cur, other);
     }
-    const GemvSeg qkv[3] = {seg_of(L.q, nullptr, h->q, h->q_dim), seg_of(L.k, nullptr, h->k, h->k_dim),
-                            seg_of(L.v, nullptr, h->v, h->k_dim)};
+    GemvSeg qkv[3] = {seg_of(L.q, nullptr, h->q, h->q_dim), {}, {}};
+    if (L.own_kv()) {  // a layer reading another layer's cache projects q only
+      qkv[1] = seg_of(L.k, nullptr, h->k, h->k_dim);
+      qkv[2] = seg_of(L.v, nullptr, h->v, h->k_dim);
+    }
+    const int nqkv = L.own_kv() ? 3 : 1;
     const AttnParams ap = attn_params(h, L);
     const KVLayer kv = kv_layer(h, li);
-    if (T == 1 && decode && h->layer_kernel && !h->tree_active) {
+    if (T == 1 && decode && h->layer_kernel && !h->tree_active && L.own_kv()) {
       DecodeLayerIn in = {};
       in.qkv = qkv;
       in.o = seg_of(L.o, nullptr, h->proj, H);
@@ -778,7 +844,7 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
       (void)cudaGetLastError();
       h->layer_kernel = false;  // the model's shapes: per-op launches from here on
     }
-    if ((e = gemv_fused(qkv, 3, 1, H, pro, T, st, &h->gemv_split))) return e;
+    if ((e = gemv_fused(qkv, nqkv, 1, H, pro, T, st, &h->gemv_split))) return e;
     if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
     const GemvSeg o = seg_of(L.o, nullptr, h->proj, H);
     GemvPrologue po = {};
@@ -823,8 +889,10 @@ cudaError_t run_layers(sfc_stage *h, int64_t T, int64_t max_keys, bool decode, c
       if (e) return e;
     }
     if ((e = gemv(L.q->type, L.q->dev, nullptr, h->q_dim, H, h->xn, T, h->q, h->q_dim, st))) return e;
-    if ((e = gemv(L.k->type, L.k->dev, nullptr, h->k_dim, H, h->xn, T, h->k, h->k_dim, st))) return e;
-    if ((e = gemv(L.v->type, L.v->dev, nullptr, h->k_dim, H, h->xn, T, h->v, h->k_dim, st))) return e;
+    if (L.own_kv()) {
+      if ((e = gemv(L.k->type, L.k->dev, nullptr, h->k_dim, H, h->xn, T, h->k, h->k_dim, st))) return e;
+      if ((e = gemv(L.v->type, L.v->dev, nullptr, h->k_dim, H, h->xn, T, h->v, h->k_dim, st))) return e;
+    }
     const AttnParams ap = attn_params(h, L);
     const KVLayer kv = kv_layer(h, li);
     if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
@@ -1432,7 +1500,7 @@ int sfc_commit_tree(sfc_stage *h, const char *request_id, const int32_t *path, i
   cudaStream_t st = h->stream;
   if (h->kv_arena && !h->layers.empty()) {
     SFC_CUDA(cudaMemcpyAsync(h->tree_path_dev, path, size_t(n_path) * 4, cudaMemcpyHostToDevice, st));
-    SFC_CUDA(kv_compact(h->kv_arena, int(h->layers.size()), h->max_sessions, h->kv_slot_stride, s->slot, h->n_kv,
+    SFC_CUDA(kv_compact(h->kv_arena, h->kv_slabs, h->max_sessions, h->kv_slot_stride, s->slot, h->n_kv,
                         h->max_ctx, h->head_dim, h->kv_f32 ? 4 : 2, int(s->len), h->tree_path_dev, int(n_path), st));
     SFC_CUDA(cudaStreamSynchronize(st));
   }
@@ -1476,6 +1544,7 @@ int sfc_session_fill_synthetic(sfc_stage *h, const char *request_id, int64_t n_p
   if (rc) return rc;
   const int64_t elt = h->kv_f32 ? 4 : 2;
   for (size_t li = 0; li < h->layers.size(); ++li) {
+    if (!h->layers[li].own_kv()) continue;  // its cache is its source layer's
     KVLayer kv = kv_layer(h, li);
     for (int part = 0; part < 2; ++part)
       for (int kh = 0; kh < h->n_kv; ++kh) {

@@ -375,7 +375,28 @@ class OracleStage:
         self.head_dim, self.n_heads, self.n_kv = hd, q_dim // hd, max(1, k_dim // hd)
         rf = tensors.get("rope_freqs.weight")
         self.rope_freqs = None if rf is None else self._f32(rf)
+        if self._e4b():
+            # should_use_packed_rope_freqs (real_forward.rs:158-160): RoPE on, no frequency scales
+            self.rope_freqs = np.zeros(0, np.float32)
+            for i in layers:  # validate_stage_split_constraints (real_forward.rs:1459-1481)
+                src = self._attention_config(i)[3]
+                if src is not None and not (layout.start_layer <= src <= layout.end_layer):
+                    raise ValueError(f"real_forward stage {layout.stage_id} (layers {layout.start_layer}-"
+                                     f"{layout.end_layer}) is unsupported for {layout.model_id}: layer {i} requires "
+                                     f"shared KV from layer {src} outside this stage")
         self.sessions: dict[str, dict] = {}
+
+    def _e4b(self) -> bool:
+        return ("gemma-4-e4b" in self.layout.model_id and self.hidden == 2560 and self.head_dim in (256, 512))
+
+    def _attention_config(self, i: int):
+        """layer_attention_config_for_layout (real_forward.rs:1407-1457): (rope base, rotary dims,
+        proportional, shared-KV source layer or None, sliding window or 0)."""
+        if not self._e4b():
+            return self.rope_theta, self.head_dim, False, None, 0
+        if i % 6 == 5:
+            return 1_000_000.0, self.head_dim // 4, True, (23 if i >= 24 else None), 0
+        return 10_000.0, self.head_dim, False, (22 if i >= 24 else None), 512
 
     @staticmethod
     def _f32(entry) -> np.ndarray:
@@ -406,26 +427,33 @@ class OracleStage:
         p = f"blk.{i}"
         H, nh, nkv, hd = self.hidden, self.n_heads, self.n_kv, self.head_dim
         T = states.shape[0]
+        theta, rot, prop, src, win = self._attention_config(i)
         x = rms_norm(states, self._f32(self.t[f"{p}.attn_norm.weight"]))
         q_all = self._mm(f"{p}.attn_q.weight", x)
-        k_all = self._mm(f"{p}.attn_k.weight", x)
-        v_all = self._mm(f"{p}.attn_v.weight", x)
         q_all = per_head_rms_norm(q_all, self._f32(self.t[f"{p}.attn_q_norm.weight"]), nh, hd)
-        k_all = per_head_rms_norm(k_all, self._f32(self.t[f"{p}.attn_k_norm.weight"]), nkv, hd)
-        v_all = per_head_rms_norm(v_all, None, nkv, hd)
-        kc, vc = kv.setdefault(i, ([], []))
+        if src is None:
+            k_all = self._mm(f"{p}.attn_k.weight", x)
+            v_all = self._mm(f"{p}.attn_v.weight", x)
+            k_all = per_head_rms_norm(k_all, self._f32(self.t[f"{p}.attn_k_norm.weight"]), nkv, hd)
+            v_all = per_head_rms_norm(v_all, None, nkv, hd)
+            kc, vc = kv.setdefault(i, ([], []))
+        else:  # shared KV: the source layer's cache, already holding these positions (:1561-1640)
+            kc, vc = kv[src]
         att = np.empty((T, nh * hd), np.float32)
         for t in range(T):
-            q, k = q_all[t], k_all[t]
+            q = q_all[t]
             if self.rope_freqs is not None:
-                q = rope(q, nh, hd, self.rope_freqs, pos0 + t, self.rope_theta)
-                k = rope(k, nkv, hd, self.rope_freqs, pos0 + t, self.rope_theta)
-            v = v_all[t]
-            if self.kv_fp16:
-                k, v = fp16_round(k), fp16_round(v)
-            kc.append(k)
-            vc.append(v)
-            att[t] = gqa_attention(q, np.stack(kc), np.stack(vc), nh, nkv, hd, limit=pos0 + t + 1)
+                q = rope(q, nh, hd, self.rope_freqs, pos0 + t, theta, rot, prop)
+            if src is None:
+                k = k_all[t]
+                if self.rope_freqs is not None:
+                    k = rope(k, nkv, hd, self.rope_freqs, pos0 + t, theta, rot, prop)
+                v = v_all[t]
+                if self.kv_fp16:
+                    k, v = fp16_round(k), fp16_round(v)
+                kc.append(k)
+                vc.append(v)
+            att[t] = gqa_attention(q, np.stack(kc), np.stack(vc), nh, nkv, hd, limit=pos0 + t + 1, window=win)
         o = self._mm(f"{p}.attn_output.weight", att)
         o = rms_norm(o, self._f32(self.t[f"{p}.post_attention_norm.weight"]))
         states = o + states
