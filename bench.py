@@ -75,7 +75,11 @@ class ClockSampler:
                  "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "--format=csv,noheader,nounits", "-lms", "25"], stdout=self.f, stderr=subprocess.DEVNULL)
+            # the timed region starts once sampling has (nvidia-smi takes a moment to start)
+            t_end = time.time() + 3.0
+            while time.time() < t_end and self.path.stat().st_size == 0:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
