@@ -962,33 +962,88 @@ void put_index_entry(JsonWriter &w, const Slice &s, uint64_t pack_offset) {  // 
 
 }  // namespace
 
+namespace {
+
+// StageResidencyAdapter::load (lib.rs:3424-3453): the bundle, checked against itself and the GGUF
+// file, and the stage with that index.
+struct Adapter {
+  std::string model_name, arch;
+  std::vector<BundleStage> stages;
+  GgufFile f;
+  const BundleStage *st = nullptr;
+  bool load(const std::string &bundle_dir, const std::string &gguf_path, uint32_t stage_index, std::string &err) {
+    if (!load_bundle(bundle_dir, model_name, arch, stages, err)) return false;
+    if (!f.bytes.map_file(gguf_path, err) || !f.parse(err)) return false;
+    for (auto &s : stages)  // validate_against_gguf (lib.rs:3405-3422)
+      for (const auto *set : {&s.required, &s.optional})
+        for (auto &name : *set)
+          if (f.find(name) < 0) {
+            err = "Stage " + std::to_string(uint64_t(s.stage_index) + 1) + " references tensor " + name +
+                  " which is not present in GGUF";
+            return false;
+          }
+    for (auto &s : stages)
+      if (s.stage_index == stage_index) {
+        st = &s;
+        break;
+      }
+    if (!st) {
+      err = "Stage " + std::to_string(uint64_t(stage_index) + 1) + " not found in runtime bundle";
+      return false;
+    }
+    return true;
+  }
+  // read_slice (lib.rs:3606-3613): the slice's bytes inside the mapped file
+  const uint8_t *slice_bytes(const Slice &s, const std::string &gguf_path, std::string &err) const {
+    if (s.file_offset > f.bytes.size || s.byte_len > f.bytes.size - s.file_offset) {
+      err = "Tensor " + s.name + " slice runs past the end of " + gguf_path;
+      return nullptr;
+    }
+    return f.bytes.data + s.file_offset;
+  }
+};
+
+// sanitize_tensor_filename (lib.rs:3627-3636): ASCII letters, digits, '-' and '_' stay; every other
+// character (a whole UTF-8 sequence) becomes one '_'.
+std::string sanitize_tensor_filename(const std::string &name) {
+  std::string out;
+  for (size_t i = 0; i < name.size();) {
+    const unsigned char c = static_cast<unsigned char>(name[i]);
+    const bool keep = (c >= 'a' && c <= 'z') || (c >= 'A' && c <= 'Z') || (c >= '0' && c <= '9') || c == '-' ||
+                      c == '_';
+    out += keep ? char(c) : '_';
+    size_t len = 1;
+    if (c >= 0xF0) len = 4;
+    else if (c >= 0xE0) len = 3;
+    else if (c >= 0xC0) len = 2;
+    i += len;
+  }
+  return out;
+}
+
+}  // namespace
+
+bool materialize_stage_from_bundle(const std::string &bundle_dir, const std::string &gguf_path, uint32_t stage_index,
+                                   const std::string &out_dir, std::vector<std::string> &written, std::string &err) {
+  Adapter a;
+  if (!a.load(bundle_dir, gguf_path, stage_index, err) || !mkdirs(out_dir, err)) return false;
+  for (const Slice &s : a.st->req_slices) {  // materialize_required_tensors (lib.rs:3500-3510)
+    const uint8_t *b = a.slice_bytes(s, gguf_path, err);
+    if (!b) return false;
+    const std::string path = path_join(out_dir, sanitize_tensor_filename(s.name));
+    if (!put_file(path, std::string(reinterpret_cast<const char *>(b), size_t(s.byte_len)), err)) return false;
+    written.push_back(path);
+  }
+  return true;
+}
+
 bool pack_stage_from_bundle(const std::string &bundle_dir, const std::string &gguf_path, uint32_t stage_index,
                             bool include_optional, const std::string &out_dir, std::string &index_path,
                             std::string &err) {
-  std::string model_name, arch;
-  std::vector<BundleStage> stages;
-  if (!load_bundle(bundle_dir, model_name, arch, stages, err)) return false;
-  GgufFile f;
-  if (!f.bytes.map_file(gguf_path, err) || !f.parse(err)) return false;
-  // validate_against_gguf (lib.rs:3405-3422)
-  for (auto &st : stages)
-    for (const auto *set : {&st.required, &st.optional})
-      for (auto &name : *set)
-        if (f.find(name) < 0) {
-          err = "Stage " + std::to_string(uint64_t(st.stage_index) + 1) + " references tensor " + name +
-                " which is not present in GGUF";
-          return false;
-        }
-  const BundleStage *st = nullptr;
-  for (auto &s : stages)
-    if (s.stage_index == stage_index) {
-      st = &s;
-      break;
-    }
-  if (!st) {
-    err = "Stage " + std::to_string(uint64_t(stage_index) + 1) + " not found in runtime bundle";
-    return false;
-  }
+  Adapter a;
+  if (!a.load(bundle_dir, gguf_path, stage_index, err)) return false;
+  const BundleStage *st = a.st;
+  const std::string &model_name = a.model_name, &arch = a.arch;
   if (!mkdirs(out_dir, err)) return false;
   const std::string n = std::to_string(uint64_t(stage_index) + 1);
   const std::string pack_path = path_join(out_dir, "stage-" + n + "-required.pack");
@@ -1005,12 +1060,12 @@ bool pack_stage_from_bundle(const std::string &bundle_dir, const std::string &gg
   std::vector<uint64_t> offs;
   uint64_t off = 0;
   for (const Slice *s : slices) {
-    if (s->file_offset > f.bytes.size || s->byte_len > f.bytes.size - s->file_offset) {
+    const uint8_t *b = a.slice_bytes(*s, gguf_path, err);
+    if (!b) {
       fclose(pf);
-      err = "Tensor " + s->name + " slice runs past the end of " + gguf_path;
       return false;
     }
-    if (s->byte_len && fwrite(f.bytes.data + s->file_offset, 1, size_t(s->byte_len), pf) != size_t(s->byte_len)) {
+    if (s->byte_len && fwrite(b, 1, size_t(s->byte_len), pf) != size_t(s->byte_len)) {
       fclose(pf);
       err = "Failed to write " + pack_path;
       return false;
@@ -1171,6 +1226,53 @@ int sfc_gguf_metadata_u32(const sfc_gguf *g, const char *key, uint32_t *value) {
   return g->f.meta_u32(key, *value) ? SFC_OK : SFC_ABSENT;
 }
 
+int sfc_gguf_metadata_array(const sfc_gguf *g, const char *key, uint32_t *elem_type, uint64_t *count) {
+  clear_error();
+  SFC_REQUIRE(g && key && count, "null argument");
+  const GgufValue *v = g->f.get(key);
+  if (!v || v->type != 9) return SFC_ABSENT;
+  if (elem_type) *elem_type = uint32_t(v->u);
+  *count = uint64_t(v->arr.size());
+  return SFC_OK;
+}
+
+int sfc_gguf_metadata_f32_array(const sfc_gguf *g, const char *key, float *out, uint64_t cap, uint64_t *n) {
+  clear_error();
+  SFC_REQUIRE(g && key && n && (out || cap == 0), "null argument");
+  const GgufValue *v = g->f.get(key);
+  if (!v || v->type != 9) return SFC_ABSENT;
+  *n = uint64_t(v->arr.size());
+  for (size_t k = 0; k < v->arr.size() && k < cap; ++k) {  // metadata_f32_array (gguf.rs:262-277)
+    const GgufValue &e = v->arr[k];
+    switch (e.type) {
+      case 6:
+      case 12: out[k] = float(e.f); break;
+      case 5: out[k] = float(e.i); break;
+      case 4: out[k] = float(e.u); break;
+      default: out[k] = 0.0f;
+    }
+  }
+  return SFC_OK;
+}
+
+int sfc_gguf_metadata_array_string(const sfc_gguf *g, const char *key, uint64_t index, char *buf, uint64_t cap,
+                                   uint64_t *len) {
+  clear_error();
+  SFC_REQUIRE(g && key && (buf || cap == 0), "null argument");
+  const GgufValue *v = g->f.get(key);
+  if (!v || v->type != 9) return SFC_ABSENT;
+  SFC_REQUIRE(index < v->arr.size(), "array %s has %zu elements, index %llu", key, v->arr.size(),
+              (unsigned long long)index);
+  const std::string s = gguf_value_string(v->arr[size_t(index)]);  // metadata_string_array (gguf.rs:253-260)
+  if (len) *len = uint64_t(s.size());
+  if (cap > 0) {
+    const size_t k = size_t(std::min<uint64_t>(cap - 1, s.size()));
+    memcpy(buf, s.data(), k);
+    buf[k] = '\0';
+  }
+  return SFC_OK;
+}
+
 int sfc_gguf_block_indices(const sfc_gguf *g, uint32_t *out, uint64_t cap, uint64_t *n) {
   clear_error();
   SFC_REQUIRE(g && n && (out || cap == 0), "null argument");
@@ -1203,6 +1305,20 @@ int sfc_gguf_write_bundle(const sfc_gguf *g, const sfc_stage_split *splits, uint
     set_error("%s", err.c_str());
     return SFC_E_IO;
   }
+  return SFC_OK;
+}
+
+int sfc_materialize_stage(const char *bundle_dir, const char *gguf_path, uint32_t stage_index, const char *out_dir,
+                          uint64_t *n_written) {
+  clear_error();
+  SFC_REQUIRE(bundle_dir && gguf_path && out_dir, "null argument");
+  std::vector<std::string> written;
+  std::string err;
+  if (!materialize_stage_from_bundle(bundle_dir, gguf_path, stage_index, out_dir, written, err)) {
+    set_error("%s", err.c_str());
+    return SFC_E_IO;
+  }
+  if (n_written) *n_written = uint64_t(written.size());
   return SFC_OK;
 }
 

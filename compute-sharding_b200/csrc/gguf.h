@@ -82,6 +82,10 @@ bool parse_block_index(const std::string &name, uint32_t &idx);  // "blk.<u32>."
 // plan_for_splits + build_manifest + write_bundle (gguf.rs:366-751) into out_dir.
 bool gguf_write_bundle(const GgufFile &f, const std::vector<StageSplitC> &splits, const std::string &out_dir,
                        std::string &err);
+// StageResidencyAdapter::load + materialize_required_tensors (lib.rs:3424-3510): one file per
+// required tensor, named by sanitize_tensor_filename.
+bool materialize_stage_from_bundle(const std::string &bundle_dir, const std::string &gguf_path, uint32_t stage_index,
+                                   const std::string &out_dir, std::vector<std::string> &written, std::string &err);
 // StageResidencyAdapter::load + pack_required_tensors / pack_all_tensors (lib.rs:3283-3613).
 bool pack_stage_from_bundle(const std::string &bundle_dir, const std::string &gguf_path, uint32_t stage_index,
                             bool include_optional, const std::string &out_dir, std::string &index_path,

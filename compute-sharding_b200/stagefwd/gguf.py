@@ -56,11 +56,18 @@ _sig("sfc_gguf_find_tensor", ctypes.c_int, _P, ctypes.c_char_p, ctypes.POINTER(_
 _sig("sfc_gguf_metadata_key", ctypes.c_int, _P, _U64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_U32))
 _sig("sfc_gguf_metadata_string", ctypes.c_int, _P, ctypes.c_char_p, ctypes.c_char_p, _U64, ctypes.POINTER(_U64))
 _sig("sfc_gguf_metadata_u32", ctypes.c_int, _P, ctypes.c_char_p, ctypes.POINTER(_U32))
+_sig("sfc_gguf_metadata_array", ctypes.c_int, _P, ctypes.c_char_p, ctypes.POINTER(_U32), ctypes.POINTER(_U64))
+_sig("sfc_gguf_metadata_f32_array", ctypes.c_int, _P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), _U64,
+     ctypes.POINTER(_U64))
+_sig("sfc_gguf_metadata_array_string", ctypes.c_int, _P, ctypes.c_char_p, _U64, ctypes.c_char_p, _U64,
+     ctypes.POINTER(_U64))
 _sig("sfc_gguf_block_indices", ctypes.c_int, _P, ctypes.POINTER(_U32), _U64, ctypes.POINTER(_U64))
 _sig("sfc_gguf_even_split", ctypes.c_int, _P, _U32, ctypes.POINTER(StageSplit))
 _sig("sfc_gguf_write_bundle", ctypes.c_int, _P, ctypes.POINTER(StageSplit), _U32, ctypes.c_char_p)
 _sig("sfc_pack_stage", ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p, _U32, ctypes.c_int, ctypes.c_char_p,
      ctypes.c_char_p, _U64)
+_sig("sfc_materialize_stage", ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p, _U32, ctypes.c_char_p,
+     ctypes.POINTER(_U64))
 
 
 @dataclass(frozen=True)
@@ -172,6 +179,36 @@ class GgufFile:
                "metadata_string")
         return buf.raw[: int(n.value)].decode()
 
+    def metadata_string_array(self, key: str) -> list[str] | None:
+        """metadata_string_array (gguf.rs:253-260)."""
+        t, n = _U32(), _U64()
+        rc = _lib.sfc_gguf_metadata_array(self._h, key.encode(), ctypes.byref(t), ctypes.byref(n))
+        if rc == SFC_ABSENT:
+            return None
+        _check(rc, "metadata_string_array")
+        out = []
+        for i in range(int(n.value)):
+            ln = _U64()
+            _check(_lib.sfc_gguf_metadata_array_string(self._h, key.encode(), i, None, 0, ctypes.byref(ln)),
+                   "metadata_string_array")
+            buf = ctypes.create_string_buffer(int(ln.value) + 1)
+            _check(_lib.sfc_gguf_metadata_array_string(self._h, key.encode(), i, buf, len(buf), ctypes.byref(ln)),
+                   "metadata_string_array")
+            out.append(buf.raw[: int(ln.value)].decode())
+        return out
+
+    def metadata_f32_array(self, key: str) -> list[float] | None:
+        """metadata_f32_array (gguf.rs:262-277)."""
+        n = _U64()
+        rc = _lib.sfc_gguf_metadata_f32_array(self._h, key.encode(), None, 0, ctypes.byref(n))
+        if rc == SFC_ABSENT:
+            return None
+        _check(rc, "metadata_f32_array")
+        buf = (ctypes.c_float * max(int(n.value), 1))()
+        _check(_lib.sfc_gguf_metadata_f32_array(self._h, key.encode(), buf, n.value, ctypes.byref(n)),
+               "metadata_f32_array")
+        return [float(buf[i]) for i in range(int(n.value))]
+
     def metadata_u32(self, key: str) -> int | None:
         v = _U32()
         rc = _lib.sfc_gguf_metadata_u32(self._h, key.encode(), ctypes.byref(v))
@@ -219,3 +256,12 @@ def pack_stage(bundle_dir, gguf_path, stage_index: int, out_dir, include_optiona
     _check(_lib.sfc_pack_stage(_fs(bundle_dir), _fs(gguf_path), stage_index, int(include_optional), _fs(out_dir),
                                buf, len(buf)), "pack_stage")
     return Path(os.fsdecode(buf.value))
+
+
+def materialize_stage(bundle_dir, gguf_path, stage_index: int, out_dir) -> int:
+    """StageResidencyAdapter::load + materialize_required_tensors (lib.rs:3424-3510): one file per
+    required tensor of the stage in out_dir.  Returns the number of files written."""
+    n = _U64()
+    _check(_lib.sfc_materialize_stage(_fs(bundle_dir), _fs(gguf_path), stage_index, _fs(out_dir), ctypes.byref(n)),
+           "materialize_stage")
+    return int(n.value)

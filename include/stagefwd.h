@@ -298,6 +298,15 @@ int sfc_gguf_metadata_key(const sfc_gguf *g, uint64_t index, const char **key, u
 int sfc_gguf_metadata_string(const sfc_gguf *g, const char *key, char *buf, uint64_t cap, uint64_t *len);
 /* metadata_u32 (gguf.rs:279-287): u32, or u64 / i32 / i64 values that fit; else SFC_ABSENT. */
 int sfc_gguf_metadata_u32(const sfc_gguf *g, const char *key, uint32_t *value);
+/* An array value: its element type and length; SFC_ABSENT if the key is missing or not an array. */
+int sfc_gguf_metadata_array(const sfc_gguf *g, const char *key, uint32_t *elem_type, uint64_t *count);
+/* metadata_f32_array (gguf.rs:262-277): f32 / f64 / i32 / u32 elements as f32, any other type 0.
+ * *n = the array's length, the first cap written.  SFC_ABSENT if not an array. */
+int sfc_gguf_metadata_f32_array(const sfc_gguf *g, const char *key, float *out, uint64_t cap, uint64_t *n);
+/* metadata_string_array (gguf.rs:253-260): element `index` as text (metadata_value_to_string);
+ * same buffer rule as sfc_gguf_metadata_string. */
+int sfc_gguf_metadata_array_string(const sfc_gguf *g, const char *key, uint64_t index, char *buf, uint64_t cap,
+                                   uint64_t *len);
 /* block_indices (gguf.rs:219-233): sorted distinct n of blk.<n>.*; *n = count, first cap written. */
 int sfc_gguf_block_indices(const sfc_gguf *g, uint32_t *out, uint64_t cap, uint64_t *n);
 /* suggest_even_stage_split (gguf.rs:307-329): out[stages]; the first (layers % stages) stages take
@@ -314,6 +323,12 @@ int sfc_gguf_write_bundle(const sfc_gguf *g, const sfc_stage_split *splits, uint
  * index_path (cap bytes, NUL included) when cap > 0. */
 int sfc_pack_stage(const char *bundle_dir, const char *gguf_path, uint32_t stage_index, int include_optional,
                    const char *out_dir, char *index_path, uint64_t cap);
+/* StageResidencyAdapter::load + materialize_required_tensors (lib.rs:3424-3510; the
+ * bin/materialize_stage_required.rs tool): each required tensor of the stage as its own file in
+ * out_dir (created), named by sanitize_tensor_filename (lib.rs:3627-3636: characters other than
+ * ASCII letters, digits, '-' and '_' become '_'). */
+int sfc_materialize_stage(const char *bundle_dir, const char *gguf_path, uint32_t stage_index, const char *out_dir,
+                          uint64_t *n_written);
 /* A stage straight from a GGUF file (no pack): the layout's layers start..end plus, as the
  * runtime plan would give it, rope_freqs and the shared auxiliaries, token_embd on the head (and on
  * the tail when the file has no output.weight: tied logits) and output* on the tail.  Tensors are

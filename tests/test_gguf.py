@@ -12,7 +12,7 @@ from gguf_util import ARR, BOOL, F32, F64, I32, I64, STR, U8, U32, U64, gguf_byt
 
 sfg = pytest.importorskip("stagefwd.gguf")
 from stagefwd import StageError  # noqa: E402
-from stagefwd.gguf import GgufFile, StageSplit, pack_stage  # noqa: E402
+from stagefwd.gguf import GgufFile, StageSplit, materialize_stage, pack_stage  # noqa: E402
 from stagefwd.pipeline import even_stage_split  # noqa: E402
 
 
@@ -57,6 +57,17 @@ def test_gguf_py_fixture_parses_identically(mixed):
                      "blk.1.ffn_down.weight": "Layer", "blk.2.post_ffw_norm.weight": "Layer",
                      "per_layer_token_embd.weight": "SharedAuxiliary", "output_norm.weight": "TailOnly",
                      "fixture.unknown": "UnknownGlobal"}
+    # array metadata (gguf.rs:253-277)
+    assert f.metadata_string_array("fixture.arr_str") == ["a", "b c", ""]
+    assert f.metadata_string_array("fixture.arr_f32") == ["0.5", "1.25", "-3"]
+    assert f.metadata_f32_array("fixture.arr_f32") == [0.5, 1.25, -3.0]
+    assert f.metadata_f32_array("fixture.arr_i32") == [1.0, -2.0, 3.0]
+    assert f.metadata_f32_array("fixture.arr_u64") == [0.0, 0.0]  # only f32 / f64 / i32 / u32 convert
+    assert f.metadata_f32_array("fixture.arr_empty") is None  # gguf-py's writer drops empty arrays
+    e = GgufFile.parse_bytes(gguf_bytes([("empty", ARR, (F32, [])), ("words", ARR, (STR, ["x", "é"]))], []))
+    assert e.metadata_f32_array("empty") == [] and e.metadata_string_array("empty") == []
+    assert e.metadata_string("empty") == "[]" and e.metadata_string_array("words") == ["x", "é"]
+    assert f.metadata_f32_array("fixture.u32") is None and f.metadata_string_array("absent") is None
     # parse_bytes of the same bytes gives the same view
     g = GgufFile.parse_bytes(path.read_bytes())
     assert g.tensors == f.tensors and g.metadata_keys == f.metadata_keys
@@ -265,3 +276,20 @@ def test_even_split_matches_pipeline_rule():
     assert f.suggest_even_stage_split(0) is None and f.suggest_even_stage_split(43) is None
     g = GgufFile.parse_bytes(gguf_bytes([], []))
     assert g.inferred_layer_count() is None and g.suggest_even_stage_split(1) is None
+
+
+def test_materialize_required_tensors(tmp_path):
+    """materialize_required_tensors (lib.rs:3500-3510) with sanitize_tensor_filename (:3627-3636)."""
+    path, section = toy_gguf(tmp_path)
+    GgufFile.parse_file(path).write_bundle(TOY_SPLITS, tmp_path / "bundle")
+    out = tmp_path / "materialized"
+    assert materialize_stage(tmp_path / "bundle", path, 0, out) == 2
+    assert sorted(p.name for p in out.iterdir()) == ["blk_0_attn_q_weight", "token_embd_weight"]
+    assert (out / "token_embd_weight").read_bytes() == section[:100]
+    assert (out / "blk_0_attn_q_weight").read_bytes() == section[100:200]
+    # a multi-byte character becomes one '_'
+    data = gguf_bytes([("llama.block_count", U32, 1)], [("blk.0.\u00e9-x_y", [1], 0, 0)], data=bytes(8))
+    (tmp_path / "u.gguf").write_bytes(data)
+    GgufFile.parse_file(tmp_path / "u.gguf").write_bundle([StageSplit(0, 0, 0)], tmp_path / "ub")
+    assert materialize_stage(tmp_path / "ub", tmp_path / "u.gguf", 0, tmp_path / "um") == 1
+    assert [p.name for p in (tmp_path / "um").iterdir()] == ["blk_0__-x_y"]
