@@ -25,6 +25,7 @@
 #include "capi_common.h"
 #include "gguf.h"
 #include "json.h"
+#include "payload.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -1314,6 +1315,56 @@ int sfc_sample_tail(sfc_stage *h, const float *hidden, int64_t n, uint32_t *toke
   *token = uint32_t(t);
   if (score) *score = s;
   return SFC_OK;
+}
+
+// The hidden rows of a hand-off payload, checked as decode_hidden_states (real_forward.rs:1826-1850).
+static int payload_rows(const sfc_stage *h, const void *bytes, uint64_t n, uint64_t hidden_dim, PayloadSections &s,
+                        std::vector<float> &rows) {
+  SFC_REQUIRE(bytes || n == 0, "null argument");
+  stage_tensor_sections(static_cast<const uint8_t *>(bytes), n, s);
+  SFC_REQUIRE(hidden_dim != 0, "Hidden-state hidden_dim must be nonzero");
+  SFC_REQUIRE(s.hidden_len % (hidden_dim * 4) == 0,
+              "Hidden-state byte length %llu is not a multiple of hidden_dim * 4 = %llu",
+              (unsigned long long)s.hidden_len, (unsigned long long)(hidden_dim * 4));
+  SFC_REQUIRE(hidden_dim == uint64_t(h->hidden), "payload hidden_dim %llu, stage hidden size %d",
+              (unsigned long long)hidden_dim, h->hidden);
+  SFC_REQUIRE(s.hidden_len > 0, "Hidden-state payload is empty");
+  rows.resize(size_t(s.hidden_len / 4));
+  memcpy(rows.data(), s.hidden, size_t(s.hidden_len));  // any alignment in, aligned floats out
+  return SFC_OK;
+}
+
+int sfc_continue_forward_bytes(sfc_stage *h, const char *request_id, const void *bytes, uint64_t n,
+                               uint64_t hidden_dim, void *out, uint64_t cap, uint64_t *out_len) {
+  clear_error();
+  SFC_REQUIRE(h && request_id && out_len, "null argument");
+  SFC_REQUIRE(!h->is_head, "Head stage should use begin_prompt, not continue_forward");
+  PayloadSections s;
+  std::vector<float> in;
+  int rc = payload_rows(h, bytes, n, hidden_dim, s, in);
+  if (rc) return rc;
+  const uint64_t need = encoded_stage_tensor_bytes(s.hidden_len, s.aux_len);
+  *out_len = need;
+  SFC_REQUIRE(out && cap >= need, "output holds %llu bytes, the payload needs %llu", (unsigned long long)cap,
+              (unsigned long long)need);
+  const std::string aux(reinterpret_cast<const char *>(s.aux), s.aux ? size_t(s.aux_len) : 0);  // out may be bytes
+  std::vector<float> res(in.size());
+  rc = sfc_continue_forward(h, request_id, in.data(), int64_t(in.size() / size_t(h->hidden)), res.data());
+  if (rc) return rc;
+  encode_stage_tensor(reinterpret_cast<const uint8_t *>(res.data()), s.hidden_len,
+                      reinterpret_cast<const uint8_t *>(aux.data()), aux.size(), static_cast<uint8_t *>(out));
+  return SFC_OK;
+}
+
+int sfc_sample_tail_bytes(sfc_stage *h, const void *bytes, uint64_t n, uint64_t hidden_dim, uint32_t *token,
+                          float *score) {
+  clear_error();
+  SFC_REQUIRE(h && token, "null argument");
+  PayloadSections s;
+  std::vector<float> rows;
+  int rc = payload_rows(h, bytes, n, hidden_dim, s, rows);
+  if (rc) return rc;
+  return sfc_sample_tail(h, rows.data(), int64_t(rows.size() / size_t(h->hidden)), token, score);  // last row
 }
 
 int sfc_forward_dev(sfc_stage *h, const char *const *request_ids, const int32_t *seq_tokens, int n_seq,

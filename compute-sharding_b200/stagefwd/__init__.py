@@ -104,6 +104,11 @@ _sig("sfc_session_len", _I64, _P, ctypes.c_char_p)
 _sig("sfc_session_fill_synthetic", _I, _P, ctypes.c_char_p, _I64, _U64)
 _sig("sfc_generate_greedy", _I, _P, ctypes.c_char_p, _P, _I64, _I64, _P)
 _sig("sfc_last_profile", _I, _P, ctypes.POINTER(Profile))
+_PU64 = ctypes.POINTER(_U64)
+_sig("sfc_stage_tensor_sections", _I, ctypes.c_char_p, _U64, _PU64, _PU64, _PU64, _PU64)
+_sig("sfc_encode_stage_tensor_bytes", _I, ctypes.c_char_p, _U64, ctypes.c_char_p, _U64, _P, _U64, _PU64)
+_sig("sfc_continue_forward_bytes", _I, _P, ctypes.c_char_p, ctypes.c_char_p, _U64, _U64, _P, _U64, _PU64)
+_sig("sfc_sample_tail_bytes", _I, _P, ctypes.c_char_p, _U64, _U64, ctypes.POINTER(_U32), ctypes.POINTER(_F))
 
 lib = _lib
 
@@ -137,6 +142,31 @@ def exported_symbols() -> list[str]:
     import re
     text = HEADER_PATH.read_text()
     return sorted(set(re.findall(r"\b(sfc_[a-z0-9_]+)\s*\(", text)))
+
+
+# ---------------------------------------------------------------- hand-off payloads (StageTensor::bytes)
+def stage_tensor_byte_sections(payload: bytes) -> tuple[bytes, bytes | None, bool]:
+    """stage_tensor_byte_sections (lib.rs:75-96): (hidden bytes, aux bytes or None, framed)."""
+    ho, hl, ao, al = _U64(), _U64(), _U64(), _U64()
+    rc = _lib.sfc_stage_tensor_sections(payload, len(payload), ctypes.byref(ho), ctypes.byref(hl), ctypes.byref(ao),
+                                        ctypes.byref(al))
+    if rc not in (0, 1):
+        _check(rc, "stage_tensor_byte_sections")
+    hidden = payload[ho.value: ho.value + hl.value]
+    aux = payload[ao.value: ao.value + al.value] if al.value else None
+    return hidden, aux, rc == 0
+
+
+def encode_stage_tensor_bytes(hidden: bytes, aux: bytes | None = None) -> bytes:
+    """encode_stage_tensor_bytes (lib.rs:98-118)."""
+    aux = aux or b""
+    n = _U64()
+    _check(_lib.sfc_encode_stage_tensor_bytes(hidden, len(hidden), aux, len(aux), None, 0, ctypes.byref(n)),
+           "encode_stage_tensor_bytes")
+    out = ctypes.create_string_buffer(max(int(n.value), 1))
+    _check(_lib.sfc_encode_stage_tensor_bytes(hidden, len(hidden), aux, len(aux), out, n.value, ctypes.byref(n)),
+           "encode_stage_tensor_bytes")
+    return out.raw[: int(n.value)]
 
 
 # ---------------------------------------------------------------- kernel-level API (torch tensors)
@@ -327,6 +357,21 @@ class CudaStageBackend:
         _check(_lib.sfc_continue_forward(self.h, request_id.encode(), hidden.ctypes.data, hidden.shape[0],
                                          out.ctypes.data), "continue_forward")
         return out
+
+    def continue_forward_bytes(self, request_id: str, payload: bytes, hidden_dim: int) -> bytes:
+        """continue_forward on StageTensor::bytes (bare or stb1-framed rows; the aux section is
+        carried through)."""
+        n = _U64()
+        out = ctypes.create_string_buffer(len(payload) + 16)
+        _check(_lib.sfc_continue_forward_bytes(self.h, request_id.encode(), payload, len(payload), hidden_dim, out,
+                                               len(out), ctypes.byref(n)), "continue_forward_bytes")
+        return out.raw[: int(n.value)]
+
+    def sample_tail_bytes(self, payload: bytes, hidden_dim: int) -> tuple[int, float]:
+        tok, sc = _U32(0), _F(0)
+        _check(_lib.sfc_sample_tail_bytes(self.h, payload, len(payload), hidden_dim, ctypes.byref(tok),
+                                          ctypes.byref(sc)), "sample_tail_bytes")
+        return int(tok.value), float(sc.value)
 
     def sample_tail(self, hidden) -> tuple[int, float]:
         hidden = np.ascontiguousarray(np.atleast_2d(hidden), dtype=np.float32)

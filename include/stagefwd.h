@@ -212,6 +212,27 @@ int sfc_sample_tree(sfc_stage *h, const float *hidden, const int32_t *parent, co
  * the session by n_path.  Call on every stage after sfc_sample_tree. */
 int sfc_commit_tree(sfc_stage *h, const char *request_id, const int32_t *path, int64_t n_path);
 
+/* Hand-off payloads as the reference's StageTensor::bytes: f32 little-endian rows [T][hidden], bare
+ * or framed "stb1" | u32 hidden_len | u32 aux_len | hidden | aux (crates/stage-forward-lab/src/
+ * lib.rs:36-118).  sfc_stage_tensor_sections: stage_tensor_byte_sections — offsets and lengths of
+ * the two sections; SFC_ABSENT (with the whole buffer as the hidden section) when the bytes are not
+ * a well-formed frame.  sfc_encode_stage_tensor_bytes: encode_stage_tensor_bytes — bare hidden
+ * bytes without aux, else the frame; out = NULL queries the size. */
+int sfc_stage_tensor_sections(const void *bytes, uint64_t n, uint64_t *hidden_offset, uint64_t *hidden_len,
+                              uint64_t *aux_offset, uint64_t *aux_len);
+int sfc_encode_stage_tensor_bytes(const void *hidden, uint64_t hidden_len, const void *aux, uint64_t aux_len,
+                                  void *out, uint64_t cap, uint64_t *out_len);
+/* continue_forward on a StageTensor payload (real_forward.rs:2054-2254): decodes the hidden rows
+ * (decode_hidden_states, :1826-1850: the byte length must be a multiple of hidden_dim * 4), runs
+ * sfc_continue_forward and writes the output rows framed with the input's aux section unchanged
+ * (:2383-2387); *out_len = the output size (also set when cap is too small).  out may be bytes
+ * itself but must not otherwise overlap it. */
+int sfc_continue_forward_bytes(sfc_stage *h, const char *request_id, const void *bytes, uint64_t n,
+                               uint64_t hidden_dim, void *out, uint64_t cap, uint64_t *out_len);
+/* sample_tail on a StageTensor payload: the last hidden row (decode_hidden_state, real_forward.rs:1818-1824). */
+int sfc_sample_tail_bytes(sfc_stage *h, const void *bytes, uint64_t n, uint64_t hidden_dim, uint32_t *token,
+                          float *score);
+
 /* Session management (real_forward.rs:294-317; rollback lib.rs:2236-2269). */
 int sfc_clear_decode_session(sfc_stage *h, const char *request_id);
 int sfc_rollback_kv(sfc_stage *h, const char *request_id, int64_t keep);
