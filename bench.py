@@ -112,6 +112,16 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- reference arm (CPU)
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_decode_sample(n_steps: int, prompt_len: int = 8):
     """The reference's CPU stage path restated (oracle, kind 'port') on all host cores:
     42-layer greedy decode tokens/s.  Returns (tokens/s, threads, description)."""
@@ -146,7 +156,8 @@ def run_reference(args):
             "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": bs1_config(world),
-            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc,
+                             "cpu": cpu_model()},
             "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -311,7 +322,8 @@ def run_single(args):
                 "d2h_bytes_per_step": HIDDEN * 4 + 8,
                 "path": "begin_token_ids + sample_tail through the C ABI with host buffers each token"},
         "roofline": roof,
-        "cpu_baseline": {"value": cpu_tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc},
+        "cpu_baseline": {"value": cpu_tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc,
+                         "cpu": cpu_model()},
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
