@@ -1181,11 +1181,14 @@ int sfc_stage_open_gguf(const char *gguf_path, const sfc_layout *layout, const s
     HostTensor ht;
     ht.name = t.name;
     ht.type = int(t.type);
+    double elems = 1.0;
     for (uint64_t d : t.dims) {
       SFC_REQUIRE(d < (uint64_t(1) << 40), "tensor %s: dimension %llu too large", t.name.c_str(),
                   (unsigned long long)d);
       ht.dims.push_back(int64_t(d));
+      elems *= double(d);
     }
+    SFC_REQUIRE(elems < 281474976710656.0, "tensor %s: %.0f elements is too many", t.name.c_str(), elems);  // 2^48
     const int64_t gb = gguf_tensor_bytes(ht.type, ht.dims);
     const uint64_t off = f.data_offset + t.offset;
     if (gb >= 0) {
