@@ -293,3 +293,28 @@ def test_materialize_required_tensors(tmp_path):
     GgufFile.parse_file(tmp_path / "u.gguf").write_bundle([StageSplit(0, 0, 0)], tmp_path / "ub")
     assert materialize_stage(tmp_path / "ub", tmp_path / "u.gguf", 0, tmp_path / "um") == 1
     assert [p.name for p in (tmp_path / "um").iterdir()] == ["blk_0__-x_y"]
+
+
+def test_written_json_has_serde_pretty_layout(tmp_path):
+    """Every JSON file the bundle and pack writers produce is laid out exactly as serde_json's pretty
+    printer lays it out (two-space indent, `"key": value`, one element per line, `[]` when empty,
+    lowercase \\u00XX escapes, no trailing newline) -- which for these documents is what Python's
+    json.dumps(indent=2, ensure_ascii=False) prints, field order kept."""
+    section = bytes(64)
+    meta = [("general.name", STR, 'q"uote\\\\ \x01 ctl é'), ("general.architecture", STR, "toy"),
+            ("llama.block_count", U32, 3), ("llama.embedding_length", U32, 8)]
+    tensors = [("token_embd.weight", [4, 2], 0, 0), ("blk.0.w", [2], 0, 32), ("blk.1.w", [2], 0, 40),
+               ("blk.2.w", [2], 0, 48), ("output_norm.weight", [2], 0, 56)]
+    path = tmp_path / "m.gguf"
+    path.write_bytes(gguf_bytes(meta, tensors, data=section))
+    f = GgufFile.parse_file(path)
+    f.write_bundle(f.suggest_even_stage_split(3), tmp_path / "b")
+    pack_stage(tmp_path / "b", path, 1, tmp_path / "p", include_optional=True)
+    files = sorted((tmp_path / "b").glob("*.json")) + sorted((tmp_path / "p").glob("*.json"))
+    assert len(files) == 1 + 3 + 3 + 3 + 1
+    for p in files:
+        text = p.read_text()
+        assert text == json.dumps(json.loads(text), indent=2, ensure_ascii=False), p.name
+    m = json.loads((tmp_path / "b" / "model-shard-manifest.json").read_text())
+    assert m["model_name"] == 'q"uote\\\\ \x01 ctl é' and m["hidden_size"] == 8
+    assert [r["role"] for r in m["runtime_plan"]] == ["head", "middle", "tail"]
