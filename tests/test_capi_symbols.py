@@ -55,3 +55,23 @@ def test_stage_open_rejects_bad_index_name(tmp_path):
     bad.write_text("{}")
     with pytest.raises(sf.StageError, match="index.json"):
         sf.CudaStageBackend(bad).load_layout("m", "s", 0, 0, True, True)
+
+
+def test_gguf_and_payload_entry_points_validate_on_the_host(tmp_path):
+    import ctypes
+    import stagefwd as sf
+    import stagefwd.gguf  # noqa: F401  (declares the GGUF prototypes)
+    with pytest.raises(sf.StageError, match="Failed to open"):
+        sf.CudaStageBackend(gguf_path=tmp_path / "absent.gguf").load_layout("m", "s", 0, 0, True, True)
+    junk = tmp_path / "junk.gguf"
+    junk.write_bytes(b"GGML" + bytes(60))
+    with pytest.raises(sf.StageError, match="Not a GGUF file"):
+        sf.CudaStageBackend(gguf_path=junk).load_layout("m", "s", 0, 0, True, True)
+    n = ctypes.c_uint64()
+    assert sf.lib.sfc_continue_forward_bytes(None, b"r", b"", 0, 4, None, 0, ctypes.byref(n)) == -1
+    assert b"null argument" in sf.lib.sfc_last_error()
+    buf = ctypes.create_string_buffer(64)
+    assert sf.lib.sfc_pack_stage(str(tmp_path / "no-bundle").encode(), str(junk).encode(), 0, 0,
+                                 str(tmp_path / "out").encode(), buf, 64) == -3
+    assert b"Failed to read" in sf.lib.sfc_last_error() and b"model-shard-manifest.json" in sf.lib.sfc_last_error()
+    assert sf.lib.sfc_gguf_open(None, None) == -1
