@@ -262,6 +262,19 @@ int apply_options(sfc_stage *h, const sfc_options *o) {
 
 // Builds device tensors, infers the config, allocates caches and buffers.
 int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
+  {  // Per-layer embeddings (PLE: a layer with inp_gate and proj, real_forward.rs:1753-1778) are not
+     // implemented here; refuse such a stage instead of running it without them.
+    std::set<int> gate, proj;
+    for (const auto &ht : hts) {
+      const int li = layer_of(ht.name);
+      if (li < 0) continue;
+      if (ht.name.find(".inp_gate.weight") != std::string::npos) gate.insert(li);
+      if (ht.name.find(".proj.weight") != std::string::npos) proj.insert(li);
+    }
+    for (int li : gate)
+      SFC_REQUIRE(!proj.count(li), "layer %d has per-layer embedding tensors (inp_gate, proj): PLE is not "
+                                  "supported by this backend", li);
+  }
   // classification + config inference (real_forward.rs:2258-2283)
   std::map<int, Layer> layer_map;
   std::vector<std::pair<HostTensor *, DevTensor *>> uploads;

@@ -19,6 +19,7 @@ from __future__ import annotations
 import ctypes
 import json
 import math
+import struct
 import os
 from dataclasses import dataclass, field
 from pathlib import Path
@@ -223,6 +224,7 @@ class ModelSpec:
     types: dict = field(default_factory=lambda: {
         "attn_q": Q4_K, "attn_k": Q4_K, "attn_v": Q6_K, "attn_output": Q4_K,
         "ffn_gate": Q4_K, "ffn_up": Q4_K, "ffn_down": Q6_K, "token_embd": F16})
+    ple_dim: int = 0             # > 0: per-layer embedding inputs (PLE) of this width, F16 matrices
 
     @property
     def q_dim(self):
@@ -251,13 +253,19 @@ class ModelSpec:
             (f"{p}.ffn_up.weight", t["ffn_up"], [H, F]),
             (f"{p}.ffn_down.weight", t["ffn_down"], [F, H]),
             (f"{p}.post_ffw_norm.weight", F32, [H]),
-        ]
+        ] + ([(f"{p}.inp_gate.weight", F16, [H, self.ple_dim]), (f"{p}.proj.weight", F16, [self.ple_dim, H]),
+              (f"{p}.post_norm.weight", F32, [H])] if self.ple_dim else [])
 
     def stage_tensor_shapes(self, start: int, end: int, is_head: bool, is_tail: bool):
         out = []
         if is_head or is_tail:
             out.append(("token_embd.weight", self.types["token_embd"], [self.hidden, self.vocab]))
         out.append(("rope_freqs.weight", F32, [self.head_dim // 2]))
+        if self.ple_dim:  # shared auxiliary tensors (gguf.rs:774-781): every stage holds them
+            P = self.ple_dim * self.n_layers
+            out += [("per_layer_token_embd.weight", F16, [P, self.vocab]),
+                    ("per_layer_model_proj.weight", F16, [self.hidden, P]),
+                    ("per_layer_proj_norm.weight", F32, [self.ple_dim])]
         for i in range(start, end + 1):
             out.extend(self.layer_tensor_shapes(i))
         if is_tail:
@@ -273,7 +281,7 @@ class ModelSpec:
             return np.ones(in_dim, np.float32).view(np.uint8).copy()
         if t == F32:  # norm weights
             return synth_tensor(F32, key, rows, in_dim, self.norm_sigma, 1.0)
-        if name == "token_embd.weight":
+        if name in ("token_embd.weight", "per_layer_token_embd.weight"):
             return synth_tensor(t, key, rows, in_dim, self.embd_sigma)
         return synth_tensor(t, key, rows, in_dim, self.w_sigma)
 
@@ -384,7 +392,33 @@ class OracleStage:
                     raise ValueError(f"real_forward stage {layout.stage_id} (layers {layout.start_layer}-"
                                      f"{layout.end_layer}) is unsupported for {layout.model_id}: layer {i} requires "
                                      f"shared KV from layer {src} outside this stage")
+        # PLE (real_forward.rs:2320-2338): width from per_layer_proj_norm, layer count from the projection
+        pn, mp = tensors.get("per_layer_proj_norm.weight"), tensors.get("per_layer_model_proj.weight")
+        self.ple_dim = int(pn[1][0]) if pn is not None else 0
+        self.ple_layers = int(mp[1][1]) // self.ple_dim if self.ple_dim and mp is not None else 0
+        self.last_ple = None
         self.sessions: dict[str, dict] = {}
+
+    def compute_ple_inputs(self, ids, embeds: np.ndarray) -> np.ndarray:
+        """compute_ple_inputs (real_forward.rs:1157-1299) for every model layer: [T][layers][ple_dim].
+        The model projection of the scaled token embedding, times hidden^-1/2, RMS-normed per ple_dim
+        chunk with per_layer_proj_norm (eps 1e-6), plus the token's per-layer embedding row times
+        sqrt(ple_dim), all times 2^-1/2."""
+        P, L = self.ple_dim, self.ple_layers
+        if P == 0 or L == 0:
+            raise ValueError(f"PLE not configured (ple_dim={P}, num_layers={L})")
+        proj = self._mm("per_layer_model_proj.weight", embeds)  # [T][L*P]
+        proj = proj * np.float32(np.float32(embeds.shape[1]) ** np.float32(-0.5))
+        norm = self._f32(self.t["per_layer_proj_norm.weight"])
+        proj = rms_norm(proj.reshape(-1, P), norm, 1e-6).reshape(len(ids), L * P)  # rms_norm_chunked_inplace
+        t, dims, raw = self.t["per_layer_token_embd.weight"]
+        rb = bytes_per_row(t, dims[0])
+        embed_scale, combine_scale = np.float32(math.sqrt(P)), np.float32(2.0 ** -0.5)
+        out = np.empty((len(ids), L * P), np.float32)
+        for i, tid in enumerate(ids):
+            row = dequantize_rows(t, raw[int(tid) * rb:(int(tid) + 1) * rb], 1, dims[0])[0]
+            out[i] = (proj[i] + row * embed_scale) * combine_scale
+        return out.reshape(len(ids), L, P)
 
     def _e4b(self) -> bool:
         return ("gemma-4-e4b" in self.layout.model_id and self.hidden == 2560 and self.head_dim in (256, 512))
@@ -422,7 +456,7 @@ class OracleStage:
             out[i] = dequantize_rows(t, raw[int(tid) * rb:(int(tid) + 1) * rb], 1, H)[0] * scale
         return out
 
-    def _layer(self, i: int, states: np.ndarray, pos0: int, kv: dict) -> np.ndarray:
+    def _layer(self, i: int, states: np.ndarray, pos0: int, kv: dict, ple=None) -> np.ndarray:
         """forward_layer_seq, real_forward.rs:1483-1793 (generic schedule, no PLE)."""
         p = f"blk.{i}"
         H, nh, nkv, hd = self.hidden, self.n_heads, self.n_kv, self.head_dim
@@ -464,14 +498,23 @@ class OracleStage:
         d = self._mm(f"{p}.ffn_down.weight", a)
         d = rms_norm(d, self._f32(self.t[f"{p}.post_ffw_norm.weight"]))
         states = d + states
+        ig, pj = self.t.get(f"{p}.inp_gate.weight"), self.t.get(f"{p}.proj.weight")
+        if ig is not None and pj is not None and ple is not None:  # real_forward.rs:1753-1778
+            gated = gelu_tanh_mul(self._mm(f"{p}.inp_gate.weight", states), ple)
+            pr = self._mm(f"{p}.proj.weight", gated)
+            pn = self.t.get(f"{p}.post_norm.weight")
+            if pn is not None:
+                pr = rms_norm(pr, self._f32(pn))
+            states = pr + states
         sc = self.t.get(f"{p}.layer_output_scale.weight")
         if sc is not None:
             states = states * self._f32(sc)[0]
         return states
 
-    def run_layers(self, states: np.ndarray, pos0: int, kv: dict) -> np.ndarray:
+    def run_layers(self, states: np.ndarray, pos0: int, kv: dict, ple_all=None) -> np.ndarray:
+        """run_stage_layers (real_forward.rs:1992-2052): PLE inputs by global layer index."""
         for i in self.layers:
-            states = self._layer(i, states, pos0, kv)
+            states = self._layer(i, states, pos0, kv, None if ple_all is None else ple_all[:, i, :])
         return states
 
     def _session(self, req: str, n: int, fresh: bool) -> dict:
@@ -489,17 +532,21 @@ class OracleStage:
         if len(ids) == 0:
             raise ValueError("Empty prompt")
         s = self._session(req, len(ids), fresh=(len(ids) > 1 and not append))
-        out = self.run_layers(self.embed(ids), s["seq_len"], s["kv"])
+        emb = self.embed(ids)
+        # the head computes every layer's PLE inputs; later stages receive them in the aux section
+        self.last_ple = self.compute_ple_inputs(ids, emb) if self.ple_dim else None
+        out = self.run_layers(emb, s["seq_len"], s["kv"], self.last_ple)
         s["seq_len"] += len(ids)
         return out
 
-    def continue_forward(self, req: str, hidden: np.ndarray, append: bool = False) -> np.ndarray:
-        """continue_forward_inner (real_forward.rs:2054-2254), same session rule."""
+    def continue_forward(self, req: str, hidden: np.ndarray, append: bool = False, ple_all=None) -> np.ndarray:
+        """continue_forward_inner (real_forward.rs:2054-2254), same session rule; ple_all: the
+        per-layer inputs [T][layers][ple_dim] from the head (the aux section's PLE part)."""
         if self.layout.is_head:
             raise ValueError("Head stage should use begin_prompt, not continue_forward")
         hidden = np.ascontiguousarray(np.atleast_2d(hidden), np.float32)
         s = self._session(req, hidden.shape[0], fresh=(hidden.shape[0] > 1 and not append))
-        out = self.run_layers(hidden, s["seq_len"], s["kv"])
+        out = self.run_layers(hidden, s["seq_len"], s["kv"], ple_all)
         s["seq_len"] += hidden.shape[0]
         return out
 
@@ -618,3 +665,47 @@ def bfs_tree(branching, max_nodes: int):
                 nxt.append(len(parent) - 1)
         frontier = nxt
     return parent
+
+
+# ---------------------------------------------------------------- stage aux section
+def prefix_hashes(token_ids) -> list:
+    """prefix_hashes (real_forward.rs:319-333): 64-bit FNV-1a over each token id's little-endian
+    bytes, one running hash per prefix."""
+    h, out = 0xCBF29CE484222325, []
+    for tid in token_ids:
+        for b in int(tid).to_bytes(4, "little"):
+            h = ((h ^ b) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+        out.append(h)
+    return out
+
+
+def encode_prompt_aux(ple_all, ple_dim: int, hashes=()) -> bytes | None:
+    """encode_prompt_aux (real_forward.rs:1852-1894): "rsa1" | u32 seq_len | u32 layers | u32 ple_dim |
+    u32 n_hashes | f32 [seq][layers][ple_dim] | u64 hashes; None when both parts are empty."""
+    seq = 0 if ple_all is None else int(ple_all.shape[0])
+    layers = 0 if ple_all is None or seq == 0 else int(ple_all.shape[1])
+    if seq * layers * ple_dim == 0 and not hashes:
+        return None
+    head = b"rsa1" + struct.pack("<IIII", seq, layers, ple_dim, len(hashes))
+    body = b"" if ple_all is None else np.ascontiguousarray(ple_all, np.float32).tobytes()
+    return head + body + b"".join(struct.pack("<Q", h) for h in hashes)
+
+
+def decode_prompt_aux(b: bytes):
+    """decode_prompt_aux (real_forward.rs:1896-1990): (ple_all [seq][layers][ple_dim], hashes) from an
+    "rsa1" section, or from the older "rpl1" one (PLE only)."""
+    if len(b) >= 20 and b[:4] == b"rsa1":
+        seq, layers, pdim, nh = struct.unpack_from("<IIII", b, 4)
+        want = 20 + seq * layers * pdim * 4 + nh * 8
+        if len(b) != want:
+            raise ValueError(f"Invalid prompt-aux byte length {len(b)} (expected {want})")
+        ple = np.frombuffer(b, np.float32, seq * layers * pdim, 20).reshape(seq, layers, pdim)
+        off = 20 + seq * layers * pdim * 4
+        return ple, list(struct.unpack_from(f"<{nh}Q", b, off))
+    if len(b) < 16 or b[:4] != b"rpl1":
+        raise ValueError("Invalid prompt-aux payload")
+    seq, layers, pdim = struct.unpack_from("<III", b, 4)
+    want = 16 + seq * layers * pdim * 4
+    if len(b) != want:
+        raise ValueError(f"Invalid prompt-aux byte length {len(b)} (expected {want})")
+    return np.frombuffer(b, np.float32, seq * layers * pdim, 16).reshape(seq, layers, pdim), []

@@ -75,3 +75,15 @@ def test_gguf_and_payload_entry_points_validate_on_the_host(tmp_path):
                                  str(tmp_path / "out").encode(), buf, 64) == -3
     assert b"Failed to read" in sf.lib.sfc_last_error() and b"model-shard-manifest.json" in sf.lib.sfc_last_error()
     assert sf.lib.sfc_gguf_open(None, None) == -1
+
+
+def test_stage_with_per_layer_embeddings_is_refused(tmp_path):
+    """A stage whose layers carry PLE tensors is refused at load (before any device work) instead of
+    running without them."""
+    import stagefwd as sf
+    import stage_oracle as so
+    spec = so.ModelSpec(hidden=256, n_heads=2, n_kv=1, head_dim=128, ffn=512, vocab=300, n_layers=2, seed=3,
+                        ple_dim=64)
+    idx = so.write_pack(tmp_path, "stage-0", "full", 0, so.synth_stage(spec, 0, 1, True, True))
+    with pytest.raises(sf.StageError, match="PLE is not supported"):
+        sf.CudaStageBackend(idx).load_layout("m", "s", 0, 1, True, True)
