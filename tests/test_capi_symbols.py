@@ -87,3 +87,15 @@ def test_stage_with_per_layer_embeddings_is_refused(tmp_path):
     idx = so.write_pack(tmp_path, "stage-0", "full", 0, so.synth_stage(spec, 0, 1, True, True))
     with pytest.raises(sf.StageError, match="PLE is not supported"):
         sf.CudaStageBackend(idx).load_layout("m", "s", 0, 1, True, True)
+
+
+def test_header_is_plain_c(tmp_path):
+    """include/stagefwd.h is the FFI boundary: it must compile as C99 (what a cgo / bindgen / ctypes
+    binding sees), warning-free."""
+    import shutil
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-x", "c", str(HEADER)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
