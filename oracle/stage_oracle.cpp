@@ -396,11 +396,14 @@ void or_rope_apply(float *x, int n_heads, int head_dim, const float *freqs, int6
   }
 }
 
-void or_gqa_attention(const float *q, const float *kc, const float *vc, int64_t n_pos, int64_t limit,
-                      int64_t window, int n_heads, int n_kv, int head_dim, float *out) {
+// Cached key / value rows come either as one [n_pos][n_kv * head_dim] matrix or as one pointer per
+// row (the stage driver's per-position rows, read in place); the arithmetic is the same.
+extern "C++" {
+template <typename KRow, typename VRow>
+static void gqa_attention_impl(const float *q, KRow krow, VRow vrow, int64_t n_pos, int64_t limit, int64_t window,
+                               int n_heads, int n_kv, int head_dim, float *out) {
   int groups = n_heads / n_kv;
   int64_t seq_len = limit >= 0 ? std::min(limit, n_pos) : n_pos;
-  int64_t row = int64_t(n_kv) * head_dim;
   for (int64_t i = 0; i < int64_t(n_heads) * head_dim; ++i) out[i] = 0.f;
   if (seq_len <= 0) return;
   int64_t w0 = window > 0 ? std::max<int64_t>(0, seq_len - window) : 0;
@@ -409,7 +412,7 @@ void or_gqa_attention(const float *q, const float *kc, const float *vc, int64_t 
     int kvh = h / groups;
     const float *qh = q + int64_t(h) * head_dim;
     for (int64_t t = w0; t < seq_len; ++t) {
-      const float *k = kc + t * row + int64_t(kvh) * head_dim;
+      const float *k = krow(t) + int64_t(kvh) * head_dim;
       float s = 0.f;
       for (int d = 0; d < head_dim; ++d) s += qh[d] * k[d];
       scores[t - w0] = s;
@@ -430,11 +433,27 @@ void or_gqa_attention(const float *q, const float *kc, const float *vc, int64_t 
     }
     float *o = out + int64_t(h) * head_dim;
     for (int64_t t = w0; t < seq_len; ++t) {
-      const float *v = vc + t * row + int64_t(kvh) * head_dim;
+      const float *v = vrow(t) + int64_t(kvh) * head_dim;
       float wt = scores[t - w0];
       for (int d = 0; d < head_dim; ++d) o[d] += wt * v[d];
     }
   }
+}
+}  // extern "C++"
+
+void or_gqa_attention(const float *q, const float *kc, const float *vc, int64_t n_pos, int64_t limit,
+                      int64_t window, int n_heads, int n_kv, int head_dim, float *out) {
+  const int64_t row = int64_t(n_kv) * head_dim;
+  gqa_attention_impl(
+      q, [&](int64_t t) { return kc + t * row; }, [&](int64_t t) { return vc + t * row; }, n_pos, limit, window,
+      n_heads, n_kv, head_dim, out);
+}
+
+void or_gqa_attention_rows(const float *q, const float *const *krows, const float *const *vrows, int64_t n_pos,
+                           int64_t limit, int64_t window, int n_heads, int n_kv, int head_dim, float *out) {
+  gqa_attention_impl(
+      q, [&](int64_t t) { return krows[t]; }, [&](int64_t t) { return vrows[t]; }, n_pos, limit, window, n_heads,
+      n_kv, head_dim, out);
 }
 
 int or_logits_top_k(int type, const uint8_t *raw, int64_t vocab, int64_t hidden, const float *h, int k,

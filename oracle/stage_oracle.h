@@ -64,6 +64,9 @@ void or_rope_apply(float *x, int n_heads, int head_dim, const float *freqs, int6
 void or_gqa_attention(const float *q, const float *kc, const float *vc, int64_t n_pos,
                       int64_t limit, int64_t window, int n_heads, int n_kv, int head_dim,
                       float *out);
+// Same, with the cached rows as one pointer per position (read in place).
+void or_gqa_attention_rows(const float *q, const float *const *krows, const float *const *vrows, int64_t n_pos,
+                           int64_t limit, int64_t window, int n_heads, int n_kv, int head_dim, float *out);
 
 /* real_math.rs:2119-2488 (matmul_raw_top_k). logits over rows [0, vocab), softcap if cap>0,
  * argmax with ties to the lowest index, top-k descending (k may be 0).

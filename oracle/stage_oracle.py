@@ -64,6 +64,7 @@ class _Lib:
         L.or_gelu_tanh_mul_inplace.argtypes = [P, P, I64]
         L.or_rope_apply.argtypes = [P, I, I, P, I64, ctypes.c_uint32, F, I, I]
         L.or_gqa_attention.argtypes = [P, P, P, I64, I64, I64, I, I, I, P]
+        L.or_gqa_attention_rows.argtypes = [P, P, P, I64, I64, I64, I, I, I, P]
         L.or_logits_top_k.argtypes = [I, P, I64, I64, P, I, F, P, P, P, P, P, I]
         L.or_mix64.argtypes = [U64, U64]
         L.or_mix64.restype = U64
@@ -146,6 +147,25 @@ def rope(x: np.ndarray, n_heads: int, head_dim: int, freqs, position: int, theta
     lib().or_rope_apply(_p(x), n_heads, head_dim, _p(f), f.shape[0], position, theta,
                         head_dim if rotary_dim is None else rotary_dim, int(proportional))
     return x
+
+
+def _row_pointers(rows) -> np.ndarray:
+    ptr = np.empty(len(rows), np.uintp)
+    for i, r in enumerate(rows):
+        if r.dtype != np.float32 or not r.flags.c_contiguous:
+            raise ValueError("cached rows must be contiguous float32")
+        ptr[i] = r.ctypes.data
+    return ptr
+
+
+def gqa_attention_rows(q: np.ndarray, krows: list, vrows: list, n_heads: int, n_kv: int, head_dim: int,
+                       limit: int = -1, window: int = 0) -> np.ndarray:
+    """gqa_attention over a cache held as one array per position (read in place, no copy)."""
+    q = np.ascontiguousarray(q, np.float32)
+    kp, vp = _row_pointers(krows), _row_pointers(vrows)
+    out = np.empty(n_heads * head_dim, np.float32)
+    lib().or_gqa_attention_rows(_p(q), _p(kp), _p(vp), len(krows), limit, window, n_heads, n_kv, head_dim, _p(out))
+    return out
 
 
 def gqa_attention(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, n_heads: int, n_kv: int, head_dim: int,
@@ -487,7 +507,7 @@ class OracleStage:
                     k, v = fp16_round(k), fp16_round(v)
                 kc.append(k)
                 vc.append(v)
-            att[t] = gqa_attention(q, np.stack(kc), np.stack(vc), nh, nkv, hd, limit=pos0 + t + 1, window=win)
+            att[t] = gqa_attention_rows(q, kc, vc, nh, nkv, hd, limit=pos0 + t + 1, window=win)
         o = self._mm(f"{p}.attn_output.weight", att)
         o = rms_norm(o, self._f32(self.t[f"{p}.post_attention_norm.weight"]))
         states = o + states
@@ -549,6 +569,18 @@ class OracleStage:
         out = self.run_layers(hidden, s["seq_len"], s["kv"], ple_all)
         s["seq_len"] += hidden.shape[0]
         return out
+
+    def fill_session_synthetic(self, req: str, n_pos: int, seed: int = 0):
+        """A session whose cache holds n_pos seeded N(0,1) keys and values in every layer that has
+        its own cache (benchmarks: a decode step's cost does not depend on the cached values)."""
+        rng = np.random.default_rng(seed)
+        kv = {}
+        width = self.n_kv * self.head_dim
+        for i in self.layers:
+            if self._attention_config(i)[3] is None:
+                kv[i] = ([r for r in rng.standard_normal((n_pos, width), np.float32)],
+                         [r for r in rng.standard_normal((n_pos, width), np.float32)])
+        self.sessions[req] = {"seq_len": n_pos, "kv": kv}
 
     def rollback(self, req: str, keep: int):
         s = self.sessions[req]
