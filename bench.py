@@ -4,6 +4,7 @@ HBM bandwidth, against the reference's CPU stage path timed on this host.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N ... bench.py --gpus N   (one pipeline stage per GPU)
+  python bench.py --case decode|gemv|gemm [...]      (fixed workloads for profilers, no JSON line)
 
 One JSON line on rank 0.  `value` = bs1 greedy decode tokens/s (whole job); `bs64` = batched
 decode tokens/s; `roofline` = the Q4_K GEMV (10240 x 2560, one token, cold L2) against the
@@ -17,6 +18,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -36,6 +38,9 @@ EMBD_BYTES = VOCAB * HIDDEN * 2
 # dram__bytes_read.sum + dram__bytes_write.sum of one qgemv_kernel<1,1> launch on that shape, from
 # the ncu capture summarised in profiles/qgemv_q4k_10240x2560_1tok.md
 GEMV_DRAM_BYTES = 14_810_368
+# greedy steps compared between the pipeline and a one-GPU run of the whole model (N > 1)
+CHECK_STEPS = 64
+BS64_WORKLOAD = "64 sequences, contexts uniform 512..3584 (seeded synthetic KV), 1 token each per step"
 
 
 def bs1_config(world: int = 1) -> dict:
@@ -61,14 +66,18 @@ def peaks():
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, enabled: bool = True):
         self.index = index
+        self.enabled = enabled
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        fd, name = tempfile.mkstemp(prefix="sfc_clocks_", suffix=".csv")
+        os.close(fd)
+        self.path = Path(name)
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),
@@ -96,6 +105,7 @@ class ClockSampler:
     def summary(self):
         try:
             rows = [r.split(",") for r in self.path.read_text().strip().splitlines() if r.strip()]
+            self.path.unlink()
         except Exception:
             return None
         if not rows:
@@ -290,7 +300,7 @@ def run_single(args):
         bs64_step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    bsteps = max(2, args.steps // 8)
+    bsteps = max(16, args.steps // 4)
     e0.record()
     for _ in range(bsteps):
         bs64_step()
@@ -312,7 +322,7 @@ def run_single(args):
         "config": bs1_config(1),
         "bs1_step_bandwidth_gbs": token_bytes / (bs1_s / args.steps) / 1e9,
         "bs64": {"value": bs64_tps, "unit": "tokens/s", "steps": bsteps, "ms_per_step": bs64_s * 1e3 / bsteps,
-                 "workload": "64 sequences, contexts uniform 512..3584 (seeded synthetic KV), 1 token each per step"},
+                 "workload": BS64_WORKLOAD},
         "gemv": {"value": roof["achieved"], "unit": "GB/s", "frac_of_hbm": roof["frac"]},
         "spec_verify": dict(spec_res, workload="1024 cached positions, 16-node draft tree (2-2-2-2, BFS, truncated) "
                                                "of random tokens: tree-masked forward of 42 layers, logits over "
@@ -331,13 +341,14 @@ def run_single(args):
 
 
 def run_pipeline(args):
+    import datetime
     import torch
     import torch.distributed as dist
     import stagefwd as sf
     from stagefwd.pipeline import CudaCompute, Pipeline, even_stage_split, make_groups
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     ranks = make_groups(rank, world)
     start, end = even_stage_split(N_LAYERS, world)[rank]
     be = sf.CudaStageBackend(synthetic=sf.ModelShape(), device=local, rope_theta=10000.0, max_ctx=4096,
@@ -347,7 +358,26 @@ def run_pipeline(args):
     comp = CudaCompute(be, HIDDEN, 512, dev)
     pipe = Pipeline(comp, ranks, HIDDEN, dev)
     rng = np.random.default_rng(1234)
-    prompt = torch.from_numpy(rng.integers(0, VOCAB, PROMPT).astype(np.int64)).to(dev)
+    prompt_np = rng.integers(0, VOCAB, PROMPT).astype(np.int64)
+    prompt = torch.from_numpy(prompt_np).to(dev)
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t)
+
+    # greedy stream of the pipeline on the seeded prompt; rank 0 also runs the whole model on one
+    # GPU and compares (identical tokens for CHECK_STEPS steps)
+    check = pipe.generate("check", prompt, CHECK_STEPS)
+    match = None
+    if rank == 0:
+        full = sf.CudaStageBackend(synthetic=sf.ModelShape(), device=local, rope_theta=10000.0,
+                                   max_ctx=PROMPT + CHECK_STEPS + 8, max_sessions=1).load_layout(
+            "synthetic-gemma", "full", 0, N_LAYERS - 1, True, True)
+        ref = full.generate_greedy("check", prompt_np.astype(np.uint32), CHECK_STEPS)
+        full.close()
+        match = check.cpu().tolist() == ref.tolist()
+    be.clear_decode_session("check")
 
     # bs1
     pipe.generate("warm", prompt, max(args.warmup, 3))
@@ -358,61 +388,58 @@ def run_pipeline(args):
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     k0 = sf.kernel_launches()
-    with ClockSampler(local) as clk:
+    # clocks are sampled on rank 0's GPU only: one sampler process per rank slowed the ranks
+    with ClockSampler(local, enabled=rank == 0) as clk:
         e0.record()
         for _ in range(args.steps):
             tok = pipe.step(["bs1"], [1], tok if tok is not None else torch.zeros(1, dtype=torch.int64, device=dev))
         e1.record()
         torch.cuda.synchronize()
     dist.barrier()
-    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    bs1_s = float(t)
+    bs1_s = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     launches = sf.kernel_launches() - k0
 
     # e2e: the same bs1 decode through the public pipeline API, each step's input token copied
-    # from pinned host memory on the head and the sampled token read back to the host
+    # from pinned host memory on the head and the sampled token read back to the host; timed by
+    # the host clock on every rank (max over ranks)
     htok = torch.zeros(1, dtype=torch.int64, pin_memory=True)
     if ranks.is_head:
         htok.copy_(tok.view(1))
     dist.barrier()
     torch.cuda.synchronize()
-    e0.record()
+    t0 = time.perf_counter()
     for _ in range(args.steps):
         x = htok.to(dev, non_blocking=True) if ranks.is_head else None
         nxt = pipe.step(["bs1"], [1], x)
         if ranks.is_head:
             htok.copy_(nxt.view(1))
-    e1.record()
     torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
     dist.barrier()
-    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_s = float(t)
 
-    # bs64: 8 microbatches of 8 sequences
+    # bs64: contexts 512..3584, as one microbatch per stage (the fastest schedule here) and as 8
+    # microbatches of 8 sequences (the schedule the workload states)
     ctx = rng.integers(512, 3585, 64)
     names = [f"b{i}" for i in range(64)]
-    for i, n in enumerate(names):
-        be.fill_session_synthetic(n, int(ctx[i]), seed=100 + i)
-    # one microbatch per stage keeps every stage busy; a stage's GEMM launch costs about the same for
-    # 8 or 64 rows, so more, smaller microbatches only add launches (8 x 8 on 2 GPUs: 1725 tok/s)
-    n_mb = world
-    mb = 64 // n_mb
-    mbs = [names[mb * m: mb * m + mb] for m in range(n_mb)]
-    tokens = [torch.from_numpy(rng.integers(0, VOCAB, mb).astype(np.int64)).to(dev) for _ in range(n_mb)]
-    pipe.decode_microbatched(mbs, tokens, max(args.warmup, 2))
-    torch.cuda.synchronize()
-    dist.barrier()
-    bsteps = max(2, args.steps // 8)
-    e0.record()
-    pipe.decode_microbatched(mbs, tokens, bsteps)
-    e1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    bs64_s = float(t)
+    bsteps = max(16, args.steps // 4)
+    bs64 = {}
+    for label, n_mb in (("one_microbatch_per_stage", world), ("microbatches_of_8", 8)):
+        for i, n in enumerate(names):
+            be.fill_session_synthetic(n, int(ctx[i]), seed=100 + i)
+        mb = 64 // n_mb
+        mbs = [names[mb * m: mb * m + mb] for m in range(n_mb)]
+        tokens = [torch.from_numpy(rng.integers(0, VOCAB, mb).astype(np.int64)).to(dev) for _ in range(n_mb)]
+        pipe.decode_microbatched(mbs, tokens, max(args.warmup, 3))
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record()
+        pipe.decode_microbatched(mbs, tokens, bsteps)
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+        bs64[label] = {"value": 64 * bsteps / t, "unit": "tokens/s", "steps": bsteps, "ms_per_step": 1e3 * t / bsteps,
+                       "microbatches": f"{n_mb} x {mb} sequences"}
     be.close()
     roof = None
     if rank == 0:
@@ -421,20 +448,72 @@ def run_pipeline(args):
         roof["peak_kind"] = peak_kind
     dist.barrier()
     if rank == 0:
+        best = max(bs64.values(), key=lambda d: d["value"])
         line = {"metric": METRIC, "value": args.steps / bs1_s, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": bs1_s * 1e3 / args.steps,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic",
                 "config": dict(bs1_config(world), split=even_stage_split(N_LAYERS, world),
                                handoff="NCCL send/recv of f32 hidden rows"),
-                "bs64": {"value": 64 * bsteps / bs64_s, "unit": "tokens/s", "steps": bsteps,
-                         "microbatches": f"{n_mb} x {mb} sequences"},
+                "tokens_match_1gpu": match,
+                "tokens_match_steps": CHECK_STEPS,
+                "bs64": dict(best, workload=BS64_WORKLOAD, schedules=bs64),
                 "e2e": {"value": args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 8,
                         "d2h_bytes_per_step": 8,
-                        "path": "Pipeline.step per token, token from pinned host memory to the head and back"},
+                        "path": "Pipeline.step per token, token from pinned host memory to the head and back; "
+                                "host clock, max over ranks"},
                 "roofline": roof, "gpu_launches": launches, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- fixed workloads for profilers
+def case_decode(steps: int, ctx: int, batch: int):
+    """`steps` eager decode steps of `batch` sequences after `ctx` seeded cached positions, through
+    the device-pointer stage calls (no CUDA graph, so every kernel is its own launch)."""
+    import torch
+    import stagefwd as sf
+    dev = torch.device("cuda")
+    shape = sf.ModelShape()
+    be = sf.CudaStageBackend(synthetic=shape, rope_theta=10000.0, max_ctx=max(ctx + steps + 8, 64),
+                             max_sessions=batch + 2, max_batch_tokens=max(batch, 8)).load_layout(
+        "synthetic-gemma", "full", 0, shape.n_layers - 1, True, True)
+    names = [f"s{i}" for i in range(batch)]
+    for i, n in enumerate(names):
+        be.fill_session_synthetic(n, ctx, seed=100 + i)
+    ids = torch.arange(batch, dtype=torch.int32, device=dev) * 997 + 11
+    out = torch.empty(batch, shape.hidden, device=dev)
+    tk = torch.empty(batch, dtype=torch.int64, device=dev)
+    sc = torch.empty(batch, dtype=torch.float32, device=dev)
+    for _ in range(steps):
+        be.forward_dev(names, [1] * batch, ids_dev=ids, out_dev=out, append=True)
+        be.sample_dev(out, tk, sc)
+        ids.copy_(tk.to(torch.int32))
+    torch.cuda.synchronize()
+    be.close()
+    print("decode", steps, "steps, batch", batch, "ctx", ctx, "tokens", tk.tolist()[:8])
+
+
+def case_matmul(launches: int, tokens: int):
+    """`launches` calls of sfc_matmul on the Q4_K 10240 x 2560 shape with `tokens` tokens (the GEMV
+    from 1 to 7 tokens, the tensor-core GEMM from 8), over weight copies larger than twice the L2."""
+    import torch
+    import stagefwd as sf
+    dev = torch.device("cuda")
+    rows, k = 10240, 2560
+    wbytes = rows * (k // 256) * 144
+    copies = int(np.ceil(2 * (126 << 20) / wbytes)) + 2
+    ws = [sf.prepare_weights(sf.Q4_K, sf.synth_tensor(sf.Q4_K, 1, f"gemv.{i}", rows, k, 0.02), rows, k)
+          for i in range(copies)]
+    x = torch.randn(tokens, k, device=dev)
+    y = torch.empty(tokens, rows, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    for i in range(launches):
+        rc = sf.lib.sfc_matmul(sf.Q4_K, ws[i % copies].data_ptr(), rows, k, x.data_ptr(), tokens, y.data_ptr(), st)
+        if rc:
+            raise RuntimeError(f"sfc_matmul failed: {rc}")
+    torch.cuda.synchronize()
+    print("matmul", launches, "launches of Q4_K", rows, "x", k, "with", tokens, "tokens over", copies, "weight copies")
 
 
 def main():
@@ -443,7 +522,21 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--case", choices=["decode", "gemv", "gemm"],
+                    help="run a fixed workload for a profiler instead of the benchmark")
+    ap.add_argument("--ctx", type=int, default=512, help="--case decode: cached positions per sequence")
+    ap.add_argument("--batch", type=int, default=1, help="--case decode: sequences per step")
+    ap.add_argument("--tokens", type=int, default=64, help="--case gemm: tokens per launch")
+    ap.add_argument("--launches", type=int, default=8, help="--case gemv/gemm: launches")
     args = ap.parse_args()
+    if args.case:
+        import torch
+        torch.cuda.set_device(0)
+        if args.case == "decode":
+            case_decode(args.steps, args.ctx, args.batch)
+        else:
+            case_matmul(args.launches, 1 if args.case == "gemv" else args.tokens)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -70,6 +70,15 @@ int sfc_device_error(unsigned *code) {
 
 int64_t sfc_kernel_launches(void) { return g_kernel_launches; }
 
+int sfc_selftest_bounded_wait(unsigned spin_limit, int complete, void *stream) {
+  clear_error();
+  SFC_REQUIRE(spin_limit > 0, "spin_limit must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SFC_CUDA(wait_selftest(spin_limit, complete ? 1 : 0, st));
+  SFC_CUDA(cudaStreamSynchronize(st));
+  return SFC_OK;
+}
+
 int64_t sfc_weight_device_bytes(int ggml_type, int64_t rows, int64_t in_dim) {
   if (!type_supported(ggml_type) || rows < 0) {
     set_error("unsupported ggml type %d", ggml_type);

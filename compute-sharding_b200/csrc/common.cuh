@@ -86,9 +86,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after MBAR_SPIN_LIMIT polls and records DEV_WAIT_TIMEOUT.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, unsigned *err) {
-  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i)
+// Bounded wait: gives up after `limit` polls (MBAR_SPIN_LIMIT by default) and records
+// DEV_WAIT_TIMEOUT in *err.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, unsigned *err,
+                                                  unsigned limit = MBAR_SPIN_LIMIT) {
+  for (unsigned i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   if (err) atomicExch(err, DEV_WAIT_TIMEOUT);
   return false;

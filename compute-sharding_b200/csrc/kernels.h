@@ -4,16 +4,21 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace sfc {
 
 // ---- launch helpers
+// SM count of the current device, cached per device ordinal (concurrent first calls on one device
+// store the same value).
 inline int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
+  int n = dev >= 0 ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (n <= 0) {
+    if (dev < 0 || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev >= 0) cache[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -214,6 +219,10 @@ size_t attention_scratch_bytes(int64_t n_tok, const AttnParams &p, int64_t max_k
 cudaError_t attention(const float *q, float *out, KVLayer kv, const SeqInfo *seqs, const int32_t *tok_seq,
                       const int32_t *tok_limit, const uint64_t *tok_mask, int64_t n_tok, int64_t max_keys,
                       const AttnParams &p, void *scratch, size_t scratch_bytes, cudaStream_t st);
+
+// Bounded-wait self-test (ops.cu): one bounded mbarrier wait of `limit` polls on a barrier that
+// completes (complete = 1) or never does (complete = 0, which records DEV_WAIT_TIMEOUT).
+cudaError_t wait_selftest(unsigned limit, int complete, cudaStream_t st);
 
 // Decode-graph bookkeeping (see ops.cu).
 cudaError_t decode_advance(const int64_t *tok, int64_t *out_tokens, int32_t *step, SeqInfo *seqs, int n_seq,

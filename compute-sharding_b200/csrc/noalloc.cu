@@ -24,7 +24,10 @@ constexpr size_t NOALLOC_SCRATCH_BYTES = 64 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 
 // Device address of g_noalloc_scratch, looked up once per device with that device current.
-// (In host code the symbol itself is only a host-side stand-in, not a device address.)
+// (In host code the symbol itself is only a host-side stand-in, not a device address.)  The
+// cached address stays valid while the device's context does; after a cudaDeviceReset by the
+// host process the module is loaded again and the address may differ, so the entry point's
+// contract excludes calls on a device after it has been reset.
 static std::mutex g_noalloc_mu;
 static void *g_noalloc_ptr[64] = {};
 

@@ -441,4 +441,25 @@ cudaError_t attention(const float *q, float *out, KVLayer kv, const SeqInfo *seq
                     p.n_heads, p.head_dim, ns);
 }
 
+// ---------------------------------------------------------------- bounded-wait self-test
+// One thread waits, through the same bounded mbarrier wait the streaming kernels use, on a barrier
+// that either completes (complete = 1: the thread arrives first) or that nothing ever arrives on
+// (complete = 0).  No copy is in flight at any time, so giving up leaves nothing behind: the wait
+// runs out after `limit` polls, records DEV_WAIT_TIMEOUT in *err and the kernel returns.
+__global__ void wait_selftest_kernel(unsigned limit, int complete, unsigned *err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  if (complete) asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bar)) : "memory");
+  mbar_wait_bounded(&bar, 0, err, limit);
+}
+
+cudaError_t wait_selftest(unsigned limit, int complete, cudaStream_t st) {
+  unsigned *err = device_error_ptr();
+  if (!err) return cudaErrorInvalidValue;
+  wait_selftest_kernel<<<1, 32, 0, st>>>(limit, complete, err);
+  return cudaGetLastError();
+}
+
 }  // namespace sfc

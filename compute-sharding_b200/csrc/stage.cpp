@@ -58,6 +58,9 @@ struct Layer {
 struct Session {
   int slot = -1;
   int64_t len = 0;
+  // The draft tree of the last sfc_forward_tree (its rows sit after `len`, not yet committed):
+  // parents of its nodes, empty when none is pending.  Any other forward call clears it.
+  std::vector<int32_t> tree_parent;
 };
 
 // Pinned host staging ring for per-call tables (safe reuse via events).
@@ -646,9 +649,12 @@ int session_for(sfc_stage *h, const std::string &id, bool restart, Session **out
       return SFC_E_NOMEM;
     }
     h->slot_used[slot] = 1;
-    it = h->sessions.emplace(id, Session{slot, 0}).first;
+    Session fresh;
+    fresh.slot = slot;
+    it = h->sessions.emplace(id, fresh).first;
   }
   if (restart) it->second.len = 0;
+  it->second.tree_parent.clear();  // a forward writes the rows a pending draft tree occupied
   *out = &it->second;
   return SFC_OK;
 }
@@ -1490,6 +1496,7 @@ int sfc_forward_tree(sfc_stage *h, const char *request_id, const uint32_t *ids, 
   h->tree_active = false;
   s->len = len0;  // tentative: sfc_commit_tree keeps the accepted path
   if (rc) return rc;
+  s->tree_parent.assign(parent, parent + n);
   SFC_CUDA(cudaMemcpyAsync(out_hidden, h->resid, size_t(n) * h->hidden * 4, cudaMemcpyDeviceToHost, st));
   SFC_CUDA(cudaStreamSynchronize(st));
   return SFC_OK;
@@ -1559,9 +1566,14 @@ int sfc_commit_tree(sfc_stage *h, const char *request_id, const int32_t *path, i
   auto it = h->sessions.find(request_id);
   SFC_REQUIRE(it != h->sessions.end(), "unknown session %s", request_id);
   Session *s = &it->second;
-  SFC_REQUIRE(n_path >= 1 && n_path <= 64 && path[0] == 0, "path must start at the root and hold 1..64 nodes");
+  const int64_t pending = int64_t(s->tree_parent.size());
+  SFC_REQUIRE(pending > 0, "session %s has no draft tree pending (sfc_forward_tree first; a tree is committed once)",
+              request_id);
+  SFC_REQUIRE(n_path >= 1 && n_path <= pending && path[0] == 0, "path must start at the root and hold 1..%lld nodes",
+              (long long)pending);
   for (int64_t i = 1; i < n_path; ++i)
-    SFC_REQUIRE(path[i] > path[i - 1], "path nodes must increase");
+    SFC_REQUIRE(path[i] > 0 && path[i] < pending && s->tree_parent[size_t(path[i])] == path[i - 1],
+                "path[%lld] = %d is not a child of node %d in the pending tree", (long long)i, path[i], path[i - 1]);
   SFC_REQUIRE(s->len + path[n_path - 1] < h->max_ctx, "path leaves the cache");
   SFC_CUDA(cudaSetDevice(h->device));
   cudaStream_t st = h->stream;
@@ -1572,6 +1584,7 @@ int sfc_commit_tree(sfc_stage *h, const char *request_id, const int32_t *path, i
     SFC_CUDA(cudaStreamSynchronize(st));
   }
   s->len += n_path;
+  s->tree_parent.clear();
   return SFC_OK;
 }
 
@@ -1592,6 +1605,7 @@ int sfc_rollback_kv(sfc_stage *h, const char *request_id, int64_t keep) {
   SFC_REQUIRE(keep >= 0 && keep <= it->second.len, "keep_count %lld exceeds session length %lld", (long long)keep,
               (long long)it->second.len);
   it->second.len = keep;
+  it->second.tree_parent.clear();
   return SFC_OK;
 }
 

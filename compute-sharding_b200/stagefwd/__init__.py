@@ -73,6 +73,7 @@ _sig("sfc_abi_version", _I)
 _sig("sfc_last_error", ctypes.c_char_p)
 _sig("sfc_device_error", _I, ctypes.POINTER(ctypes.c_uint))
 _sig("sfc_kernel_launches", ctypes.c_int64)
+_sig("sfc_selftest_bounded_wait", _I, ctypes.c_uint, _I, _P)
 _sig("sfc_weight_device_bytes", _I64, _I, _I64, _I64)
 _sig("sfc_prepare_weights", _I, _I, _P, _I64, _I64, _P, _P)
 _sig("sfc_dequantize_rows", _I, _I, _P, _I64, _I64, _P, _P)
@@ -262,9 +263,15 @@ def kernel_launches() -> int:
 
 
 def device_error() -> int:
+    """Read and clear the device error word (0 none, 1 a bounded wait ran out, 2 a bad argument)."""
     c = ctypes.c_uint(0)
     _check(_lib.sfc_device_error(ctypes.byref(c)), "sfc_device_error")
     return c.value
+
+
+def selftest_bounded_wait(spin_limit: int, complete: bool, stream=None):
+    """One bounded mbarrier wait of `spin_limit` polls on a barrier that completes or never does."""
+    _check(_lib.sfc_selftest_bounded_wait(spin_limit, int(complete), _stream(stream)), "sfc_selftest_bounded_wait")
 
 
 # ---------------------------------------------------------------- stage-level API

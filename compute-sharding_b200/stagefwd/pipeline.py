@@ -158,17 +158,25 @@ class Pipeline:
     def decode_microbatched(self, microbatches, tokens, n_steps: int):
         """Batched decode with microbatches in flight across stages.  `microbatches` is a list
         of request-id lists; `tokens[m]` holds the next input token of each sequence of
-        microbatch m (head only).  Sends and receives keep one order on every rank."""
+        microbatch m (head only).  On return the head's `tokens[m]` are the tokens sampled at
+        the last step (the next inputs), whatever the number of ranks.  Sends and receives keep
+        one order on every rank: the tail sends every step's samples, the head receives step
+        s-1's samples before step s and the last step's after the loop."""
         M = len(microbatches)
+        two_way = self.r.world > 1
+
+        def recv_tokens(m):
+            nxt = torch.empty(len(microbatches[m]), dtype=torch.int64, device=self.device)
+            dist.recv(nxt, src=self.r.world - 1, group=self.r.back_group)
+            tokens[m] = nxt
+
         for s in range(n_steps):
             for m in range(M):
                 ids = microbatches[m]
                 n = len(ids)
                 if self.r.is_head:
-                    if s > 0 and self.r.world > 1:
-                        nxt = torch.empty(n, dtype=torch.int64, device=self.device)
-                        dist.recv(nxt, src=self.r.world - 1, group=self.r.back_group)
-                        tokens[m] = nxt
+                    if s > 0 and two_way:
+                        recv_tokens(m)
                     x = tokens[m]
                 else:
                     x = self._recv_rows(n)
@@ -177,13 +185,15 @@ class Pipeline:
                     self._send_rows(y)
                 else:
                     nxt = self.c.sample(y).to(torch.int64).clone()
-                    if self.r.world > 1:
-                        if s < n_steps - 1:
-                            self._isend(nxt, 0, self.r.back_group)
+                    if two_way:
+                        self._isend(nxt, 0, self.r.back_group)
                     else:
                         tokens[m] = nxt
             if len(self._pending) > 4 * M:
                 self._pending[0][0].wait()
                 self._pending.pop(0)
+        if self.r.is_head and two_way and n_steps > 0:
+            for m in range(M):
+                recv_tokens(m)
         self.flush()
         return tokens

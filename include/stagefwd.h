@@ -44,8 +44,16 @@ enum {
 int sfc_abi_version(void);
 /* Message of the last failing call on this thread ("" if none). */
 const char *sfc_last_error(void);
-/* Read and clear the device-side error word of the current device (0 = none). */
+/* Read and clear the device-side error word of the current device (0 = none; 1 = a bounded
+ * device wait ran out; 2 = a kernel rejected an argument, e.g. a token id past the vocabulary). */
 int sfc_device_error(unsigned *code);
+/* Failure-detection self-test: one thread runs the bounded mbarrier wait that every streaming
+ * kernel uses, with `spin_limit` polls, on a barrier that completes (complete != 0) or that
+ * nothing ever arrives on (complete == 0).  A wait that runs out gives up, records code 1 in the
+ * device error word (read and cleared by sfc_device_error) and the kernel returns; the context
+ * stays usable.  Synchronises `stream`.  No counterpart in the reference, whose failure detection
+ * is host-side (connect timeouts and retries, crates/llama-stage-backend/src/lib.rs:2417-2538). */
+int sfc_selftest_bounded_wait(unsigned spin_limit, int complete, void *stream);
 /* Number of compute-kernel launches this library has issued in this process (stream launches
  * and launches recorded into CUDA graphs; replays of a graph are not counted).  Load-time
  * kernels (weight repacking, synthetic weight generation) are not counted. */
@@ -105,8 +113,10 @@ int sfc_sample_temperature(const float *scores_dev, int64_t n, int64_t vocab, fl
  * so a cudaMalloc inside the library would fail or fragment it).  No counterpart in the reference.  It allocates nothing: its per-CTA partials live
  * in a fixed 64 KiB array inside the library (enough for GPUs with up to 512 SMs; larger needs
  * return SFC_E_NOMEM).  The first call on each device looks up that array's device address, so
- * make it before any stream capture.  All calls share the array: calls whose kernels overlap on
- * the GPU (e.g. on two streams at once) race; nothing in it needs to start at zero. */
+ * make it before any stream capture; the address is kept for the life of the process, so a
+ * caller that resets a device (cudaDeviceReset) must not call this entry point on it afterwards.
+ * All calls share the array: calls whose kernels overlap on the GPU (e.g. on two streams at once)
+ * race; nothing in it needs to start at zero. */
 int sfc_logits_argmax_noalloc(int ggml_type, const void *w_dev, int64_t vocab, int64_t dim, const float *h_dev,
                               int64_t n_tok, float cap, float *all_scores_dev, int64_t *argmax_dev,
                               float *score_dev, void *stream);

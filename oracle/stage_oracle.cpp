@@ -325,10 +325,110 @@ int or_dequantize_rows(int type, const uint8_t *raw, int64_t n_rows, int64_t in_
   return 0;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Eight tokens side by side: lane t is token t's running sum, so each lane sees exactly the
+// operations (and roundings) of dot_row for its token; no lane ever mixes with another.
+typedef float v8f __attribute__((vector_size(32)));
+
+// A row's terms in dot_row order.  Q4_K: per (block, 64-element group j, l) the pair
+// (a1, a2) = (d1*q_lo - m1, d2*q_hi - m2) applied as sum += a1*x[j+l] + a2*x[j+32+l]
+// (quants.rs:1878-1904).  Q6_K: per (block, half, l) the four products sf*q applied as
+// sum += ((w1*x1 + w2*x2) + w3*x3) + w4*x4 (quants.rs:2640-2688).  Others: w[i], sum += w*x.
+void row_terms(int type, const uint8_t *row, int64_t in_dim, float *w) {
+  const int64_t nb = in_dim / QK_K;
+  if (type == OR_TYPE_Q4_K) {
+    for (int64_t bi = 0; bi < nb; ++bi) {
+      const uint8_t *b = row + bi * BLOCK_Q4_K;
+      const float d = h2f(b), dmin = h2f(b + 2);
+      const uint8_t *scales = b + 4, *qs = b + 16;
+      float *o = w + bi * QK_K;
+      for (int j = 0, is = 0; j < QK_K; j += 64, is += 2) {
+        uint8_t sc, m;
+        get_scale_min_k4(is, scales, &sc, &m);
+        const float d1 = d * float(sc), m1 = dmin * float(m);
+        get_scale_min_k4(is + 1, scales, &sc, &m);
+        const float d2 = d * float(sc), m2 = dmin * float(m);
+        for (int l = 0; l < 32; ++l) {
+          const uint8_t q = qs[j / 2 + l];
+          o[j + l] = d1 * float(q & 0x0F) - m1;
+          o[j + 32 + l] = d2 * float(q >> 4) - m2;
+        }
+      }
+    }
+  } else if (type == OR_TYPE_Q6_K) {
+    for (int64_t bi = 0; bi < nb; ++bi) {
+      const uint8_t *b = row + bi * BLOCK_Q6_K;
+      const uint8_t *ql = b, *qh = b + 128;
+      const int8_t *sc = (const int8_t *)(b + 192);
+      const float d = h2f(b + 208);
+      float *o = w + bi * QK_K;
+      for (int half = 0; half < 2; ++half) {
+        float sf[8];
+        for (int k = 0; k < 8; ++k) sf[k] = d * float(sc[half * 8 + k]);
+        for (int l = 0; l < 32; ++l) {
+          const int s = l / 16;
+          for (int g = 0; g < 4; ++g) o[half * 128 + g * 32 + l] = sf[s + 2 * g] * float(q6_val(ql, qh, half, l, g));
+        }
+      }
+    }
+  } else {
+    or_dequantize_rows(type, row, 1, in_dim, w);
+  }
+}
+
+__attribute__((target_clones("avx2", "default")))
+void dot_terms8(int type, const float *w, int64_t in_dim, const v8f *X, v8f &out) {
+  v8f sum = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (type == OR_TYPE_Q4_K) {
+    for (int64_t base = 0; base < in_dim; base += 64)
+      for (int l = 0; l < 32; ++l) sum = sum + (w[base + l] * X[base + l] + w[base + 32 + l] * X[base + 32 + l]);
+  } else if (type == OR_TYPE_Q6_K) {
+    for (int64_t base = 0; base < in_dim; base += 128)
+      for (int l = 0; l < 32; ++l)
+        sum = sum + (((w[base + l] * X[base + l] + w[base + 32 + l] * X[base + 32 + l]) +
+                      w[base + 64 + l] * X[base + 64 + l]) +
+                     w[base + 96 + l] * X[base + 96 + l]);
+  } else {
+    for (int64_t i = 0; i < in_dim; ++i) sum = sum + w[i] * X[i];
+  }
+  out = sum;
+}
+
+}  // namespace
+
+extern "C" {
+
 int or_matmul(int type, const uint8_t *raw, int64_t out_dim, int64_t in_dim, const float *x,
               int64_t n_tok, float *y, int threads) {
   int64_t rb = or_bytes_per_row(type, in_dim);
   if (rb == 0 || out_dim < 0 || n_tok < 0) return -1;
+  if (n_tok >= 2 && type != OR_TYPE_Q5_K) {
+    // Several tokens: a row's terms are formed once and applied to 8 tokens per pass, with each
+    // token's sum in the exact order of dot_row (bit-identical to the one-token loop below).
+    const int64_t ng = (n_tok + 7) / 8;
+    std::vector<v8f> xt(size_t(ng * in_dim));
+    for (int64_t g = 0; g < ng; ++g)
+      for (int64_t k = 0; k < in_dim; ++k) {
+        v8f v = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int t = 0; t < 8 && g * 8 + t < n_tok; ++t) v[t] = x[(g * 8 + t) * in_dim + k];
+        xt[size_t(g * in_dim + k)] = v;
+      }
+    parallel_rows(out_dim, threads, [&](int64_t lo, int64_t hi) {
+      std::vector<float> w(static_cast<size_t>(in_dim));
+      for (int64_t r = lo; r < hi; ++r) {
+        row_terms(type, raw + r * rb, in_dim, w.data());
+        for (int64_t g = 0; g < ng; ++g) {
+          v8f s;
+          dot_terms8(type, w.data(), in_dim, xt.data() + g * in_dim, s);
+          for (int t = 0; t < 8 && g * 8 + t < n_tok; ++t) y[(g * 8 + t) * out_dim + r] = s[t];
+        }
+      }
+    });
+    return 0;
+  }
   parallel_rows(out_dim, threads, [&](int64_t lo, int64_t hi) {
     for (int64_t r = lo; r < hi; ++r)
       for (int64_t t = 0; t < n_tok; ++t) y[t * out_dim + r] = dot_row(type, raw + r * rb, in_dim, x + t * in_dim);
@@ -454,6 +554,28 @@ void or_gqa_attention_rows(const float *q, const float *const *krows, const floa
   gqa_attention_impl(
       q, [&](int64_t t) { return krows[t]; }, [&](int64_t t) { return vrows[t]; }, n_pos, limit, window, n_heads,
       n_kv, head_dim, out);
+}
+
+void or_gqa_attention_rows_batch(const float *q, const float *const *krows, const float *const *vrows, int64_t n_pos,
+                                 const int64_t *limits, int64_t n_tok, int64_t window, int n_heads, int n_kv,
+                                 int head_dim, float *out, int threads) {
+  const int64_t w = int64_t(n_heads) * head_dim;
+  auto one = [&](int64_t lo, int64_t hi) {
+    for (int64_t t = lo; t < hi; ++t)
+      or_gqa_attention_rows(q + t * w, krows, vrows, n_pos, limits[t], window, n_heads, n_kv, head_dim, out + t * w);
+  };
+  if (threads <= 1 || n_tok < 2) {
+    one(0, n_tok);
+    return;
+  }
+  // tokens with more visible keys cost more: interleave them over the threads
+  const int64_t nt = std::min<int64_t>(threads, n_tok);
+  std::vector<std::thread> pool;
+  for (int64_t k = 0; k < nt; ++k)
+    pool.emplace_back([=, &one] {
+      for (int64_t t = k; t < n_tok; t += nt) one(t, t + 1);
+    });
+  for (auto &th : pool) th.join();
 }
 
 int or_logits_top_k(int type, const uint8_t *raw, int64_t vocab, int64_t hidden, const float *h, int k,

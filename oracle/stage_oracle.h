@@ -67,6 +67,11 @@ void or_gqa_attention(const float *q, const float *kc, const float *vc, int64_t 
 // Same, with the cached rows as one pointer per position (read in place).
 void or_gqa_attention_rows(const float *q, const float *const *krows, const float *const *vrows, int64_t n_pos,
                            int64_t limit, int64_t window, int n_heads, int n_kv, int head_dim, float *out);
+// n_tok queries [n_tok][n_heads*head_dim] over the same cached rows, query t seeing limits[t]
+// positions (each query's arithmetic is or_gqa_attention_rows'; queries run on `threads`).
+void or_gqa_attention_rows_batch(const float *q, const float *const *krows, const float *const *vrows, int64_t n_pos,
+                                 const int64_t *limits, int64_t n_tok, int64_t window, int n_heads, int n_kv,
+                                 int head_dim, float *out, int threads);
 
 /* real_math.rs:2119-2488 (matmul_raw_top_k). logits over rows [0, vocab), softcap if cap>0,
  * argmax with ties to the lowest index, top-k descending (k may be 0).

@@ -65,6 +65,7 @@ class _Lib:
         L.or_rope_apply.argtypes = [P, I, I, P, I64, ctypes.c_uint32, F, I, I]
         L.or_gqa_attention.argtypes = [P, P, P, I64, I64, I64, I, I, I, P]
         L.or_gqa_attention_rows.argtypes = [P, P, P, I64, I64, I64, I, I, I, P]
+        L.or_gqa_attention_rows_batch.argtypes = [P, P, P, I64, P, I64, I64, I, I, I, P, I]
         L.or_logits_top_k.argtypes = [I, P, I64, I64, P, I, F, P, P, P, P, P, I]
         L.or_mix64.argtypes = [U64, U64]
         L.or_mix64.restype = U64
@@ -165,6 +166,19 @@ def gqa_attention_rows(q: np.ndarray, krows: list, vrows: list, n_heads: int, n_
     kp, vp = _row_pointers(krows), _row_pointers(vrows)
     out = np.empty(n_heads * head_dim, np.float32)
     lib().or_gqa_attention_rows(_p(q), _p(kp), _p(vp), len(krows), limit, window, n_heads, n_kv, head_dim, _p(out))
+    return out
+
+
+def gqa_attention_rows_batch(qs: np.ndarray, krows: list, vrows: list, n_heads: int, n_kv: int, head_dim: int,
+                             limits, window: int = 0) -> np.ndarray:
+    """gqa_attention_rows for every query row of qs [T][n_heads*head_dim], query t seeing
+    limits[t] cached positions (threads over queries; each query's arithmetic is unchanged)."""
+    qs = np.ascontiguousarray(qs, np.float32)
+    lim = np.ascontiguousarray(limits, np.int64)
+    kp, vp = _row_pointers(krows), _row_pointers(vrows)
+    out = np.empty((qs.shape[0], n_heads * head_dim), np.float32)
+    lib().or_gqa_attention_rows_batch(_p(qs), _p(kp), _p(vp), len(krows), _p(lim), qs.shape[0], window, n_heads,
+                                      n_kv, head_dim, _p(out), _threads())
     return out
 
 
@@ -493,11 +507,12 @@ class OracleStage:
             kc, vc = kv.setdefault(i, ([], []))
         else:  # shared KV: the source layer's cache, already holding these positions (:1561-1640)
             kc, vc = kv[src]
-        att = np.empty((T, nh * hd), np.float32)
+        qs = np.empty((T, nh * hd), np.float32)
         for t in range(T):
             q = q_all[t]
             if self.rope_freqs is not None:
                 q = rope(q, nh, hd, self.rope_freqs, pos0 + t, theta, rot, prop)
+            qs[t] = q
             if src is None:
                 k = k_all[t]
                 if self.rope_freqs is not None:
@@ -507,7 +522,8 @@ class OracleStage:
                     k, v = fp16_round(k), fp16_round(v)
                 kc.append(k)
                 vc.append(v)
-            att[t] = gqa_attention_rows(q, kc, vc, nh, nkv, hd, limit=pos0 + t + 1, window=win)
+        # token t sees positions [0, pos0 + t] (its own k/v were appended above)
+        att = gqa_attention_rows_batch(qs, kc, vc, nh, nkv, hd, pos0 + 1 + np.arange(T), window=win)
         o = self._mm(f"{p}.attn_output.weight", att)
         o = rms_norm(o, self._f32(self.t[f"{p}.post_attention_norm.weight"]))
         states = o + states
@@ -580,6 +596,27 @@ class OracleStage:
             if self._attention_config(i)[3] is None:
                 kv[i] = ([r for r in rng.standard_normal((n_pos, width), np.float32)],
                          [r for r in rng.standard_normal((n_pos, width), np.float32)])
+        self.sessions[req] = {"seq_len": n_pos, "kv": kv}
+
+    def fill_session_like_device(self, req: str, n_pos: int, seed: int, kv_f32: bool):
+        """The cache that sfc_session_fill_synthetic writes on the device, restated: for the
+        stage's i-th layer (stage order) that has its own cache, part p (0 = K, 1 = V) of kv head h
+        holds synth_tensor(F32 if kv_f32 else F16, tensor_key(seed, f"kv.{i}.{p}.{h}"), n_pos,
+        head_dim, sigma 1) as [position][head_dim]; a cached row is the heads side by side."""
+        kv = {}
+        t = F32 if kv_f32 else F16
+        dt = np.float32 if kv_f32 else np.float16
+        for li, i in enumerate(self.layers):
+            if self._attention_config(i)[3] is not None:
+                continue
+            parts = []
+            for part in range(2):
+                heads = [np.frombuffer(synth_tensor(t, tensor_key(seed, f"kv.{li}.{part}.{kh}"), n_pos, self.head_dim,
+                                                    1.0).tobytes(), dt).astype(np.float32).reshape(n_pos, self.head_dim)
+                         for kh in range(self.n_kv)]
+                rows = np.ascontiguousarray(np.concatenate(heads, axis=1))
+                parts.append([np.ascontiguousarray(r) for r in rows])
+            kv[i] = (parts[0], parts[1])
         self.sessions[req] = {"seq_len": n_pos, "kv": kv}
 
     def rollback(self, req: str, keep: int):

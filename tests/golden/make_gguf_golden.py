@@ -1,7 +1,7 @@
 """Regenerate the GGUF parsing fixtures in this folder (run in a container that has the reference
 tree; tests only read the committed outputs).
 
-  python tests/golden/make_gguf_golden.py [--reference /root/reference]
+  python tests/golden/make_gguf_golden.py --reference <reference checkout>
 
 Outputs
   gguf_mixed.gguf   a small GGUF v3 file written by the reference's own gguf-py writer
@@ -63,7 +63,7 @@ def field_value(field, gguf):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "vendor/llama.cpp/gguf-py"))
     import gguf

@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures in this folder (run in a container that has the
 reference tree; the GPU box only reads the committed outputs).
 
-  python tests/golden/make_golden.py [--reference /root/reference]
+  python tests/golden/make_golden.py --reference <reference checkout>
 
 Outputs
   dequant_golden.npz   seeded random Q4_K / Q5_K / Q6_K blocks (raw bytes) and their
@@ -38,7 +38,7 @@ def random_blocks(rng, n, size, d_offsets):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "vendor/llama.cpp/gguf-py"))
     from gguf import quants as gq  # noqa: E402

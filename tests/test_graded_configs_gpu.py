@@ -1,0 +1,268 @@
+"""GPU parity at the sizes of the graded workloads, against the oracle and against the backend's
+own other code paths:
+
+* one full-width decoder layer (d_model 2560, 8q/4kv x 256, ffn 10240, Q4_K_M) decoding after
+  2048 cached positions;
+* the 42-layer model, vocab 262144, as head (layers 0-20) and tail (21-41) stages handing off
+  through continue_forward: a 512-token prompt, then 64 greedy tokens;
+* a 16-node draft tree (branching 2-2-2-2, BFS, truncated) at 1024 cached positions with vocab
+  262144: tree rows against their chains, the greedy acceptance walk and its bonus token;
+* one decode step of 64 sequences at contexts drawn from 512..3584 (head_dim 256): the batched
+  step against per-sequence steps and against the oracle.
+
+The cached keys and values of the long contexts are the seeded synthetic cache that
+sfc_session_fill_synthetic writes; the oracle restates it (OracleStage.fill_session_like_device),
+so both sides attend over identical caches.  Bars: f32 cache 1e-3 relative (normwise and
+max/max); fp16 cache identical tokens plus 1e-2 normwise (stage_close in test_stage_gpu.py:
+rounding-boundary flips of newly cached elements in the unscaled, sharply peaked attention).
+Hidden states of deep stacks are compared by tokens only (last-bit differences amplify
+chaotically through 21+ random layers)."""
+import numpy as np
+import pytest
+
+import stage_oracle as so
+from gpu_util import assert_close, rel_errors
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+FULL = dict(hidden=2560, n_heads=8, n_kv=4, head_dim=256, ffn=10240, vocab=262144, seed=0x5EED)
+_TENSORS: dict = {}
+
+
+@pytest.fixture(scope="module")
+def sf():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import stagefwd
+    return stagefwd
+
+
+def specs(n_layers, **kw):
+    import stagefwd
+    base = dict(FULL, n_layers=n_layers)
+    base.update(kw)
+    return so.ModelSpec(**base), stagefwd.ModelShape(**base)
+
+
+def oracle_stage(spec, start, end, head, tail, kv_f32):
+    """Oracle stage; tensors depend only on (seed, name), so they are generated once per module."""
+    tensors = {}
+    for n, t, d in spec.stage_tensor_shapes(start, end, head, tail):
+        key = (spec.seed, n, t, tuple(d))
+        if key not in _TENSORS:
+            _TENSORS[key] = (t, d, spec.synth(n, t, d))
+        tensors[n] = _TENSORS[key]
+    return so.OracleStage(tensors, so.Layout("m", f"s{start}", start, end, head, tail), rope_theta=10000.0,
+                          kv_fp16=not kv_f32)
+
+
+def gpu_stage(sf, shape, start, end, head, tail, kv_f32, max_ctx, max_sessions, max_batch_tokens=512):
+    return sf.CudaStageBackend(synthetic=shape, rope_theta=10000.0, kv_f32=kv_f32, max_ctx=max_ctx,
+                               max_sessions=max_sessions, max_batch_tokens=max_batch_tokens).load_layout(
+        "m", f"s{start}", start, end, head, tail)
+
+
+def stage_close(got, ref, kv_f32, what):
+    norm, mx = rel_errors(got, ref)
+    if kv_f32:
+        assert norm <= 1e-3 and mx <= 1e-3, f"{what}: normwise {norm:.3e}, max/max {mx:.3e}"
+    else:
+        assert norm <= 1e-2, f"{what}: normwise {norm:.3e} (fp16 KV)"
+
+
+# ---------------------------------------------------------------- one layer after 2048 positions
+@pytest.mark.parametrize("kv_f32", [True, False])
+def test_layer_decode_after_2048_cached_positions(sf, kv_f32):
+    spec, shape = specs(1)
+    g = gpu_stage(sf, shape, 0, 0, True, True, kv_f32, max_ctx=2048 + 16, max_sessions=2)
+    o = oracle_stage(spec, 0, 0, True, True, kv_f32)
+    g.fill_session_synthetic("r", 2048, seed=11)
+    o.fill_session_like_device("r", 2048, seed=11, kv_f32=kv_f32)
+    tok_g = tok_o = int(so.synth_tokens(3, "cfg2.first", 1, spec.vocab)[0])
+    for step in range(4):
+        h_g = g.begin_token_ids("r", [tok_g])
+        h_o = o.begin_token_ids("r", [tok_o], append=True)
+        stage_close(h_g, h_o, kv_f32, f"layer after {2048 + step} cached positions")
+        tok_g, tok_o = g.sample_tail(h_g)[0], o.sample_tail(h_o[-1])[0]
+        assert tok_g == tok_o, f"step {step}"
+    assert g.session_len("r") == 2048 + 4
+    g.close()
+
+
+# ---------------------------------------------------------------- head/tail split, 512-token prompt
+def test_head_tail_512_prompt_64_greedy_tokens(sf):
+    """42 layers as head 0-20 and tail 21-41 (fp16 cache, the workload's own), hidden rows handed
+    off through continue_forward; the greedy stream equals the oracle's for 64 steps."""
+    spec, shape = specs(42)
+    n_steps, prompt = 64, so.synth_tokens(29, "cfg3.prompt", 512, spec.vocab)
+    gh = gpu_stage(sf, shape, 0, 20, True, False, False, max_ctx=512 + n_steps + 8, max_sessions=2)
+    gt = gpu_stage(sf, shape, 21, 41, False, True, False, max_ctx=512 + n_steps + 8, max_sessions=2)
+    h = gh.begin_token_ids("r", prompt)
+    handoff_g = h
+    t = gt.continue_forward("r", h)
+    toks_g = [gt.sample_tail(t)[0]]
+    for _ in range(n_steps - 1):
+        toks_g.append(gt.sample_tail(gt.continue_forward("r", gh.begin_token_ids("r", [toks_g[-1]])))[0])
+    assert gh.session_len("r") == gt.session_len("r") == 512 + n_steps - 1
+    gh.close()
+    gt.close()
+
+    oh, ot = oracle_stage(spec, 0, 20, True, False, False), oracle_stage(spec, 21, 41, False, True, False)
+    h = oh.begin_token_ids("r", prompt)
+    handoff_norm, _ = rel_errors(handoff_g, h)
+    toks_o = [ot.sample_tail(ot.continue_forward("r", h)[-1])[0]]
+    for _ in range(n_steps - 1):
+        toks_o.append(ot.sample_tail(ot.continue_forward("r", oh.begin_token_ids("r", [toks_o[-1]]))[-1])[0])
+    print(f"head->tail hand-off of the prompt (512 x 2560 after 21 layers): normwise {handoff_norm:.2e}")
+    assert toks_g == toks_o
+    assert handoff_norm <= 1e-2
+
+
+# ---------------------------------------------------------------- draft tree at 1024 positions
+PARENT = np.array(so.bfs_tree([2, 2, 2, 2], 16), np.int32)
+
+
+def depths(parent):
+    d = [0] * len(parent)
+    for i in range(1, len(parent)):
+        d[i] = d[parent[i]] + 1
+    return d
+
+
+def chain(parent, n):
+    out = [n]
+    while parent[out[-1]] >= 0:
+        out.append(int(parent[out[-1]]))
+    return out[::-1]
+
+
+def oracle_node_rows(o, req, parent, nodes, n_cached):
+    """Each node's row as the last row of its root..node chain after the cached prefix.  Nodes
+    are visited depth first (pre-order): when a node is reached the cache holds the chain of the
+    node visited before it, whose first depth(node) positions are exactly the node's ancestors,
+    so one rollback and one single-token step give the node's row."""
+    dep = depths(parent)
+    kids = {i: [c for c in range(1, len(parent)) if parent[c] == i] for i in range(len(parent))}
+    order, stack = [], [0]
+    while stack:
+        n = stack.pop()
+        order.append(n)
+        stack.extend(reversed(kids[n]))
+    rows = [None] * len(parent)
+    for n in order:
+        o.rollback(req, n_cached + dep[n])
+        rows[n] = o.begin_token_ids(req, [int(nodes[n])], append=True)[-1]
+    return np.stack(rows)
+
+
+def build_greedy_tree(g, req, parent, first, vocab, rng):
+    """Node tokens level by level: a node's first child carries the token drawn at that node, so
+    the greedy walk can accept the whole depth; other children are random."""
+    nodes = np.zeros(len(parent), np.uint32)
+    nodes[0] = first
+    dep = depths(parent)
+    for level in range(max(dep)):
+        for i in range(1, len(parent)):
+            if dep[i] == level + 1:
+                nodes[i] = rng.integers(0, vocab)
+        rows = g.forward_tree(req, parent, ids=nodes)
+        for p in range(len(parent)):
+            if dep[p] == level:
+                kids = [c for c in range(1, len(parent)) if parent[c] == p]
+                if kids:
+                    nodes[kids[0]] = g.sample_tail(rows[p:p + 1])[0]
+    return nodes
+
+
+@pytest.mark.parametrize("n_layers,kv_f32", [(4, True), (42, False)])
+def test_tree_16_nodes_at_1024_cached_positions(sf, n_layers, kv_f32):
+    spec, shape = specs(n_layers)
+    n_cached = 1024
+    g = gpu_stage(sf, shape, 0, n_layers - 1, True, True, kv_f32, max_ctx=n_cached + 32, max_sessions=4)
+    g.fill_session_synthetic("v", n_cached, seed=7)
+    rng = np.random.default_rng(41)
+    nodes = build_greedy_tree(g, "v", PARENT, int(rng.integers(0, spec.vocab)), spec.vocab, rng)
+    rows = g.forward_tree("v", PARENT, ids=nodes)
+    path, nxt = g.sample_tree(rows, PARENT, nodes, temperature=0.0)
+    drawn_g = [g.sample_tail(rows[i:i + 1])[0] for i in range(len(PARENT))]
+
+    # the same rows as chains on the GPU (single-token appends after the cached prefix)
+    g.fill_session_synthetic("c", n_cached, seed=7)
+    chain_rows = []
+    for n in range(len(PARENT)):
+        g.rollback_kv("c", n_cached)
+        h = None
+        for tok in (int(nodes[p]) for p in chain(PARENT, n)):
+            h = g.begin_token_ids("c", [tok])
+        chain_rows.append(h[-1])
+    chain_rows = np.stack(chain_rows)
+
+    o = oracle_stage(spec, 0, n_layers - 1, True, True, kv_f32)
+    o.fill_session_like_device("v", n_cached, seed=7, kv_f32=kv_f32)
+    rows_o = oracle_node_rows(o, "v", PARENT, nodes, n_cached)
+    drawn_o = [o.sample_tail(r)[0] for r in rows_o]
+    path_o, nxt_o = so.tree_walk(PARENT, nodes, drawn_o)
+
+    assert drawn_g == drawn_o
+    assert list(path) == list(path_o) and nxt == nxt_o
+    assert len(path) == 5  # the tree was built so that greedy acceptance reaches the deepest level
+    if n_layers <= 4:
+        for n in range(len(PARENT)):
+            assert_close(rows[n], chain_rows[n], what=f"tree row {n} vs its chain (GPU)")
+            assert_close(rows[n], rows_o[n], what=f"tree row {n} vs oracle chain")
+    else:
+        assert [g.sample_tail(r[None])[0] for r in chain_rows] == drawn_g
+
+    # committing the accepted path leaves the session as if the path had been decoded
+    g.commit_tree("v", path)
+    assert g.session_len("v") == n_cached + len(path)
+    with pytest.raises(sf.StageError, match="no draft tree pending"):
+        g.commit_tree("v", path)
+    after = g.begin_token_ids("v", [nxt])
+    o.rollback("v", n_cached)
+    for p in path:
+        o.begin_token_ids("v", [int(nodes[p])], append=True)
+    after_o = o.begin_token_ids("v", [nxt_o], append=True)
+    if n_layers <= 4:
+        assert_close(after, after_o, what="decode step after commit")
+    assert g.sample_tail(after)[0] == o.sample_tail(after_o[-1])[0]
+    g.close()
+
+
+# ---------------------------------------------------------------- 64 sequences, contexts 512..3584
+@pytest.mark.parametrize("kv_f32", [True, False])
+def test_batched_decode_64_sequences_head_dim_256(sf, kv_f32):
+    spec, shape = specs(2)
+    n_seq = 64
+    rng = np.random.default_rng(2024)
+    ctx = rng.integers(512, 3585, n_seq)
+    first = rng.integers(0, spec.vocab, n_seq)
+    g = gpu_stage(sf, shape, 0, 1, True, True, kv_f32, max_ctx=4096, max_sessions=2 * n_seq + 2,
+                  max_batch_tokens=n_seq)
+    for i in range(n_seq):
+        g.fill_session_synthetic(f"b{i}", int(ctx[i]), seed=100 + i)
+        g.fill_session_synthetic(f"s{i}", int(ctx[i]), seed=100 + i)
+    dev = torch.device("cuda")
+    ids = torch.tensor(first, dtype=torch.int32, device=dev)
+    out = torch.empty(n_seq, shape.hidden, device=dev)
+    tk = torch.empty(n_seq, dtype=torch.int64, device=dev)
+    sc = torch.empty(n_seq, dtype=torch.float32, device=dev)
+    g.forward_dev([f"b{i}" for i in range(n_seq)], [1] * n_seq, ids_dev=ids, out_dev=out, append=True)
+    g.sample_dev(out, tk, sc)
+    torch.cuda.synchronize()
+    batched, batched_tok = out.cpu().numpy(), tk.cpu().tolist()
+    single = np.stack([g.begin_token_ids(f"s{i}", [int(first[i])])[-1] for i in range(n_seq)])
+    single_tok = [g.sample_tail(single[i:i + 1])[0] for i in range(n_seq)]
+    for i in range(n_seq):
+        stage_close(batched[i], single[i], kv_f32, f"sequence {i} (ctx {ctx[i]}): batched vs alone")
+    assert batched_tok == single_tok
+    assert all(g.session_len(f"b{i}") == ctx[i] + 1 for i in range(n_seq))
+    g.close()
+
+    o = oracle_stage(spec, 0, 1, True, True, kv_f32)
+    for i in (int(np.argmin(ctx)), int(np.argmax(ctx)), 17):
+        o.fill_session_like_device(f"o{i}", int(ctx[i]), seed=100 + i, kv_f32=kv_f32)
+        h = o.begin_token_ids(f"o{i}", [int(first[i])], append=True)
+        stage_close(batched[i], h[-1], kv_f32, f"sequence {i} (ctx {ctx[i]}) vs oracle")
+        assert batched_tok[i] == o.sample_tail(h[-1])[0]

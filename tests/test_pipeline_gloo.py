@@ -12,7 +12,11 @@ import torch.multiprocessing as mp
 
 import stage_oracle as so
 
-SPEC = dict(hidden=256, n_heads=4, n_kv=2, head_dim=64, ffn=512, vocab=200, n_layers=5, seed=31)
+# seed 33: every sequence's greedy token changes from step to step, so a pipeline that returned
+# an earlier step's samples would be caught
+SPEC = dict(hidden=256, n_heads=4, n_kv=2, head_dim=64, ffn=512, vocab=200, n_layers=5, seed=33)
+# decode_microbatched calls of 1, 2 and 1 steps: the head's tokens are checked after each call
+CALL_STEPS = (1, 2, 1)
 
 
 class OracleCompute:
@@ -55,9 +59,12 @@ def run_pipeline(rank, world, port, q):
     for i, rid in enumerate(["a", "b", "c", "d"]):  # short prefills so every session has context
         pipe.step([rid], [3], torch.tensor([i + 1, i + 2, i + 3], dtype=torch.int64), append=False)
     toks = [torch.tensor([5, 6], dtype=torch.int64), torch.tensor([7, 8], dtype=torch.int64)]
-    out = pipe.decode_microbatched(mbs, toks, 3)
+    after = []
+    for n in CALL_STEPS:
+        toks = pipe.decode_microbatched(mbs, toks, n)
+        after.append([t.tolist() for t in toks] if rank == 0 else None)
     if rank == 0:
-        q.put((gen.tolist(), [t.tolist() for t in out]))
+        q.put((gen.tolist(), after))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -82,10 +89,13 @@ def single_process_reference():
     for i, rid in enumerate(["a", "b", "c", "d"]):
         st.begin_token_ids(rid, [i + 1, i + 2, i + 3])
     toks = {"a": 5, "b": 6, "c": 7, "d": 8}
-    for _ in range(3):
-        for rid in ["a", "b", "c", "d"]:
-            toks[rid] = st.sample_tail(st.begin_token_ids(rid, [toks[rid]])[-1])[0]
-    return gen, [[toks["a"], toks["b"]], [toks["c"], toks["d"]]]
+    after = []
+    for n in CALL_STEPS:
+        for _ in range(n):
+            for rid in ["a", "b", "c", "d"]:
+                toks[rid] = st.sample_tail(st.begin_token_ids(rid, [toks[rid]])[-1])[0]
+        after.append([[toks["a"], toks["b"]], [toks["c"], toks["d"]]])
+    return gen, after
 
 
 def test_even_stage_split_matches_reference_rule():
@@ -124,3 +134,5 @@ def test_pipeline_matches_single_process(world):
     ref = single_process_reference()
     assert got[0] == ref[0]
     assert got[1] == ref[1]
+    # the sampled tokens move from call to call (the check above would see a stale step)
+    assert ref[1][0] != ref[1][1] and ref[1][1] != ref[1][2]
