@@ -44,7 +44,7 @@ __device__ float g_gemv_part[GEMV_DEFAULT_SPLIT_CTAS * GEMV_SPLIT_SLOT];
 // Segments let one launch cover several matrices with the same K (q, k and v of a layer).
 // TYPE: the weight type of every segment (T_Q4_K / T_Q6_K), or 0 for a mix (checked per unit).
 template <int NMAT, int T, int TYPE, int CW>
-__global__ void __launch_bounds__((CW + 1) * 32, CW == GEMV_CW_HALF ? 2 : 1) qgemv_kernel(const QGemvArgs a) {
+__global__ void __launch_bounds__((CW + 1) * 32, 1) qgemv_kernel(const QGemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float pro_red[GEMV_MAX_T][16];
   __shared__ int s_tdone[2];                 // finished units of the shared tiles
@@ -246,16 +246,6 @@ unsigned *device_error_ptr() {
 
 constexpr int GEMV_STAGE_TARGET = 24 * 1024;
 constexpr int GEMV_SMEM_WIDE = 227 * 1024 - 1024;  // dynamic shared memory (static use is < 1 KB)
-constexpr int GEMV_SMEM_HALF = 112 * 1024 - 512;   // two CTAs per SM
-
-// Launch shape: SFC_GEMV_HALF=1 selects the two-CTAs-per-SM configuration.
-static bool gemv_half_ctas() {
-  static const int v = [] {
-    const char *e = getenv("SFC_GEMV_HALF");
-    return e && e[0] == '1' ? 1 : 0;
-  }();
-  return v != 0;
-}
 constexpr int GEMV_RED_TARGET = 32 * 1024;
 
 size_t gemv_split_bytes(int max_ctas) {
@@ -290,7 +280,7 @@ static GemvSplit default_split() {
 template <int NMAT, int T, int TYPE, int CW>
 static cudaError_t launch_qgemv_t(QGemvArgs a, const GemvSplit &sp, cudaStream_t st) {
   auto kern = qgemv_kernel<NMAT, T, TYPE, CW>;
-  const int budget = CW == GEMV_CW_HALF ? GEMV_SMEM_HALF : GEMV_SMEM_WIDE;
+  const int budget = GEMV_SMEM_WIDE;
   const int nb = a.nb;
   int64_t tiles = 0;
   int stage_bytes = 0, nbs_min = nb;
@@ -343,9 +333,6 @@ static cudaError_t launch_qgemv_t(QGemvArgs a, const GemvSplit &sp, cudaStream_t
 
 template <int NMAT, int T, int TYPE>
 static cudaError_t launch_qgemv_cw(const QGemvArgs &a, const GemvSplit &sp, cudaStream_t st) {
-  // the half-SM shape needs two ring slots beside the activations (not the case for 2 tokens at
-  // K = 10240): otherwise, and by default, one CTA per SM
-  if (gemv_half_ctas() && launch_qgemv_t<NMAT, T, TYPE, GEMV_CW_HALF>(a, sp, st) == cudaSuccess) return cudaSuccess;
   return launch_qgemv_t<NMAT, T, TYPE, GEMV_CW_WIDE>(a, sp, st);
 }
 

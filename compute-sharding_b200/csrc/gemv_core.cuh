@@ -11,10 +11,8 @@
 namespace sfc {
 
 constexpr int GEMV_TILE = 16;       // weight rows per MMA tile
-// Consumer warps per CTA (plus one producer warp): 15 (512 threads, one CTA per SM) or 7 (256
-// threads and at most half the shared memory, so the next launch's CTA fits beside this one and
-// streams its weights while this one computes).
-constexpr int GEMV_CW_WIDE = 15, GEMV_CW_HALF = 7;
+// Consumer warps per CTA (plus one producer warp): 15, 512 threads and one CTA per SM.
+constexpr int GEMV_CW_WIDE = 15;
 constexpr int GEMV_MAX_T = 2;
 constexpr int GEMV_MAX_STAGES = 12;
 constexpr int GEMV_MAX_SEG = 3;

@@ -188,29 +188,6 @@ cudaError_t decode_attention(const float *q, const float *k, const float *v, int
                              KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, int64_t sum_keys,
                              const AttnParams &p, void *scratch, size_t scratch_bytes, unsigned *counters,
                              cudaStream_t st);
-// One decoder layer of a one-token, one-sequence decode step as a single cooperative launch
-// (decode_layer.cu): q/k/v projections with the fused residual + RMSNorm prologue, attention,
-// o projection, gate/up + GeGLU, down.  bar: two words, zero before the first launch (each launch
-// leaves the arrival word zero); split: the GEMV boundary buffers (at least num_sms() CTAs).
-struct DecodeLayerIn {
-  const GemvSeg *qkv;  // q, k, v (K = hidden)
-  GemvSeg o, gate_up, down;
-  GemvPrologue pro_qkv, pro_o, pro_gu, pro_down;
-  int64_t hidden, q_dim, ffn, max_keys;
-  const float *q, *k, *v;
-  float *att;
-  KVLayer kv;
-  const SeqInfo *seqs;
-  AttnParams ap;
-  void *attn_scratch;
-  size_t attn_scratch_bytes;
-  unsigned *bar;
-  const GemvSplit *split;
-};
-bool decode_layer_supported(const AttnParams &ap);
-size_t decode_layer_scratch_bytes(const AttnParams &ap, int64_t max_keys);
-// cudaErrorNotSupported: shapes the layer kernel does not cover (use the per-op launches).
-cudaError_t decode_layer(const DecodeLayerIn &in, cudaStream_t st);
 // causal GQA attention over the cache (real_math.rs:2697-2744); tree masks via parent links.
 size_t attention_scratch_bytes(int64_t n_tok, const AttnParams &p, int64_t max_keys);
 // tok_limit (nullable): per-token number of visible cache positions (default pos+1);

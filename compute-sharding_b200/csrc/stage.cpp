@@ -136,9 +136,6 @@ struct sfc_stage {
   int64_t attn_sum_keys = 0;  // keys of the eager batch being run (0: graph capture, fixed splits)
   void *gemv_split_mem = nullptr;     // GEMV tile-boundary counters (kept zero) and partial sums
   GemvSplit gemv_split = {};
-  // one-token decode as one launch per layer (decode_layer.cu): grid-barrier words, kept valid
-  bool layer_kernel = false;
-  unsigned *layer_bar = nullptr;
   // tensor-core GEMM path for 8+ rows (K-quant stages): operand-B staging and the up-projection
   bool gemm_ok = false;
   void *gemm_scratch = nullptr;
@@ -554,7 +551,6 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   for (int64_t t = 1; t <= T; ++t) {
     amax = std::max(amax, attention_scratch_bytes(t, ap, h->max_ctx));
     amax = std::max(amax, decode_attention_scratch_bytes(t, ap, h->max_ctx));
-    if (t == 1 && decode_layer_supported(ap)) amax = std::max(amax, decode_layer_scratch_bytes(ap, h->max_ctx));
   }
   h->attn_scratch = amax;
   h->logit_scratch = logits_scratch_bytes(T);
@@ -564,19 +560,6 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   if ((rc = alloc(&h->gemv_split_mem, int64_t(gemv_split_bytes(kGemvSplitCtas))))) return rc;
   h->gemv_split = gemv_split_view(h->gemv_split_mem, kGemvSplitCtas);
   SFC_CUDA(cudaMemset(h->gemv_split_mem, 0, gemv_split_bytes(kGemvSplitCtas)));
-  if ((rc = alloc((void **)&h->layer_bar, 256))) return rc;
-  SFC_CUDA(cudaMemset(h->layer_bar, 0, 256));
-  {
-    // one-token decode through the layer kernel: K-quant projections, supported attention shape
-    const char *env = getenv("SFC_DECODE_LAYER");
-    bool ok = h->fused && decode_layer_supported(ap) && env && env[0] == '1';
-    for (const Layer &L : h->layers) {
-      ok = ok && L.own_kv();  // the layer kernel appends every layer's own k/v
-      for (const DevTensor *w : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
-        ok = ok && w && (w->type == T_Q4_K || w->type == T_Q6_K);
-    }
-    h->layer_kernel = ok;
-  }
   if (h->fused && T >= QGEMM_MIN_TOKENS) {
     bool ok = true;
     for (const Layer &L : h->layers)
@@ -623,7 +606,7 @@ void destroy_stage(sfc_stage *h) {
   for (void *p : {(void *)h->resid, (void *)h->resid2, (void *)h->xn, (void *)h->proj, (void *)h->q, (void *)h->k, (void *)h->v,
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
-                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemv_split_mem, (void *)h->layer_bar, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
+                  (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemv_split_mem, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
                   (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores, (void *)h->logit_scores,
                   h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
@@ -822,48 +805,6 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
     const int nqkv = L.own_kv() ? 3 : 1;
     const AttnParams ap = attn_params(h, L);
     const KVLayer kv = kv_layer(h, li);
-    if (T == 1 && decode && h->layer_kernel && !h->tree_active && L.own_kv()) {
-      DecodeLayerIn in = {};
-      in.qkv = qkv;
-      in.o = seg_of(L.o, nullptr, h->proj, H);
-      in.gate_up = seg_of(L.gate, L.up, h->act, h->ffn);
-      in.down = seg_of(L.down, nullptr, h->proj, H);
-      in.pro_qkv = pro;
-      in.pro_o.mode = 0;
-      in.pro_o.x = h->att;
-      in.pro_gu.mode = 2;
-      in.pro_gu.eps = h->eps;
-      in.pro_gu.a = h->proj;
-      in.pro_gu.resid_in = cur;
-      in.pro_gu.resid_out = other;
-      in.pro_gu.w_post = F32P(L.post_attn);
-      in.pro_gu.w_next = F32P(L.ffn_norm);
-      in.pro_down.mode = 0;
-      in.pro_down.x = h->act;
-      in.hidden = H;
-      in.q_dim = h->q_dim;
-      in.ffn = h->ffn;
-      in.max_keys = h->max_ctx;  // the split count is fixed per stage (the decode graph is captured once)
-      in.q = h->q;
-      in.k = h->k;
-      in.v = h->v;
-      in.att = h->att;
-      in.kv = kv;
-      in.seqs = h->seq_dev;
-      in.ap = ap;
-      in.attn_scratch = h->scratch;
-      in.attn_scratch_bytes = std::max(h->attn_scratch, h->logit_scratch);
-      in.bar = h->layer_bar;
-      in.split = &h->gemv_split;
-      e = decode_layer(in, st);
-      if (e == cudaSuccess) {
-        std::swap(cur, other);
-        continue;
-      }
-      if (e != cudaErrorNotSupported) return e;
-      (void)cudaGetLastError();
-      h->layer_kernel = false;  // the model's shapes: per-op launches from here on
-    }
     if ((e = gemv_fused(qkv, nqkv, 1, H, pro, T, st, &h->gemv_split))) return e;
     if ((e = layer_attention(h, ap, kv, T, max_keys, decode, st))) return e;
     const GemvSeg o = seg_of(L.o, nullptr, h->proj, H);

@@ -91,13 +91,23 @@ def test_layer_decode_after_2048_cached_positions(sf, kv_f32):
 
 
 # ---------------------------------------------------------------- head/tail split, 512-token prompt
-def test_head_tail_512_prompt_64_greedy_tokens(sf):
-    """42 layers as head 0-20 and tail 21-41 (fp16 cache, the workload's own), hidden rows handed
-    off through continue_forward; the greedy stream equals the oracle's for 64 steps."""
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_head_tail_512_prompt_64_greedy_tokens(sf, kv_f32):
+    """42 layers as head 0-20 and tail 21-41, hidden rows handed off through continue_forward; the
+    greedy stream equals the oracle's for 64 steps, with the fp16 cache (the workload's own) and
+    with the f32 cache.
+
+    The prompt rows handed off after 21 layers are compared too, against the oracle's own
+    sensitivity: this random model's prefill is chaotic (unscaled attention over many keys), so the
+    oracle run again on the embedding perturbed by 1e-7 relative moves half of its rows past 1e-3
+    (median ~8e-4, 90th percentile ~0.3 after 21 layers).  With the f32 cache the GPU rows must sit
+    no further from the oracle than that perturbed run does (quantiles within 3x, or the 1e-3
+    bar); with the fp16 cache a newly cached element on the other side of an fp16 rounding boundary
+    (one fp16 ulp, 2^-11) is a far larger seed, so only the tokens are held to the bar there."""
     spec, shape = specs(42)
     n_steps, prompt = 64, so.synth_tokens(29, "cfg3.prompt", 512, spec.vocab)
-    gh = gpu_stage(sf, shape, 0, 20, True, False, False, max_ctx=512 + n_steps + 8, max_sessions=2)
-    gt = gpu_stage(sf, shape, 21, 41, False, True, False, max_ctx=512 + n_steps + 8, max_sessions=2)
+    gh = gpu_stage(sf, shape, 0, 20, True, False, kv_f32, max_ctx=512 + n_steps + 8, max_sessions=2)
+    gt = gpu_stage(sf, shape, 21, 41, False, True, kv_f32, max_ctx=512 + n_steps + 8, max_sessions=2)
     h = gh.begin_token_ids("r", prompt)
     handoff_g = h
     t = gt.continue_forward("r", h)
@@ -108,15 +118,27 @@ def test_head_tail_512_prompt_64_greedy_tokens(sf):
     gh.close()
     gt.close()
 
-    oh, ot = oracle_stage(spec, 0, 20, True, False, False), oracle_stage(spec, 21, 41, False, True, False)
+    oh, ot = oracle_stage(spec, 0, 20, True, False, kv_f32), oracle_stage(spec, 21, 41, False, True, kv_f32)
     h = oh.begin_token_ids("r", prompt)
-    handoff_norm, _ = rel_errors(handoff_g, h)
+    row_err = np.linalg.norm(handoff_g - h, axis=1) / np.linalg.norm(h, axis=1)
     toks_o = [ot.sample_tail(ot.continue_forward("r", h)[-1])[0]]
     for _ in range(n_steps - 1):
         toks_o.append(ot.sample_tail(ot.continue_forward("r", oh.begin_token_ids("r", [toks_o[-1]]))[-1])[0])
-    print(f"head->tail hand-off of the prompt (512 x 2560 after 21 layers): normwise {handoff_norm:.2e}")
+    above = row_err > 1e-3
+    print(f"\n[{'f32' if kv_f32 else 'fp16'} cache] hand-off of the prompt (512 x 2560 after 21 layers): row "
+          f"errors median {np.median(row_err):.2e}, 90th pct {np.percentile(row_err, 90):.2e}, max "
+          f"{row_err.max():.2e}; rows above 1e-3: {int(above.sum())}, the first {np.flatnonzero(above)[:8].tolist()}")
     assert toks_g == toks_o
-    assert handoff_norm <= 1e-2
+    if kv_f32:
+        emb = oh.embed(prompt)
+        pert = (emb * (1 + 1e-7 * np.random.default_rng(0).standard_normal(emb.shape))).astype(np.float32)
+        ref = oracle_stage(spec, 0, 20, True, False, kv_f32)
+        pert_err = np.linalg.norm(ref.run_layers(pert, 0, {}) - h, axis=1) / np.linalg.norm(h, axis=1)
+        print(f"oracle vs itself on a 1e-7 perturbed embedding: median {np.median(pert_err):.2e}, 90th pct "
+              f"{np.percentile(pert_err, 90):.2e}; rows above 1e-3: {int((pert_err > 1e-3).sum())}")
+        for q in (50, 90):
+            got, sens = np.percentile(row_err, q), np.percentile(pert_err, q)
+            assert got <= max(1e-3, 3 * sens), f"{q}th percentile row error {got:.2e} vs the oracle's own {sens:.2e}"
 
 
 # ---------------------------------------------------------------- draft tree at 1024 positions

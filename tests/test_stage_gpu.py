@@ -221,30 +221,3 @@ def test_tail_logits_many_rows_match_single_rows(sf):
         if i < 4:
             assert int(tk[i]) == o.sample_tail(rows[i])[0]
     g.close()
-
-
-def test_layer_kernel_decode_matches_per_op_launches(sf, monkeypatch):
-    """One launch per layer (SFC_DECODE_LAYER=1: cooperative kernel, grid barriers, the four
-    projections' weights streamed back to back) matches the oracle and the per-op launches on
-    full-size layers (d_model 2560, 8q/4kv x 256, ffn 10240; 4 of them, f32 cache: deeper random
-    stacks amplify last-bit differences chaotically), across one-split and merged attention."""
-    spec, shape = shape_pair(hidden=2560, n_heads=8, n_kv=4, head_dim=256, ffn=10240, vocab=4096, n_layers=4,
-                             seed=0x5EED)
-    prompt = so.synth_tokens(19, "prompt", 60, spec.vocab)
-    feed = so.synth_tokens(23, "feed", 8, spec.vocab)  # fixed decode inputs, crossing 64 cached keys
-    runs = {}
-    for flag in ("1", "0"):
-        monkeypatch.setenv("SFC_DECODE_LAYER", flag)
-        g = gpu_stage(sf, shape, 0, 3, True, True, kv_f32=True)
-        g.begin_token_ids("r", prompt)
-        n0 = sf.kernel_launches()
-        hs = [g.begin_token_ids("r", [int(t)])[-1] for t in feed]
-        runs[flag] = (np.stack(hs), (sf.kernel_launches() - n0) / len(feed))
-        g.close()
-    o = oracle_stage(spec, 0, 3, True, True, kv_fp16=False)
-    o.begin_token_ids("r", prompt)
-    ref = [o.begin_token_ids("r", [int(t)])[-1] for t in feed]
-    for i, r in enumerate(ref):
-        assert_close(runs["1"][0][i], r, 1e-3, f"layer kernel step {i}")
-        assert_close(runs["0"][0][i], r, 1e-3, f"per-op step {i}")
-    assert runs["1"][1] < runs["0"][1]  # the layer kernel was used: 1 launch per layer instead of 5
