@@ -197,6 +197,16 @@ cudaError_t attention(const float *q, float *out, KVLayer kv, const SeqInfo *seq
                       const int32_t *tok_limit, const uint64_t *tok_mask, int64_t n_tok, int64_t max_keys,
                       const AttnParams &p, void *scratch, size_t scratch_bytes, cudaStream_t st);
 
+// Per-layer embeddings (ops.cu).  ple_combine: in place on ple [n_tok][layers*P] holding the
+// model projection of the scaled token embeddings -> the combined per-layer inputs
+// (compute_ple_inputs, real_forward.rs:1157-1299).  ple_gelu: g[t][j] = gelu_tanh(g[t][j]) *
+// ple[t][layer*P + j].
+// ids: uint32 (ids64 = 0) or int64 token ids, checked against the vocabulary by the embedding.
+cudaError_t ple_combine(float *ple, int tok_type, const void *tok, const void *ids, int ids64, int64_t n_tok,
+                        int layers, int P, const float *norm, float proj_scale, float embed_scale, float combine_scale,
+                        cudaStream_t st);
+cudaError_t ple_gelu(float *g, const float *ple, int64_t n_tok, int P, int layers, int layer, cudaStream_t st);
+
 // Bounded-wait self-test (ops.cu): one bounded mbarrier wait of `limit` polls on a barrier that
 // completes (complete = 1) or never does (complete = 0, which records DEV_WAIT_TIMEOUT).
 cudaError_t wait_selftest(unsigned limit, int complete, cudaStream_t st);

@@ -441,6 +441,76 @@ cudaError_t attention(const float *q, float *out, KVLayer kv, const SeqInfo *seq
                     p.n_heads, p.head_dim, ns);
 }
 
+// ---------------------------------------------------------------- per-layer embeddings (PLE)
+// compute_ple_inputs (real_forward.rs:1157-1299) for the rows of one batch and every model layer.
+// In: ple [T][L*P] = per_layer_model_proj x (scaled token embedding).  Per (row t, layer l) chunk of
+// P values: v = ple * proj_scale; v = (v * 1/sqrt(mean(v^2) + eps)) * norm   (rms_norm_chunked_inplace,
+// eps 1e-6); v = (v + tok_row * embed_scale) * combine_scale, tok_row = the token's row of
+// per_layer_token_embd (F16 / BF16 / F32), proj_scale = hidden^-1/2, embed_scale = sqrt(P),
+// combine_scale = 2^-1/2.  grid (T, L).
+__global__ void __launch_bounds__(256) ple_combine_kernel(float *__restrict__ ple, const void *__restrict__ tok,
+                                                         int tok_type, const void *__restrict__ ids, int ids64, int LP,
+                                                         int P, const float *__restrict__ norm, float proj_scale,
+                                                         float embed_scale, float combine_scale, float eps) {
+  __shared__ float sh[8];
+  pdl_wait();
+  pdl_launch_dependents();
+  float *v = ple + int64_t(blockIdx.x) * LP + int64_t(blockIdx.y) * P;
+  const int64_t id = ids64 ? static_cast<const int64_t *>(ids)[blockIdx.x]
+                           : int64_t(static_cast<const uint32_t *>(ids)[blockIdx.x]);
+  const int64_t row = id * LP + int64_t(blockIdx.y) * P;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < P; i += 256) {
+    const float x = v[i] * proj_scale;
+    ss += x * x;
+  }
+  ss = block_sum<256>(ss, sh);
+  const float scale = 1.0f / sqrtf(ss / float(P) + eps);
+  for (int i = threadIdx.x; i < P; i += 256) {
+    float r;
+    if (tok_type == T_F16)
+      r = __half2float(static_cast<const __half *>(tok)[row + i]);
+    else if (tok_type == T_BF16)
+      r = __uint_as_float(uint32_t(static_cast<const uint16_t *>(tok)[row + i]) << 16);
+    else
+      r = static_cast<const float *>(tok)[row + i];
+    const float x = ((v[i] * proj_scale) * scale) * norm[i];
+    v[i] = (x + r * embed_scale) * combine_scale;
+  }
+}
+
+cudaError_t ple_combine(float *ple, int tok_type, const void *tok, const void *ids, int ids64, int64_t n_tok,
+                        int layers, int P, const float *norm, float proj_scale, float embed_scale, float combine_scale,
+                        cudaStream_t st) {
+  if (n_tok <= 0) return cudaSuccess;
+  if (tok_type != T_F16 && tok_type != T_BF16 && tok_type != T_F32) return cudaErrorInvalidValue;
+  return launch_pdl(ple_combine_kernel, dim3(unsigned(n_tok), unsigned(layers)), dim3(256), 0, st, ple, tok, tok_type,
+                    ids, ids64, layers * P, P, norm, proj_scale, embed_scale, combine_scale, 1e-6f);
+}
+
+// gated[t][j] = gelu_tanh(g[t][j]) * ple[t][l*P + j]  (real_forward.rs:1753-1778, real_math.rs:79-85)
+__global__ void ple_gelu_kernel(float *__restrict__ g, const float *__restrict__ ple, int64_t n, int P, int LP,
+                                int l) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t t = i / P;
+    const int j = int(i - t * P);
+    const float v = g[i], u = ple[t * LP + int64_t(l) * P + j];
+    const float k = 0.7978845608028654f;
+    const float inner = k * (v + 0.044715f * v * v * v);
+    g[i] = 0.5f * v * (1.0f + tanhf(inner)) * u;
+  }
+}
+
+cudaError_t ple_gelu(float *g, const float *ple, int64_t n_tok, int P, int layers, int layer, cudaStream_t st) {
+  const int64_t n = n_tok * P;
+  if (n <= 0) return cudaSuccess;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
+  return launch_pdl(ple_gelu_kernel, dim3(unsigned(blocks)), dim3(256), 0, st, g, ple, n, P, layers * P, layer);
+}
+
 // ---------------------------------------------------------------- bounded-wait self-test
 // One thread waits, through the same bounded mbarrier wait the streaming kernels use, on a barrier
 // that either completes (complete = 1: the thread arrives first) or that nothing ever arrives on

@@ -55,6 +55,72 @@ void encode_stage_tensor(const uint8_t *hidden, uint64_t hidden_len, const uint8
   memcpy(out + 8, &al, 4);
 }
 
+bool decode_prompt_aux(const uint8_t *b, uint64_t n, PromptAux &out, std::string &err) {
+  auto u32 = [&](uint64_t off) {
+    uint32_t v;
+    memcpy(&v, b + off, 4);
+    return v;
+  };
+  out = PromptAux();
+  if (n >= 20 && memcmp(b, "rsa1", 4) == 0) {
+    out.seq = u32(4);
+    out.layers = u32(8);
+    out.ple_dim = u32(12);
+    const uint32_t nh = u32(16);
+    const uint64_t vals = uint64_t(out.seq) * out.layers * out.ple_dim;
+    const uint64_t want = 20 + vals * 4 + uint64_t(nh) * 8;
+    if (n != want) {
+      err = "Invalid prompt-aux byte length " + std::to_string(n) + " (expected " + std::to_string(want) + ")";
+      return false;
+    }
+    out.ple = vals ? reinterpret_cast<const float *>(b + 20) : nullptr;
+    out.hashes.resize(nh);
+    if (nh) memcpy(out.hashes.data(), b + 20 + vals * 4, size_t(nh) * 8);
+    return true;
+  }
+  if (n < 16 || memcmp(b, "rpl1", 4) != 0) {
+    err = "Invalid prompt-aux payload";
+    return false;
+  }
+  out.seq = u32(4);
+  out.layers = u32(8);
+  out.ple_dim = u32(12);
+  const uint64_t vals = uint64_t(out.seq) * out.layers * out.ple_dim;
+  if (n != 16 + vals * 4) {
+    err = "Invalid prompt-aux byte length " + std::to_string(n) + " (expected " + std::to_string(16 + vals * 4) + ")";
+    return false;
+  }
+  out.ple = vals ? reinterpret_cast<const float *>(b + 16) : nullptr;
+  return true;
+}
+
+std::vector<uint8_t> encode_prompt_aux(const float *ple, uint32_t seq, uint32_t layers, uint32_t ple_dim,
+                                       const std::vector<uint64_t> &hashes) {
+  const uint64_t vals = ple ? uint64_t(seq) * layers * ple_dim : 0;
+  if (vals == 0 && hashes.empty()) return {};
+  if (!ple) seq = layers = 0;
+  std::vector<uint8_t> out(20 + vals * 4 + hashes.size() * 8);
+  const uint32_t nh = uint32_t(hashes.size());
+  memcpy(out.data(), "rsa1", 4);
+  memcpy(out.data() + 4, &seq, 4);
+  memcpy(out.data() + 8, &layers, 4);
+  memcpy(out.data() + 12, &ple_dim, 4);
+  memcpy(out.data() + 16, &nh, 4);
+  if (vals) memcpy(out.data() + 20, ple, size_t(vals) * 4);
+  if (nh) memcpy(out.data() + 20 + vals * 4, hashes.data(), size_t(nh) * 8);
+  return out;
+}
+
+std::vector<uint64_t> prefix_hashes(const uint32_t *ids, int64_t n) {
+  std::vector<uint64_t> out(size_t(n > 0 ? n : 0));
+  uint64_t h = 0xCBF29CE484222325ull;
+  for (int64_t i = 0; i < n; ++i) {
+    for (int k = 0; k < 4; ++k) h = (h ^ ((ids[i] >> (8 * k)) & 0xFF)) * 0x100000001B3ull;
+    out[size_t(i)] = h;
+  }
+  return out;
+}
+
 }  // namespace sfc
 
 using namespace sfc;

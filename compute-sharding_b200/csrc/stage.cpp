@@ -45,6 +45,10 @@ struct Layer {
   DevTensor *attn_norm = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *q_norm = nullptr, *k_norm = nullptr,
             *o = nullptr, *post_attn = nullptr, *ffn_norm = nullptr, *gate = nullptr, *up = nullptr,
             *down = nullptr, *post_ffw = nullptr, *scale = nullptr;
+  // per-layer embedding block (PLE, real_forward.rs:1753-1778): gate [hidden -> P], projection
+  // [P -> hidden], optional post norm
+  DevTensor *inp_gate = nullptr, *ple_proj = nullptr, *post_norm = nullptr;
+  bool has_ple() const { return inp_gate && ple_proj; }
   // attention schedule (LayerAttentionConfig, real_forward.rs:1407-1457); zeros: the stage's defaults
   float theta = 0.f;     // RoPE base
   int rotary_dim = 0;    // rotated dims (0: head_dim)
@@ -114,6 +118,15 @@ struct sfc_stage {
   std::vector<std::unique_ptr<DevTensor>> tensors;
   std::vector<Layer> layers;
   DevTensor *token_embd = nullptr, *output_norm = nullptr, *logits_w = nullptr, *rope_freqs = nullptr;
+  // PLE (real_forward.rs:1157-1299, :2320-2338): per-token table [layers*P][vocab], model projection
+  // [hidden -> layers*P], chunk norm [P]; P = ple_dim, ple_layers = layers of the whole model
+  DevTensor *ple_tok = nullptr, *ple_model_proj = nullptr, *ple_proj_norm = nullptr;
+  int ple_dim = 0, ple_layers = 0;
+  bool ple = false;             // some layer of this stage has a PLE block
+  float *ple_all = nullptr;     // [max_batch][ple_layers*P]: the current chunk's per-layer inputs
+  float *ple_gate = nullptr;    // [max_batch][P]
+  const float *ple_in = nullptr;  // host rows [n][ple_layers*P] for the next non-head forward (aux)
+  float *ple_out = nullptr;       // host rows [n][ple_layers*P] the next head forward also returns
   void *weight_arena = nullptr;
   int64_t weight_bytes = 0;
   // KV cache: [n_layers][max_sessions][K|V][n_kv][max_ctx][head_dim]
@@ -197,7 +210,10 @@ DevTensor **layer_field(Layer &L, const std::string &name) {
              {".ffn_norm.weight", &Layer::ffn_norm},
              {".post_attention_norm.weight", &Layer::post_attn},
              {".post_ffw_norm.weight", &Layer::post_ffw},
-             {".layer_output_scale.weight", &Layer::scale}};
+             {".layer_output_scale.weight", &Layer::scale},
+             {".inp_gate.weight", &Layer::inp_gate},
+             {".proj.weight", &Layer::ple_proj},
+             {".post_norm.weight", &Layer::post_norm}};
   for (auto &m : map)
     if (name.find(m.key) != std::string::npos) return &(L.*(m.f));
   return nullptr;
@@ -262,19 +278,6 @@ int apply_options(sfc_stage *h, const sfc_options *o) {
 
 // Builds device tensors, infers the config, allocates caches and buffers.
 int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
-  {  // Per-layer embeddings (PLE: a layer with inp_gate and proj, real_forward.rs:1753-1778) are not
-     // implemented here; refuse such a stage instead of running it without them.
-    std::set<int> gate, proj;
-    for (const auto &ht : hts) {
-      const int li = layer_of(ht.name);
-      if (li < 0) continue;
-      if (ht.name.find(".inp_gate.weight") != std::string::npos) gate.insert(li);
-      if (ht.name.find(".proj.weight") != std::string::npos) proj.insert(li);
-    }
-    for (int li : gate)
-      SFC_REQUIRE(!proj.count(li), "layer %d has per-layer embedding tensors (inp_gate, proj): PLE is not "
-                                  "supported by this backend", li);
-  }
   // classification + config inference (real_forward.rs:2258-2283)
   std::map<int, Layer> layer_map;
   std::vector<std::pair<HostTensor *, DevTensor *>> uploads;
@@ -313,6 +316,12 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
       h->output_norm = raw;
     } else if (ht.name == "output.weight") {
       h->logits_w = raw;
+    } else if (ht.name == "per_layer_token_embd.weight") {
+      h->ple_tok = raw;
+    } else if (ht.name == "per_layer_model_proj.weight") {
+      h->ple_model_proj = raw;
+    } else if (ht.name == "per_layer_proj_norm.weight") {
+      h->ple_proj_norm = raw;
     }
   }
   for (auto &kv : layer_map) h->layers.push_back(kv.second);
@@ -321,7 +330,7 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
 
   // norms must be F32 (real_forward.rs:478-488)
   for (auto &L : h->layers)
-    for (DevTensor *t : {L.attn_norm, L.q_norm, L.k_norm, L.post_attn, L.ffn_norm, L.post_ffw, L.scale})
+    for (DevTensor *t : {L.attn_norm, L.q_norm, L.k_norm, L.post_attn, L.ffn_norm, L.post_ffw, L.scale, L.post_norm})
       SFC_REQUIRE(!t || t->type == T_F32, "Expected F32 tensor for %s, got type %d", t->name.c_str(), t->type);
   if (h->rope_freqs) SFC_REQUIRE(h->rope_freqs->type == T_F32, "rope_freqs.weight must be F32");
   if (h->output_norm) SFC_REQUIRE(h->output_norm->type == T_F32, "output_norm.weight must be F32");
@@ -418,6 +427,43 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   } else {
     SFC_REQUIRE(h->logits_w && h->output_norm, "tail without layers needs logits tensors");
     h->hidden = int(h->output_norm->dims[0]);
+  }
+  // PLE configuration (real_forward.rs:2320-2338): width from per_layer_proj_norm, layer count from
+  // the model projection (or, on a stage without it, from the per-layer inputs it receives)
+  for (auto &L : h->layers) {
+    if (!L.inp_gate != !L.ple_proj) {
+      set_error("layer %d has only one of inp_gate / proj", L.index);
+      return SFC_E_INVALID;
+    }
+    h->ple = h->ple || L.has_ple();
+  }
+  if (h->ple) {
+    SFC_REQUIRE(h->ple_proj_norm && h->ple_proj_norm->type == T_F32, "PLE layers need per_layer_proj_norm.weight (F32)");
+    h->ple_dim = int(h->ple_proj_norm->in_dim);
+    SFC_REQUIRE(h->ple_dim > 0, "per_layer_proj_norm.weight is empty");
+    if (h->ple_model_proj) {
+      SFC_REQUIRE(h->ple_model_proj->in_dim == h->hidden && h->ple_model_proj->rows % h->ple_dim == 0,
+                  "per_layer_model_proj.weight dims do not match hidden %d / ple_dim %d", h->hidden, h->ple_dim);
+      h->ple_layers = int(h->ple_model_proj->rows / h->ple_dim);
+    } else {
+      h->ple_layers = int(h->end_layer) + 1;
+    }
+    for (auto &L : h->layers) {
+      if (!L.has_ple()) continue;
+      SFC_REQUIRE(L.index < h->ple_layers, "layer %d has no per-layer input (%d PLE layers)", L.index,
+                  h->ple_layers);
+      SFC_REQUIRE(L.inp_gate->in_dim == h->hidden && L.inp_gate->rows == h->ple_dim && L.ple_proj->in_dim == h->ple_dim &&
+                      L.ple_proj->rows == h->hidden && (!L.post_norm || L.post_norm->in_dim == h->hidden),
+                  "layer %d: PLE tensor shapes do not match hidden %d / ple_dim %d", L.index, h->hidden, h->ple_dim);
+    }
+    if (h->is_head) {
+      SFC_REQUIRE(h->ple_model_proj && h->ple_tok, "a head stage with PLE layers needs per_layer_model_proj.weight "
+                                                   "and per_layer_token_embd.weight");
+      SFC_REQUIRE(h->ple_tok->in_dim == int64_t(h->ple_layers) * h->ple_dim &&
+                      (h->ple_tok->type == T_F16 || h->ple_tok->type == T_BF16 || h->ple_tok->type == T_F32),
+                  "per_layer_token_embd.weight must be F16/BF16/F32 with %d x %d values per token", h->ple_layers,
+                  h->ple_dim);
+    }
   }
   h->fused = !h->layers.empty() && h->hidden % 256 == 0 && h->q_dim % 256 == 0 && h->ffn % 256 == 0 &&
              h->hidden <= 10240 && h->q_dim <= 10240 && h->ffn <= 10240;
@@ -543,6 +589,9 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
       (rc = alloc((void **)&h->tree_mask_dev, T * 8)) ||
       (rc = alloc((void **)&h->seq_dev, int64_t(h->max_sessions) * sizeof(SeqInfo))))
     return rc;
+  if (h->ple && ((rc = alloc((void **)&h->ple_all, T * int64_t(h->ple_layers) * h->ple_dim * 4)) ||
+                 (rc = alloc((void **)&h->ple_gate, T * int64_t(h->ple_dim) * 4))))
+    return rc;
   AttnParams ap = {};
   ap.n_heads = std::max(h->n_heads, 1);
   ap.n_kv = std::max(h->n_kv, 1);
@@ -608,7 +657,7 @@ void destroy_stage(sfc_stage *h) {
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
                   (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemv_split_mem, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
                   (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores, (void *)h->logit_scores,
-                  h->kv_arena, h->weight_arena})
+                  (void *)h->ple_all, (void *)h->ple_gate, h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
   h->ring.destroy();
   if (h->ev0) cudaEventDestroy(h->ev0);
@@ -688,6 +737,33 @@ GemvSeg seg_of(const DevTensor *w, const DevTensor *w2, float *y, int64_t ldy) {
   return g;
 }
 
+// Head ingress on the device: embedding rows of `ids` (uint32, or int64 with ids64) into h->resid and,
+// for PLE models, every layer's per-layer inputs into h->ple_all (compute_ple_inputs,
+// real_forward.rs:1157-1299: the model projection of the scaled embedding, then ple_combine).
+cudaError_t head_ingress(sfc_stage *h, const void *ids, int ids64, int64_t T, cudaStream_t st) {
+  cudaError_t e = embed(h->token_embd->type, h->token_embd->dev, h->vocab, h->hidden, ids, ids64, T, h->resid,
+                        device_error_ptr(), st);
+  if (e || !h->ple) return e;
+  const int64_t LP = int64_t(h->ple_layers) * h->ple_dim;
+  e = gemv(h->ple_model_proj->type, h->ple_model_proj->dev, nullptr, LP, h->hidden, h->resid, T, h->ple_all, LP, st);
+  if (e) return e;
+  return ple_combine(h->ple_all, h->ple_tok->type, h->ple_tok->dev, ids, ids64, T, h->ple_layers, h->ple_dim,
+                     F32P(h->ple_proj_norm), powf(float(h->hidden), -0.5f), sqrtf(float(h->ple_dim)),
+                     powf(2.0f, -0.5f), st);
+}
+
+// The per-layer embedding block of layer L (real_forward.rs:1753-1778) on the T rows of `states`:
+// states += rms_norm(proj(gelu_tanh(inp_gate(states)) * ple_in[layer])) * post_norm, then
+// states *= layer_output_scale.  states holds the full residual stream (nothing pending).
+cudaError_t ple_block(sfc_stage *h, const Layer &L, float *states, int64_t T, cudaStream_t st) {
+  const int P = h->ple_dim;
+  cudaError_t e = gemv(L.inp_gate->type, L.inp_gate->dev, nullptr, P, h->hidden, states, T, h->ple_gate, P, st);
+  if (!e) e = ple_gelu(h->ple_gate, h->ple_all, T, P, h->ple_layers, L.index, st);
+  if (!e) e = gemv(L.ple_proj->type, L.ple_proj->dev, nullptr, h->hidden, P, h->ple_gate, T, h->proj, h->hidden, st);
+  if (!e) e = add_norm(states, h->proj, F32P(L.post_norm), F32P(L.scale), 0, nullptr, nullptr, T, h->hidden, h->eps, st);
+  return e;
+}
+
 // q/k/v post-processing, KV append and attention of one layer.  Decode batches (one new token
 // per sequence) use the single fused decode kernel; other batches the two-kernel path.
 cudaError_t layer_attention(sfc_stage *h, const AttnParams &ap, const KVLayer &kv, int64_t T, int64_t max_keys,
@@ -715,12 +791,13 @@ cudaError_t run_layers_gemm(sfc_stage *h, int64_t T, int64_t max_keys, bool deco
   float *cur = h->resid, *other = h->resid2;
   void *gs = h->gemm_scratch;
   const size_t gsb = h->gemm_scratch_bytes;
+  bool pending = false;  // the previous layer's post-FFN residual add still runs in this layer's prologue
   for (size_t li = 0; li < h->layers.size(); ++li) {
     const Layer &L = h->layers[li];
     GemmPrologue pro = {};
     pro.eps = h->eps;
     pro.w_next = F32P(L.attn_norm);
-    if (li == 0) {
+    if (!pending) {
       pro.mode = L.attn_norm ? 1 : 0;
       pro.x = cur;
       pro.a = cur;
@@ -766,9 +843,16 @@ cudaError_t run_layers_gemm(sfc_stage *h, int64_t T, int64_t max_keys, bool deco
     pd.gate = h->act;
     pd.up = h->act2;
     if ((e = qgemm(&d, 1, h->ffn, pd, T, gs, gsb, st))) return e;
+    pending = true;
+    if (L.has_ple()) {  // the residual stream is needed whole: add the FFN output, then the PLE block
+      if ((e = add_norm(cur, h->proj, F32P(L.post_ffw), nullptr, 0, nullptr, nullptr, T, H, h->eps, st))) return e;
+      if ((e = ple_block(h, L, cur, T, st))) return e;
+      pending = false;
+    }
   }
   const Layer &Z = h->layers.back();
-  if ((e = add_norm(cur, h->proj, F32P(Z.post_ffw), F32P(Z.scale), 0, nullptr, nullptr, T, H, h->eps, st))) return e;
+  if (pending && (e = add_norm(cur, h->proj, F32P(Z.post_ffw), F32P(Z.scale), 0, nullptr, nullptr, T, H, h->eps, st)))
+    return e;
   if (cur != h->resid) e = cudaMemcpyAsync(h->resid, cur, size_t(T) * H * 4, cudaMemcpyDeviceToDevice, st);
   return e;
 }
@@ -778,12 +862,13 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
   cudaError_t e = cudaSuccess;
   const int H = h->hidden;
   float *cur = h->resid, *other = h->resid2;
+  bool pending = false;  // the previous layer's post-FFN residual add still runs in this layer's prologue
   for (size_t li = 0; li < h->layers.size(); ++li) {
     const Layer &L = h->layers[li];
     GemvPrologue pro = {};
     pro.eps = h->eps;
     pro.w_next = F32P(L.attn_norm);
-    if (li == 0) {
+    if (!pending) {
       pro.mode = L.attn_norm ? 1 : 0;
       pro.x = cur;
       pro.a = cur;
@@ -828,9 +913,16 @@ cudaError_t run_layers_fused(sfc_stage *h, int64_t T, int64_t max_keys, bool dec
     pd.mode = 0;
     pd.x = h->act;
     if ((e = gemv_fused(&d, 1, 1, h->ffn, pd, T, st, &h->gemv_split))) return e;
+    pending = true;
+    if (L.has_ple()) {  // the residual stream is needed whole: add the FFN output, then the PLE block
+      if ((e = add_norm(cur, h->proj, F32P(L.post_ffw), nullptr, 0, nullptr, nullptr, T, H, h->eps, st))) return e;
+      if ((e = ple_block(h, L, cur, T, st))) return e;
+      pending = false;
+    }
   }
   const Layer &Z = h->layers.back();
-  if ((e = add_norm(cur, h->proj, F32P(Z.post_ffw), F32P(Z.scale), 0, nullptr, nullptr, T, H, h->eps, st))) return e;
+  if (pending && (e = add_norm(cur, h->proj, F32P(Z.post_ffw), F32P(Z.scale), 0, nullptr, nullptr, T, H, h->eps, st)))
+    return e;
   if (cur != h->resid) e = cudaMemcpyAsync(h->resid, cur, size_t(T) * H * 4, cudaMemcpyDeviceToDevice, st);
   return e;
 }
@@ -863,6 +955,17 @@ cudaError_t run_layers(sfc_stage *h, int64_t T, int64_t max_keys, bool decode, c
     if ((e = gemv(L.gate->type, L.gate->dev, L.up->dev, h->ffn, H, h->xn, T, h->act, h->ffn, st))) return e;
     if ((e = gemv(L.down->type, L.down->dev, nullptr, H, h->ffn, h->act, T, h->proj, H, st))) return e;
     const bool more = li + 1 < h->layers.size();
+    if (L.has_ple()) {
+      if ((e = add_norm(h->resid, h->proj, F32P(L.post_ffw), nullptr, 0, nullptr, nullptr, T, H, h->eps, st))) return e;
+      if ((e = ple_block(h, L, h->resid, T, st))) return e;
+      if (more) {
+        const DevTensor *nn = h->layers[li + 1].attn_norm;
+        e = nn ? rms_norm(h->resid, F32P(nn), T, H, h->eps, h->xn, st)
+               : cudaMemcpyAsync(h->xn, h->resid, size_t(T) * H * 4, cudaMemcpyDeviceToDevice, st);
+        if (e) return e;
+      }
+      continue;
+    }
     if ((e = add_norm(h->resid, h->proj, F32P(L.post_ffw), F32P(L.scale), more ? 1 : 0,
                       more ? F32P(h->layers[li + 1].attn_norm) : nullptr, h->xn, T, H, h->eps, st)))
       return e;
@@ -878,7 +981,7 @@ struct SeqReq {
 // One forward chunk (sum of rows <= max_batch).  ids (uint32, host or device) for the head,
 // `in_dev` rows for other stages.  Output stays in h->resid.
 int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t *ids, bool ids_on_device,
-                  const float *in_dev, cudaStream_t st) {
+                  const float *in_dev, cudaStream_t st, const float *ple_host = nullptr) {
   int64_t T = 0, max_keys = 1, sum_keys = 0;
   for (auto &s : seqs) {
     SFC_REQUIRE(s.n > 0, "empty sequence in batch");
@@ -920,10 +1023,19 @@ int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t 
       SFC_CUDA(cudaMemcpyAsync(h->ids_dev, idh, size_t(T) * 4, cudaMemcpyHostToDevice, st));
       idd = h->ids_dev;
     }
-    SFC_CUDA(embed(h->token_embd->type, h->token_embd->dev, h->vocab, h->hidden, idd, 0, T, h->resid,
-                   device_error_ptr(), st));
+    SFC_CUDA(head_ingress(h, idd, 0, T, st));
   } else {
     SFC_CUDA(cudaMemcpyAsync(h->resid, in_dev, size_t(T) * h->hidden * 4, cudaMemcpyDeviceToDevice, st));
+    if (h->ple) {
+      if (!ple_host) {
+        h->ring.release(ri, st);
+        set_error("stage %s has per-layer embedding (PLE) layers: its rows need the per-layer inputs of the "
+                  "prompt aux section (continue_forward on StageTensor bytes)", h->stage_id.c_str());
+        return SFC_E_INVALID;
+      }
+      SFC_CUDA(cudaMemcpyAsync(h->ple_all, ple_host, size_t(T) * h->ple_layers * h->ple_dim * 4,
+                               cudaMemcpyHostToDevice, st));
+    }
   }
   h->ring.release(ri, st);
   h->attn_sum_keys = sum_keys;
@@ -953,11 +1065,16 @@ int forward_single(sfc_stage *h, const char *req, const uint32_t *ids_host, cons
       SFC_CUDA(cudaMemcpyAsync(h->hn, in_host + t0 * h->hidden, size_t(c) * h->hidden * 4, cudaMemcpyHostToDevice,
                                st));
     }
-    rc = forward_chunk(h, {SeqReq{s, c}}, ids_host ? ids_host + t0 : nullptr, false, h->hn, st);
+    rc = forward_chunk(h, {SeqReq{s, c}}, ids_host ? ids_host + t0 : nullptr, false, h->hn, st,
+                       h->ple_in ? h->ple_in + t0 * int64_t(h->ple_layers) * h->ple_dim : nullptr);
     if (rc) return rc;
     if (out_host)
       SFC_CUDA(cudaMemcpyAsync(out_host + t0 * h->hidden, h->resid, size_t(c) * h->hidden * 4,
                                cudaMemcpyDeviceToHost, st));
+    if (h->ple_out && h->ple && h->is_head) {  // the chunk's per-layer inputs, for the aux section
+      const int64_t LP = int64_t(h->ple_layers) * h->ple_dim;
+      SFC_CUDA(cudaMemcpyAsync(h->ple_out + t0 * LP, h->ple_all, size_t(c) * LP * 4, cudaMemcpyDeviceToHost, st));
+    }
   }
   SFC_CUDA(cudaEventRecord(h->ev1, st));
   SFC_CUDA(cudaStreamSynchronize(st));
@@ -1254,6 +1371,35 @@ int sfc_begin_token_ids(sfc_stage *h, const char *request_id, const uint32_t *id
   return forward_single(h, request_id, ids, nullptr, n, out_hidden, n > 1);
 }
 
+int sfc_begin_token_ids_bytes(sfc_stage *h, const char *request_id, const uint32_t *ids, int64_t n, void *out,
+                              uint64_t cap, uint64_t *out_len) {
+  clear_error();
+  SFC_REQUIRE(h && ids && out_len, "null argument");
+  SFC_REQUIRE(h->is_head, "Only the head stage may accept prompt ingress");
+  SFC_REQUIRE(n > 0, "Empty prompt");
+  const int64_t LP = h->ple ? int64_t(h->ple_layers) * h->ple_dim : 0;
+  const uint64_t hidden_len = uint64_t(n) * h->hidden * 4;
+  const uint64_t aux_len = (LP || n > 1) ? 20 + uint64_t(n) * LP * 4 + (n > 1 ? uint64_t(n) * 8 : 0) : 0;
+  const uint64_t need = encoded_stage_tensor_bytes(hidden_len, aux_len);
+  *out_len = need;
+  SFC_REQUIRE(out && cap >= need, "output holds %llu bytes, the payload needs %llu", (unsigned long long)cap,
+              (unsigned long long)need);
+  std::vector<float> rows(size_t(n) * h->hidden), ple(size_t(n * LP));
+  h->ple_out = LP ? ple.data() : nullptr;
+  const int rc = forward_single(h, request_id, ids, nullptr, n, rows.data(), n > 1);
+  h->ple_out = nullptr;
+  if (rc) return rc;
+  // begin_token_sequence (real_forward.rs:1096-1103): prefix hashes of a multi-token prompt and the
+  // per-layer inputs of every model layer travel in the aux section
+  const std::vector<uint8_t> aux = encode_prompt_aux(LP ? ple.data() : nullptr, uint32_t(n), uint32_t(h->ple_layers),
+                                                     uint32_t(h->ple_dim),
+                                                     n > 1 ? prefix_hashes(ids, n) : std::vector<uint64_t>());
+  SFC_REQUIRE(aux.size() == aux_len, "prompt aux size %zu, expected %llu", aux.size(), (unsigned long long)aux_len);
+  encode_stage_tensor(reinterpret_cast<const uint8_t *>(rows.data()), hidden_len, aux.data(), aux.size(),
+                      static_cast<uint8_t *>(out));
+  return SFC_OK;
+}
+
 int sfc_continue_forward(sfc_stage *h, const char *request_id, const float *in_hidden, int64_t n, float *out_hidden) {
   clear_error();
   SFC_REQUIRE(h && in_hidden, "null argument");
@@ -1311,8 +1457,28 @@ int sfc_continue_forward_bytes(sfc_stage *h, const char *request_id, const void 
   SFC_REQUIRE(out && cap >= need, "output holds %llu bytes, the payload needs %llu", (unsigned long long)cap,
               (unsigned long long)need);
   const std::string aux(reinterpret_cast<const char *>(s.aux), s.aux ? size_t(s.aux_len) : 0);  // out may be bytes
+  const int64_t rows = int64_t(in.size() / size_t(h->hidden));
+  std::vector<float> ple;  // per-layer inputs of the rows, [rows][ple_layers * ple_dim]
+  if (h->ple) {
+    // decode_prompt_aux (real_forward.rs:1896-1990); the per-layer inputs of every model layer
+    SFC_REQUIRE(s.aux, "stage %s has per-layer embedding (PLE) layers but the payload carries no prompt aux",
+                h->stage_id.c_str());
+    PromptAux pa;
+    std::string err;
+    SFC_REQUIRE(decode_prompt_aux(reinterpret_cast<const uint8_t *>(aux.data()), aux.size(), pa, err), "%s",
+                err.c_str());
+    SFC_REQUIRE(pa.ple && int64_t(pa.seq) == rows && int(pa.ple_dim) == h->ple_dim && int(pa.layers) >= h->ple_layers,
+                "prompt aux holds %u x %u x %u per-layer inputs; the stage needs %lld rows x %d layers x %d",
+                pa.seq, pa.layers, pa.ple_dim, (long long)rows, h->ple_layers, h->ple_dim);
+    const int64_t LP = int64_t(h->ple_layers) * h->ple_dim, LPin = int64_t(pa.layers) * pa.ple_dim;
+    ple.resize(size_t(rows * LP));
+    for (int64_t r = 0; r < rows; ++r)
+      memcpy(ple.data() + r * LP, reinterpret_cast<const uint8_t *>(pa.ple) + r * LPin * 4, size_t(LP) * 4);
+  }
   std::vector<float> res(in.size());
-  rc = sfc_continue_forward(h, request_id, in.data(), int64_t(in.size() / size_t(h->hidden)), res.data());
+  h->ple_in = h->ple ? ple.data() : nullptr;
+  rc = sfc_continue_forward(h, request_id, in.data(), rows, res.data());
+  h->ple_in = nullptr;
   if (rc) return rc;
   encode_stage_tensor(reinterpret_cast<const uint8_t *>(res.data()), s.hidden_len,
                       reinterpret_cast<const uint8_t *>(aux.data()), aux.size(), static_cast<uint8_t *>(out));
@@ -1623,8 +1789,7 @@ int sfc_generate_greedy(sfc_stage *h, const char *request_id, const uint32_t *pr
       cudaGraph_t g = nullptr;
       const long long k0 = g_kernel_launches;
       SFC_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-      cudaError_t e = embed(h->token_embd->type, h->token_embd->dev, h->vocab, h->hidden, h->tok_dev, 1, 1, h->resid,
-                            device_error_ptr(), st);
+      cudaError_t e = head_ingress(h, h->tok_dev, 1, 1, st);
       if (!e) e = run_layers(h, 1, h->max_ctx, true, st);
       if (!e) {
         if (h->output_norm)

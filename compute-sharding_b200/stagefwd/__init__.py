@@ -109,6 +109,7 @@ _PU64 = ctypes.POINTER(_U64)
 _sig("sfc_stage_tensor_sections", _I, ctypes.c_char_p, _U64, _PU64, _PU64, _PU64, _PU64)
 _sig("sfc_encode_stage_tensor_bytes", _I, ctypes.c_char_p, _U64, ctypes.c_char_p, _U64, _P, _U64, _PU64)
 _sig("sfc_continue_forward_bytes", _I, _P, ctypes.c_char_p, ctypes.c_char_p, _U64, _U64, _P, _U64, _PU64)
+_sig("sfc_begin_token_ids_bytes", _I, _P, ctypes.c_char_p, _P, _I64, _P, _U64, _PU64)
 _sig("sfc_sample_tail_bytes", _I, _P, ctypes.c_char_p, _U64, _U64, ctypes.POINTER(_U32), ctypes.POINTER(_F))
 
 lib = _lib
@@ -364,6 +365,18 @@ class CudaStageBackend:
         _check(_lib.sfc_continue_forward(self.h, request_id.encode(), hidden.ctypes.data, hidden.shape[0],
                                          out.ctypes.data), "continue_forward")
         return out
+
+    def begin_token_ids_bytes(self, request_id: str, ids) -> bytes:
+        """begin_prompt's StageTensor bytes: the rows framed with the prompt aux section (prefix
+        hashes of a multi-token prompt, every layer's per-layer inputs for a PLE model)."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        n = _U64()
+        _lib.sfc_begin_token_ids_bytes(self.h, request_id.encode(), ids.ctypes.data, ids.shape[0], None, 0,
+                                       ctypes.byref(n))  # size query (fails on the null output)
+        out = ctypes.create_string_buffer(max(int(n.value), 1))
+        _check(_lib.sfc_begin_token_ids_bytes(self.h, request_id.encode(), ids.ctypes.data, ids.shape[0], out,
+                                              len(out), ctypes.byref(n)), "begin_token_ids_bytes")
+        return out.raw[: int(n.value)]
 
     def continue_forward_bytes(self, request_id: str, payload: bytes, hidden_dim: int) -> bytes:
         """continue_forward on StageTensor::bytes (bare or stb1-framed rows; the aux section is

@@ -232,11 +232,19 @@ int sfc_stage_tensor_sections(const void *bytes, uint64_t n, uint64_t *hidden_of
                               uint64_t *aux_offset, uint64_t *aux_len);
 int sfc_encode_stage_tensor_bytes(const void *hidden, uint64_t hidden_len, const void *aux, uint64_t aux_len,
                                   void *out, uint64_t cap, uint64_t *out_len);
+/* begin_prompt's StageTensor payload for token ids (begin_token_sequence, real_forward.rs:988-1121,
+ * aux :1096-1103): the output rows framed with the prompt aux section when there is one ("rsa1":
+ * the prefix hashes of a multi-token prompt and, for a model with per-layer embeddings, the
+ * per-layer inputs of every model layer, real_forward.rs:1852-1894); bare rows otherwise.
+ * *out_len = the payload size (also set when cap is too small). */
+int sfc_begin_token_ids_bytes(sfc_stage *h, const char *request_id, const uint32_t *ids, int64_t n, void *out,
+                              uint64_t cap, uint64_t *out_len);
 /* continue_forward on a StageTensor payload (real_forward.rs:2054-2254): decodes the hidden rows
  * (decode_hidden_states, :1826-1850: the byte length must be a multiple of hidden_dim * 4), runs
  * sfc_continue_forward and writes the output rows framed with the input's aux section unchanged
  * (:2383-2387); *out_len = the output size (also set when cap is too small).  out may be bytes
- * itself but must not otherwise overlap it. */
+ * itself but must not otherwise overlap it.  A stage with per-layer embedding (PLE) layers takes
+ * their inputs from the aux section (decode_prompt_aux, :1896-1990) and fails without it. */
 int sfc_continue_forward_bytes(sfc_stage *h, const char *request_id, const void *bytes, uint64_t n,
                                uint64_t hidden_dim, void *out, uint64_t cap, uint64_t *out_len);
 /* sample_tail on a StageTensor payload: the last hidden row (decode_hidden_state, real_forward.rs:1818-1824). */

@@ -77,16 +77,22 @@ def test_gguf_and_payload_entry_points_validate_on_the_host(tmp_path):
     assert sf.lib.sfc_gguf_open(None, None) == -1
 
 
-def test_stage_with_per_layer_embeddings_is_refused(tmp_path):
-    """A stage whose layers carry PLE tensors is refused at load (before any device work) instead of
-    running without them."""
+def test_per_layer_embedding_stage_validation(tmp_path):
+    """Stages whose layers carry PLE tensors are checked at load, before any device work: the chunk
+    norm must be there, and a head needs the per-token table and the model projection."""
     import stagefwd as sf
     import stage_oracle as so
     spec = so.ModelSpec(hidden=256, n_heads=2, n_kv=1, head_dim=128, ffn=512, vocab=300, n_layers=2, seed=3,
                         ple_dim=64)
-    idx = so.write_pack(tmp_path, "stage-0", "full", 0, so.synth_stage(spec, 0, 1, True, True))
-    with pytest.raises(sf.StageError, match="PLE is not supported"):
-        sf.CudaStageBackend(idx).load_layout("m", "s", 0, 1, True, True)
+    full = so.synth_stage(spec, 0, 1, True, True)
+    cases = [("per_layer_proj_norm.weight", "per_layer_proj_norm"),
+             ("per_layer_token_embd.weight", "per_layer_token_embd"),
+             ("blk.1.proj.weight", "only one of inp_gate / proj")]
+    for k, (drop, msg) in enumerate(cases):
+        tensors = {n: t for n, t in full.items() if n != drop}
+        idx = so.write_pack(tmp_path / str(k), "stage-0", "full", 0, tensors)
+        with pytest.raises(sf.StageError, match=msg):
+            sf.CudaStageBackend(idx).load_layout("m", "s", 0, 1, True, True)
 
 
 def test_header_is_plain_c(tmp_path):

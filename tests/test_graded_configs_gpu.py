@@ -90,12 +90,28 @@ def test_layer_decode_after_2048_cached_positions(sf, kv_f32):
     g.close()
 
 
+def assert_same_stream(toks_g, toks_o, tail, tail_rows, tie=1e-2):
+    """Identical greedy streams, except that the streams may part at a step where the oracle's two
+    best capped scores are within `tie` of each other (a near-tie that the 1e-3 bar on the state
+    before it cannot decide) and the GPU took the runner-up; steps after that are not compared."""
+    for i, (a, b) in enumerate(zip(toks_g, toks_o)):
+        if a == b:
+            continue
+        _, _, top, _ = tail.sample_tail(tail_rows[i], top_k=2)
+        (t1, s1), (t2, s2) = top
+        print(f"streams part at step {i}: GPU {a}, oracle {b}; oracle top-2 {t1} ({s1:.6f}), {t2} ({s2:.6f})")
+        assert a == t2 and abs(s1 - s2) <= tie, f"step {i}: GPU {a}, oracle top-2 {top} (not a near-tie)"
+        return
+    assert len(toks_g) == len(toks_o)
+
+
 # ---------------------------------------------------------------- head/tail split, 512-token prompt
 @pytest.mark.parametrize("kv_f32", [False, True])
 def test_head_tail_512_prompt_64_greedy_tokens(sf, kv_f32):
     """42 layers as head 0-20 and tail 21-41, hidden rows handed off through continue_forward; the
     greedy stream equals the oracle's for 64 steps, with the fp16 cache (the workload's own) and
-    with the f32 cache.
+    with the f32 cache (streams may part only where the oracle's two best scores nearly tie: see
+    assert_same_stream).
 
     The prompt rows handed off after 21 layers are compared too, against the oracle's own
     sensitivity: this random model's prefill is chaotic (unscaled attention over many keys), so the
@@ -121,14 +137,16 @@ def test_head_tail_512_prompt_64_greedy_tokens(sf, kv_f32):
     oh, ot = oracle_stage(spec, 0, 20, True, False, kv_f32), oracle_stage(spec, 21, 41, False, True, kv_f32)
     h = oh.begin_token_ids("r", prompt)
     row_err = np.linalg.norm(handoff_g - h, axis=1) / np.linalg.norm(h, axis=1)
-    toks_o = [ot.sample_tail(ot.continue_forward("r", h)[-1])[0]]
+    tail_rows = [ot.continue_forward("r", h)[-1]]
+    toks_o = [ot.sample_tail(tail_rows[-1])[0]]
     for _ in range(n_steps - 1):
-        toks_o.append(ot.sample_tail(ot.continue_forward("r", oh.begin_token_ids("r", [toks_o[-1]]))[-1])[0])
+        tail_rows.append(ot.continue_forward("r", oh.begin_token_ids("r", [toks_o[-1]]))[-1])
+        toks_o.append(ot.sample_tail(tail_rows[-1])[0])
     above = row_err > 1e-3
     print(f"\n[{'f32' if kv_f32 else 'fp16'} cache] hand-off of the prompt (512 x 2560 after 21 layers): row "
           f"errors median {np.median(row_err):.2e}, 90th pct {np.percentile(row_err, 90):.2e}, max "
           f"{row_err.max():.2e}; rows above 1e-3: {int(above.sum())}, the first {np.flatnonzero(above)[:8].tolist()}")
-    assert toks_g == toks_o
+    assert_same_stream(toks_g, toks_o, ot, tail_rows)
     if kv_f32:
         emb = oh.embed(prompt)
         pert = (emb * (1 + 1e-7 * np.random.default_rng(0).standard_normal(emb.shape))).astype(np.float32)
