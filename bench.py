@@ -38,6 +38,9 @@ EMBD_BYTES = VOCAB * HIDDEN * 2
 # dram__bytes_read.sum + dram__bytes_write.sum of one qgemv_kernel<1,1> launch on that shape, from
 # the ncu capture summarised in profiles/qgemv_q4k_10240x2560_1tok.md
 GEMV_DRAM_BYTES = 14_810_368
+# the tail stage's logits pass (262144 x 2560 fp16 table) in layers' worth of time for the split
+# (64-row decode: about two layers)
+TAIL_COST_LAYERS = 2.0
 # greedy steps compared between the pipeline and a one-GPU run of the whole model (N > 1)
 CHECK_STEPS = 64
 BS64_WORKLOAD = "64 sequences, contexts uniform 512..3584 (seeded synthetic KV), 1 token each per step"
@@ -345,12 +348,13 @@ def run_pipeline(args):
     import torch
     import torch.distributed as dist
     import stagefwd as sf
-    from stagefwd.pipeline import CudaCompute, Pipeline, even_stage_split, make_groups
+    from stagefwd.pipeline import CudaCompute, Pipeline, balanced_stage_split, make_groups
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     ranks = make_groups(rank, world)
-    start, end = even_stage_split(N_LAYERS, world)[rank]
+    split = balanced_stage_split(N_LAYERS, world, TAIL_COST_LAYERS)
+    start, end = split[rank]
     be = sf.CudaStageBackend(synthetic=sf.ModelShape(), device=local, rope_theta=10000.0, max_ctx=4096,
                              max_sessions=66, max_batch_tokens=512).load_layout(
         "synthetic-gemma", f"stage-{rank}", start, end, ranks.is_head, ranks.is_tail)
@@ -453,7 +457,7 @@ def run_pipeline(args):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": bs1_s * 1e3 / args.steps,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic",
-                "config": dict(bs1_config(world), split=even_stage_split(N_LAYERS, world),
+                "config": dict(bs1_config(world), split=split, tail_cost_layers=TAIL_COST_LAYERS,
                                handoff="NCCL send/recv of f32 hidden rows"),
                 "tokens_match_1gpu": match,
                 "tokens_match_steps": CHECK_STEPS,

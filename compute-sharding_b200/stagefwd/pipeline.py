@@ -32,6 +32,50 @@ def even_stage_split(total_layers: int, stages: int) -> list[tuple[int, int]]:
     return out
 
 
+def balanced_stage_split(total_layers: int, stages: int, tail_cost: float = 0.0) -> list[tuple[int, int]]:
+    """Contiguous layer ranges that minimise the largest stage cost, every layer costing 1 and the
+    tail stage carrying `tail_cost` more (its logits pass, in layers' worth).  With tail_cost 0 the
+    result has the same stage sizes as even_stage_split, ordered so that earlier stages take the
+    extra layers (gguf.rs:307-329).  The reference offers only the even split; this option exists for
+    the tail's tied-embedding logits (1.34 GB per pass for the 262144 x 2560 table)."""
+    if stages <= 0 or stages > total_layers:
+        raise ValueError(f"cannot split {total_layers} layers into {stages} stages")
+    if tail_cost <= 0:
+        return even_stage_split(total_layers, stages)
+
+    def fits(cap):  # greedy from the tail: the tail first, then as many layers per stage as fit
+        sizes, left = [], total_layers
+        for i in range(stages):
+            budget = cap - (tail_cost if i == 0 else 0.0)
+            rest = stages - i - 1  # stages still to fill need at least one layer each
+            take = min(int(budget + 1e-9), left - rest)
+            if take < 1:
+                return None
+            sizes.append(take)
+            left -= take
+        return sizes[::-1] if left == 0 else None
+
+    lo, hi = 1.0, float(total_layers) + tail_cost
+    best = fits(hi)
+    for _ in range(60):  # bisection on the largest stage cost
+        mid = (lo + hi) / 2
+        got = fits(mid)
+        if got is None:
+            lo = mid
+        else:
+            hi, best = mid, got
+    # the tail takes the most layers its share allows; the rest are split evenly over the other
+    # stages (earlier stages take the extra layers, as the even split does)
+    tail = min(int(hi - tail_cost + 1e-9), total_layers - (stages - 1))
+    if stages > 1 and tail >= 1 and -(-(total_layers - tail) // (stages - 1)) <= hi + 1e-9:
+        return even_stage_split(total_layers - tail, stages - 1) + [(total_layers - tail, total_layers - 1)]
+    out, start = [], 0
+    for n in best:
+        out.append((start, start + n - 1))
+        start += n
+    return out
+
+
 class StageCompute:
     """Per-rank compute interface used by the pipeline driver."""
 

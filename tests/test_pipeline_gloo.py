@@ -107,6 +107,22 @@ def test_even_stage_split_matches_reference_rule():
         even_stage_split(3, 4)
 
 
+def test_balanced_split_counts_the_tail_logits():
+    from stagefwd.pipeline import balanced_stage_split, even_stage_split
+
+    def cost(split, tc):
+        return max((e - s + 1) + (tc if i == len(split) - 1 else 0) for i, (s, e) in enumerate(split))
+
+    for n in (1, 2, 3, 4, 8):
+        assert balanced_stage_split(42, n, 0.0) == even_stage_split(42, n)
+        for tc in (0.5, 2.0, 4.0, 12.0):
+            sp = balanced_stage_split(42, n, tc)
+            assert sp[0][0] == 0 and sp[-1][1] == 41 and all(sp[i][1] + 1 == sp[i + 1][0] for i in range(n - 1))
+            assert all(e >= s for s, e in sp)
+            assert cost(sp, tc) <= cost(even_stage_split(42, n), tc)
+    assert [e - s + 1 for s, e in balanced_stage_split(42, 8, 2.0)] == [6, 6, 6, 5, 5, 5, 5, 4]
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_pipeline_matches_single_process(world):
     ctx = mp.get_context("spawn")
