@@ -394,6 +394,9 @@ def run_pipeline(args):
     k0 = sf.kernel_launches()
     # clocks are sampled on rank 0's GPU only: one sampler process per rank slowed the ranks
     with ClockSampler(local, enabled=rank == 0) as clk:
+        # the sampler starts on rank 0 only: line the ranks up again before the timed region
+        dist.barrier()
+        torch.cuda.synchronize()
         e0.record()
         for _ in range(args.steps):
             tok = pipe.step(["bs1"], [1], tok if tok is not None else torch.zeros(1, dtype=torch.int64, device=dev))
