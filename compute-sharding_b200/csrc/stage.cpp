@@ -611,10 +611,15 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
   SFC_CUDA(cudaMemset(h->gemv_split_mem, 0, gemv_split_bytes(kGemvSplitCtas)));
   if (h->fused && T >= QGEMM_MIN_TOKENS) {
     bool ok = true;
-    for (const Layer &L : h->layers)
+    for (const Layer &L : h->layers) {
       for (const DevTensor *w : {L.q, L.k, L.v, L.o, L.gate, L.up, L.down})
         ok = ok && (w ? qgemm_supported(w->type, w->in_dim) && reinterpret_cast<uintptr_t>(w->dev) % 16 == 0
                       : (w == L.k || w == L.v) && !L.own_kv());
+      // one GEMM launch covers q/k/v and the gate/up pair: fp16 and K-quant weights do not mix in one
+      for (const DevTensor *w : {L.k, L.v})
+        ok = ok && (!w || !L.q || (w->type == T_F16) == (L.q->type == T_F16));
+      ok = ok && (!L.gate || !L.up || (L.gate->type == T_F16) == (L.up->type == T_F16));
+    }
     if (ok) {
       size_t gb = 0;
       for (int64_t K : {int64_t(H), int64_t(h->q_dim), int64_t(h->ffn)}) gb = std::max(gb, qgemm_scratch_bytes(T, K));
