@@ -1,6 +1,5 @@
 // gemv_core.cuh — device core of the K-quant GEMV (see gemv.cu): activation image, tensor-pipe
 // MMA units, the CTA work partition and stage walk, and the cross-CTA finish of shared tiles.
-// Shared by the per-matrix GEMV kernel and the fused decode-layer kernel.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -559,33 +558,6 @@ __device__ __forceinline__ int build_stage_table(const QGemvArgs &a, const CtaTi
   while (wk.more(ct) && n < a.max_stages) wk.next(a, ct, tab[n++]);
   if (wk.more(ct) && a.err) atomicExch(a.err, DEV_BAD_ARG);
   return n;
-}
-
-// Producer warp: streams the stages of a table into the ring (lane 0 issues; the whole warp calls).
-template <int NMAT>
-__device__ __forceinline__ void produce_stages(const QGemvArgs &a, const GemvStage *tab, int nstages, uint8_t *ring,
-                                               uint64_t *full, uint64_t *empty, RingPos &rp, int &issued, int lane) {
-  for (int s = 0; s < nstages; ++s) {
-    if (issued >= a.nstage) {  // wait for the slot's previous stage to be consumed
-      if (lane == 0) mbar_wait_bounded(&empty[rp.slot], uint32_t(rp.phase ^ 1), a.err);
-      __syncwarp();
-    }
-    if (lane == 0) {
-      const GemvStage st = tab[s];
-      const GemvSegK &S = a.seg[st.sg];
-      // the stage's records of each matrix: one contiguous range
-      const uint32_t bytes = uint32_t(st.nbs) * uint32_t(S.rec);
-      const int64_t first = int64_t(st.tau - S.tile0) * a.nb + st.b0;
-      mbar_arrive_expect_tx(&full[rp.slot], bytes * NMAT);
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m)
-        bulk_g2s(ring + size_t(rp.slot) * a.stage_bytes + m * S.nbs * S.rec, S.w[m] + first * S.rec, bytes,
-                 &full[rp.slot]);
-    }
-    __syncwarp();
-    ++issued;
-    rp.advance(a.nstage);
-  }
 }
 
 // Producer warp of a one-projection launch: walks the CTA's stages itself (the same walk that fills
