@@ -4,7 +4,7 @@ HBM bandwidth, against the reference's CPU stage path timed on this host.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N ... bench.py --gpus N   (one pipeline stage per GPU)
-  python bench.py --case decode|gemv|gemm [...]      (fixed workloads for profilers, no JSON line)
+  python bench.py --case decode|prefill|gemv|gemm [...]   (fixed workloads for profilers, no JSON line)
 
 One JSON line on rank 0.  `value` = bs1 greedy decode tokens/s (whole job); `bs64` = batched
 decode tokens/s; `roofline` = the Q4_K GEMV (10240 x 2560, one token, cold L2) against the
@@ -37,13 +37,19 @@ LAYER_WEIGHT_BYTES = 60_518_400
 EMBD_BYTES = VOCAB * HIDDEN * 2
 # dram__bytes_read.sum + dram__bytes_write.sum of one qgemv_kernel<1,1> launch on that shape, from
 # the ncu capture summarised in profiles/qgemv_q4k_10240x2560_1tok.md
-GEMV_DRAM_BYTES = 14_810_368
+GEMV_DRAM_BYTES = 14_816_512
 # the tail stage's logits pass (262144 x 2560 fp16 table) in layers' worth of time for the split
 # (64-row decode: about two layers)
 TAIL_COST_LAYERS = 2.0
 # greedy steps compared between the pipeline and a one-GPU run of the whole model (N > 1)
 CHECK_STEPS = 64
 BS64_WORKLOAD = "64 sequences, contexts uniform 512..3584 (seeded synthetic KV), 1 token each per step"
+# multiply-add FLOPs of one 512-token prefill: the projections of 42 layers (q 2048, k 1024, v 1024,
+# o, gate, up, down over hidden 2560 / ffn 10240), causal attention (8 query heads x 256 dims, QK and
+# PV), and the logits of the last row (262144 x 2560)
+LAYER_PARAMS = 2560 * (2048 + 1024 + 1024) + 2048 * 2560 + 3 * 2560 * 10240
+PREFILL_FLOP = (2 * PROMPT * LAYER_PARAMS * N_LAYERS + N_LAYERS * 2 * 2 * 8 * 256 * PROMPT * (PROMPT + 1) // 2
+                + 2 * HIDDEN * VOCAB)
 
 
 def bs1_config(world: int = 1) -> dict:
@@ -64,6 +70,14 @@ def peaks():
         d = json.loads(p.read_text())
         return d.get("hbm_gbs", 6650.0), "measured"
     return 6650.0, "fallback"
+
+
+def bf16_sustained_tflops() -> float:
+    """Dense bf16 GEMM throughput held for seconds (the denominator for a whole prefill)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text()).get("bf16_tflops_sustained", 1400.0))
+    return 1400.0
 
 
 class ClockSampler:
@@ -283,12 +297,39 @@ def run_single(args):
         spec_res[label] = {"ms_per_verify": 1e3 * statistics.median(times), "accepted_mean": float(np.mean(accepted))}
     be.clear_decode_session("verify")
 
+    # ---- prefill / time to first token: the 512-token prompt into a fresh session (42 layers on the
+    # tensor-core GEMM), logits of the last row and argmax; device-timed with the ids already on the
+    # device, and end to end through the C ABI (host ids in, rows and the token back to the host)
+    dev = torch.device("cuda")
+    pids = torch.from_numpy(prompt.astype(np.int32)).to(dev)
+    pout = torch.empty(PROMPT, HIDDEN, device=dev)
+    ptok = torch.empty(1, dtype=torch.int64, device=dev)
+    psc = torch.empty(1, dtype=torch.float32, device=dev)
+    pf_dev, pf_host = [], []
+    for rep in range(max(args.warmup, 3) + 5):
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        be.forward_dev(["pf"], [PROMPT], ids_dev=pids, out_dev=pout, append=False)
+        be.sample_dev(pout[PROMPT - 1:], ptok, psc)
+        f1.record()
+        torch.cuda.synchronize()
+        be.clear_decode_session("pf")
+        t0 = time.perf_counter()
+        rows = be.begin_token_ids("pfh", prompt)
+        be.sample_tail(rows[PROMPT - 1:])
+        dt = time.perf_counter() - t0
+        be.clear_decode_session("pfh")
+        if rep >= max(args.warmup, 3):
+            pf_dev.append(f0.elapsed_time(f1))
+            pf_host.append(dt * 1e3)
+    pf_ms = statistics.median(pf_dev)
+    bf16_peak = bf16_sustained_tflops()
+
     # ---- bs64 batched decode, contexts 512..3584 (seeded), one token per sequence per step
     ctx = rng.integers(512, 3585, 64)
     names = [f"b{i}" for i in range(64)]
     for i, n in enumerate(names):
         be.fill_session_synthetic(n, int(ctx[i]), seed=100 + i)
-    dev = torch.device("cuda")
     ids = torch.from_numpy(rng.integers(0, VOCAB, 64).astype(np.int32)).to(dev)
     out = torch.empty(64, HIDDEN, device=dev)
     tk = torch.empty(64, dtype=torch.int64, device=dev)
@@ -327,6 +368,11 @@ def run_single(args):
         "bs64": {"value": bs64_tps, "unit": "tokens/s", "steps": bsteps, "ms_per_step": bs64_s * 1e3 / bsteps,
                  "workload": BS64_WORKLOAD},
         "gemv": {"value": roof["achieved"], "unit": "GB/s", "frac_of_hbm": roof["frac"]},
+        "prefill": {"ttft_ms": pf_ms, "ttft_ms_e2e": statistics.median(pf_host), "tflops": PREFILL_FLOP / pf_ms / 1e9,
+                    "frac_of_bf16_sustained": PREFILL_FLOP / pf_ms / 1e9 / bf16_peak,
+                    "flop": PREFILL_FLOP,
+                    "workload": "512-token prompt, fresh session, 42 layers + last-row logits + argmax; "
+                                "e2e = begin_token_ids + sample_tail with host buffers"},
         "spec_verify": dict(spec_res, workload="1024 cached positions, 16-node draft tree (2-2-2-2, BFS, truncated) "
                                                "of random tokens: tree-masked forward of 42 layers, logits over "
                                                "262144, acceptance walk (greedy / seeded T=0.8), KV compaction; "
@@ -501,6 +547,29 @@ def case_decode(steps: int, ctx: int, batch: int):
     print("decode", steps, "steps, batch", batch, "ctx", ctx, "tokens", tk.tolist()[:8])
 
 
+def case_prefill(steps: int, tokens: int):
+    """`steps` prefills of a `tokens`-token prompt into a fresh session (42 layers on the tensor-core
+    GEMM, last-row logits and argmax), device-pointer calls."""
+    import torch
+    import stagefwd as sf
+    dev = torch.device("cuda")
+    shape = sf.ModelShape()
+    be = sf.CudaStageBackend(synthetic=shape, rope_theta=10000.0, max_ctx=max(tokens + 8, 64), max_sessions=2,
+                             max_batch_tokens=tokens).load_layout("synthetic-gemma", "full", 0, shape.n_layers - 1,
+                                                                  True, True)
+    ids = torch.arange(tokens, dtype=torch.int32, device=dev) * 997 % shape.vocab
+    out = torch.empty(tokens, shape.hidden, device=dev)
+    tk = torch.empty(1, dtype=torch.int64, device=dev)
+    sc = torch.empty(1, dtype=torch.float32, device=dev)
+    for _ in range(steps):
+        be.forward_dev(["p"], [tokens], ids_dev=ids, out_dev=out, append=False)
+        be.sample_dev(out[tokens - 1:], tk, sc)
+        be.clear_decode_session("p")
+    torch.cuda.synchronize()
+    be.close()
+    print("prefill", steps, "x", tokens, "tokens, first token", int(tk.item()))
+
+
 def case_matmul(launches: int, tokens: int):
     """`launches` calls of sfc_matmul on the Q4_K 10240 x 2560 shape with `tokens` tokens (the GEMV
     from 1 to 7 tokens, the tensor-core GEMM from 8), over weight copies larger than twice the L2."""
@@ -529,11 +598,11 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--case", choices=["decode", "gemv", "gemm"],
+    ap.add_argument("--case", choices=["decode", "prefill", "gemv", "gemm"],
                     help="run a fixed workload for a profiler instead of the benchmark")
     ap.add_argument("--ctx", type=int, default=512, help="--case decode: cached positions per sequence")
     ap.add_argument("--batch", type=int, default=1, help="--case decode: sequences per step")
-    ap.add_argument("--tokens", type=int, default=64, help="--case gemm: tokens per launch")
+    ap.add_argument("--tokens", type=int, default=64, help="--case gemm / prefill: tokens per launch / prompt")
     ap.add_argument("--launches", type=int, default=8, help="--case gemv/gemm: launches")
     args = ap.parse_args()
     if args.case:
@@ -541,6 +610,8 @@ def main():
         torch.cuda.set_device(0)
         if args.case == "decode":
             case_decode(args.steps, args.ctx, args.batch)
+        elif args.case == "prefill":
+            case_prefill(args.steps, args.tokens)
         else:
             case_matmul(args.launches, 1 if args.case == "gemv" else args.tokens)
         return

@@ -196,6 +196,26 @@ size_t attention_scratch_bytes(int64_t n_tok, const AttnParams &p, int64_t max_k
 cudaError_t attention(const float *q, float *out, KVLayer kv, const SeqInfo *seqs, const int32_t *tok_seq,
                       const int32_t *tok_limit, const uint64_t *tok_mask, int64_t n_tok, int64_t max_keys,
                       const AttnParams &p, void *scratch, size_t scratch_bytes, cudaStream_t st);
+// Merge of split-key partials [n_tok][n_heads][n_split][hd + 2] (m, l, unnormalised sums).
+cudaError_t attn_combine(const float *part, float *out, int64_t n_tok, int n_heads, int hd, int n_split,
+                         cudaStream_t st);
+
+// The same attention on the tensor cores (fattn.cu) for an fp16 cache: the batch's rows in query
+// tiles of flash_attention_tile_tokens(p) consecutive tokens of one sequence (FaTileRef: sequence
+// index, first token within it), the cache as the arena of `arena_rows` rows of head_dim fp16
+// (layer slab, slot, K|V, kv head, position), this layer's slab from row `layer_row0`.
+struct FaTileRef {
+  int32_t seq, t0;
+};
+bool flash_attention_supported(const AttnParams &p);
+int flash_attention_tile_tokens(const AttnParams &p);
+// Builds (and caches) the cache's tensor map; false when the arena cannot be described.
+bool flash_attention_prepare(void *kv_arena, int64_t arena_rows, int head_dim);
+size_t flash_attention_scratch_bytes(int64_t n_tok, const AttnParams &p);
+cudaError_t flash_attention(const float *q, float *out, void *kv_arena, int64_t arena_rows, int64_t layer_row0,
+                            const SeqInfo *seqs, const FaTileRef *tiles, int n_tiles, const int32_t *tok_limit,
+                            const uint64_t *tok_mask, int64_t n_tok, int64_t max_keys, const AttnParams &p,
+                            void *scratch, size_t scratch_bytes, cudaStream_t st);
 
 // Per-layer embeddings (ops.cu).  ple_combine: in place on ple [n_tok][layers*P] holding the
 // model projection of the scaled token embeddings -> the combined per-layer inputs

@@ -389,6 +389,13 @@ __global__ void attn_combine_kernel(const float *__restrict__ part, float *__res
   }
 }
 
+cudaError_t attn_combine(const float *part, float *out, int64_t n_tok, int n_heads, int hd, int n_split,
+                         cudaStream_t st) {
+  if (n_tok <= 0) return cudaSuccess;
+  return launch_pdl(attn_combine_kernel, dim3(unsigned(n_tok), unsigned(n_heads)), dim3(256), 0, st, part, out, n_heads,
+                    hd, n_split);
+}
+
 static int attn_splits(int64_t n_tok, const AttnParams &p, int64_t max_keys) {
   const int64_t ctas = n_tok * p.n_kv;
   int64_t want = (2 * num_sms() + ctas - 1) / ctas;

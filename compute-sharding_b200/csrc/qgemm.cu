@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace sfc {
 
@@ -75,130 +76,6 @@ struct QGemmArgs {
   int64_t part_ld;       // tiles * 128
   unsigned *err;
 };
-
-// ---------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// bring a box into L2 ahead of its load into shared memory
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
-// K-quant records of 8 consecutive 16-row tiles for one block: map [tile][block][chunk][bytes]
-__device__ __forceinline__ void tma_load_rec(void *dst, const CUtensorMap *map, int block, int tile, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(block), "r"(tile), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_rec(const CUtensorMap *map, int block, int tile) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global [%0, {%1, %2, %3, %4}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(0), "r"(0), "r"(block), "r"(tile)
-               : "memory");
-}
-
-// Non-suspending poll (mbarrier.test_wait): a thread parked by try_wait can wake well after the
-// phase completes, which stalls the single-thread MMA and producer loops.  Bounded like
-// mbar_wait_bounded.
-constexpr unsigned QG_SPIN_LIMIT = 1u << 28;
-__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_spin(uint64_t *bar, uint32_t parity, unsigned *err) {
-  for (unsigned i = 0; i < QG_SPIN_LIMIT; ++i)
-    if (mbar_test(bar, parity)) return true;
-  if (err) atomicExch(err, DEV_WAIT_TIMEOUT);
-  return false;
-}
-
-// One lane polls the barrier and the warp proceeds together (dozens of threads spinning on one
-// mbarrier slow down the threads that complete it).  For barriers that only order work; data
-// written by the async proxy is waited for by every reading thread.
-__device__ __forceinline__ void warp_wait(uint64_t *bar, uint32_t parity, unsigned *err) {
-  if ((threadIdx.x & 31) == 0) mbar_spin(bar, parity, err);
-  __syncwarp();
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (A and B both fp16), fp32 accumulate
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
-         (uint64_t(2) << 61);
-}
-
-template <int NREG>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[NREG]);
-
-template <>
-__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, uint32_t (&r)[4]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(taddr));
-}
-
-template <>
-__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-
-template <>
-__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 16-byte piece j (8 fp16 along K) of row n in a 128-byte-swizzled K-major tile
-__device__ __forceinline__ uint32_t sw128_off(int n, int j) {
-  return uint32_t((n >> 3) * 1024 + (n & 7) * 128 + ((j ^ (n & 7)) << 4));
-}
 
 // fp16x2 (1024 + q0, 1024 + q1) -> (q0 * s, q1 * s): (1024 + q) * s - 1024 * s is exact and
 // representable (q <= 15, s <= 63), so the single rounding of the fused multiply-add is exact.
@@ -415,24 +292,6 @@ constexpr int QK_ACOL0 = 256;  // first TMEM column of the A ring
 constexpr int QK_TMEM_COLS = 512;
 
 constexpr int QK_BST = 2;      // B ring: two 256-element blocks (QG_CPB chunks of 2*TN rows x 128 B each)
-
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, fp32 accumulate
-__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
 
 __host__ __device__ constexpr size_t qgemm_kq_smem(int tn) {
   return 1024 + size_t(QK_BST) * QG_CPB * 2 * tn * 128 + size_t(QG_RST) * QG_RAW_BYTES + 4 * QG_META * tn * 4 +
@@ -931,19 +790,6 @@ cudaError_t geglu(const float *gate, const float *up, float *out, int64_t n, cud
 }
 
 // ---------------------------------------------------------------- host side
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // Tiled K-quant records as a 4D uint8 view [tile][block][rec/row_x][row_x] (row_x = 256 B for Q4_K,
 // 240 B for Q6_K), box = one block's records of 8 tiles (128 weight rows); tiles past the end read
 // as zeros.

@@ -160,6 +160,12 @@ struct sfc_stage {
   uint64_t *tree_mask_dev = nullptr;
   bool tree_active = false;
   float *tree_scores = nullptr;
+  // tensor-core attention for multi-row batches (fp16 cache): query tiles of the current batch
+  bool fa_ok = false;
+  int fa_tt = 0;                       // tokens per query tile
+  FaTileRef *fa_tiles_dev = nullptr;   // [max_batch + max_sessions]
+  int fa_ntiles = 0;
+  int64_t kv_rows = 0;                 // head_dim-element rows of the KV arena
   int64_t tree_scores_rows = 0;
   // tensor-core logits for 8+ rows (fp16 tied embedding): raw then capped scores of up to 64 rows
   float *logit_scores = nullptr;
@@ -561,7 +567,11 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
                 h->max_ctx, h->max_sessions);
       return SFC_E_NOMEM;
     }
+    // positions past a sequence's end are read (and multiplied by zero weights) by the tensor-core
+    // attention's whole key tiles: keep every cache row finite from the start
+    SFC_CUDA(cudaMemset(h->kv_arena, 0, size_t(h->kv_bytes)));
   }
+  h->kv_rows = h->head_dim > 0 ? h->kv_bytes / elt / h->head_dim : 0;
   h->slot_used.assign(size_t(h->max_sessions), 0);
 
   // activations
@@ -601,6 +611,14 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
     amax = std::max(amax, attention_scratch_bytes(t, ap, h->max_ctx));
     amax = std::max(amax, decode_attention_scratch_bytes(t, ap, h->max_ctx));
   }
+  ap.kv_f32 = h->kv_f32;
+  ap.max_ctx = h->max_ctx;
+  h->fa_ok = T >= 2 && flash_attention_supported(ap) && flash_attention_prepare(h->kv_arena, h->kv_rows, h->head_dim);
+  if (h->fa_ok) {
+    h->fa_tt = flash_attention_tile_tokens(ap);
+    amax = std::max(amax, flash_attention_scratch_bytes(T, ap));
+    if ((rc = alloc((void **)&h->fa_tiles_dev, (T + h->max_sessions) * int64_t(sizeof(FaTileRef))))) return rc;
+  }
   h->attn_scratch = amax;
   h->logit_scratch = logits_scratch_bytes(T);
   if ((rc = alloc(&h->scratch, int64_t(std::max(h->attn_scratch, h->logit_scratch))))) return rc;
@@ -633,7 +651,8 @@ int build_stage(sfc_stage *h, std::vector<HostTensor> &hts) {
     }
   }
   SFC_CUDA(cudaMemset(h->attn_counters, 0, size_t(T) * ap.n_kv * 4));
-  rc = h->ring.init(size_t(T) * 8 + size_t(h->max_sessions) * sizeof(SeqInfo) + 256);
+  rc = h->ring.init(size_t(T) * 8 + size_t(h->max_sessions) * sizeof(SeqInfo) +
+                    size_t(T + h->max_sessions) * sizeof(FaTileRef) + 256);
   if (rc) return rc;
   return SFC_OK;
 }
@@ -661,7 +680,7 @@ void destroy_stage(sfc_stage *h) {
                   (void *)h->att, (void *)h->act, (void *)h->hn, (void *)h->score_dev, (void *)h->ids_dev,
                   (void *)h->tok_dev, (void *)h->gen_tokens_dev, (void *)h->tok_seq_dev, (void *)h->step_dev,
                   (void *)h->seq_dev, h->scratch, (void *)h->attn_counters, h->gemv_split_mem, h->gemm_scratch, (void *)h->act2, (void *)h->tree_rope_dev,
-                  (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores, (void *)h->logit_scores,
+                  (void *)h->tree_limit_dev, (void *)h->tree_path_dev, (void *)h->tree_mask_dev, (void *)h->tree_scores, (void *)h->logit_scores, (void *)h->fa_tiles_dev,
                   (void *)h->ple_all, (void *)h->ple_gate, h->kv_arena, h->weight_arena})
     if (p) cudaFree(p);
   h->ring.destroy();
@@ -780,6 +799,13 @@ cudaError_t layer_attention(sfc_stage *h, const AttnParams &ap, const KVLayer &k
   cudaError_t e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev,
                            tr ? h->tree_rope_dev : nullptr, T, ap, st);
   if (e) return e;
+  if (h->fa_ok && h->fa_ntiles > 0 && !decode && flash_attention_supported(ap)) {
+    const int64_t elt = h->kv_f32 ? 4 : 2;
+    const int64_t row0 = (static_cast<char *>(kv.base) - static_cast<char *>(h->kv_arena)) / elt / h->head_dim;
+    return flash_attention(h->q, h->att, h->kv_arena, h->kv_rows, row0, h->seq_dev, h->fa_tiles_dev, h->fa_ntiles,
+                           tr ? h->tree_limit_dev : nullptr, tr ? h->tree_mask_dev : nullptr, T, max_keys, ap,
+                           h->scratch, h->attn_scratch, st);
+  }
   return attention(h->q, h->att, kv, h->seq_dev, h->tok_seq_dev, tr ? h->tree_limit_dev : nullptr,
                    tr ? h->tree_mask_dev : nullptr, T, max_keys, ap, h->scratch, h->attn_scratch, st);
 }
@@ -1011,6 +1037,14 @@ int forward_chunk(sfc_stage *h, const std::vector<SeqReq> &seqs, const uint32_t 
   }
   SFC_CUDA(cudaMemcpyAsync(h->seq_dev, si, seqs.size() * sizeof(SeqInfo), cudaMemcpyHostToDevice, st));
   SFC_CUDA(cudaMemcpyAsync(h->tok_seq_dev, ts, size_t(T) * 4, cudaMemcpyHostToDevice, st));
+  h->fa_ntiles = 0;
+  if (h->fa_ok && T > 1) {  // query tiles for the tensor-core attention (after ids in the staging buffer)
+    FaTileRef *ft = reinterpret_cast<FaTileRef *>(ts + 2 * T);
+    for (size_t i = 0; i < seqs.size(); ++i)
+      for (int32_t t0 = 0; t0 < seqs[i].n; t0 += h->fa_tt) ft[h->fa_ntiles++] = FaTileRef{int32_t(i), t0};
+    SFC_CUDA(cudaMemcpyAsync(h->fa_tiles_dev, ft, size_t(h->fa_ntiles) * sizeof(FaTileRef), cudaMemcpyHostToDevice,
+                             st));
+  }
   if (h->is_head) {
     const uint32_t *idd = ids;
     if (!ids_on_device) {
