@@ -172,41 +172,49 @@ __global__ void __launch_bounds__(FA_THREADS, 1) flash_attention_kernel(const __
 
   // ---- Q tile into shared memory: row r = g*TT + i, q * 2^u split into fp16 hi + lo (K-major,
   // 128-byte swizzle, one 16 KB tile per 64-dim chunk); lane l holds dims 8l..8l+7
-  for (int r = warp; r < FA_M; r += FA_THREADS / 32) {
-    const int g = r / TT, i = r % TT;
-    const bool valid = tile.t0 + i < sq.n_tok;
-    const int64_t t = int64_t(sq.tok0) + tile.t0 + i;
-    float v[8];
-    const bool on = valid && lane * 8 < hd;
-    if (on) {
-      const float *src = a.q + t * int64_t(a.n_heads) * hd + int64_t(kvh * G + g) * hd + lane * 8;
-      const float4 f0 = *reinterpret_cast<const float4 *>(src), f1 = *reinterpret_cast<const float4 *>(src + 4);
-      v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-      v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
-    } else {
+  constexpr int QB = 4;  // rows per warp per pass: their loads are issued together
+  for (int r0 = warp * QB; r0 < FA_M; r0 += (FA_THREADS / 32) * QB) {
+    float v[QB][8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = 0.f;
-    }
-    float mx = 0.f;
+    for (int b = 0; b < QB; ++b) {
+      const int r = r0 + b, g = r / TT, i = r % TT;
+      const bool on = r < FA_M && tile.t0 + i < sq.n_tok && lane * 8 < hd;
+      if (on) {
+        const int64_t t = int64_t(sq.tok0) + tile.t0 + i;
+        const float *src = a.q + t * int64_t(a.n_heads) * hd + int64_t(kvh * G + g) * hd + lane * 8;
+        const float4 f0 = *reinterpret_cast<const float4 *>(src), f1 = *reinterpret_cast<const float4 *>(src + 4);
+        v[b][0] = f0.x; v[b][1] = f0.y; v[b][2] = f0.z; v[b][3] = f0.w;
+        v[b][4] = f1.x; v[b][5] = f1.y; v[b][6] = f1.z; v[b][7] = f1.w;
+      } else {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
-    mx = warp_max(mx);
-    int E = int((__float_as_uint(mx) >> 23) & 0xFF) - 126;  // mx < 2^E
-    if (E < -100) E = -100;
-    const float up = __uint_as_float(uint32_t(127 + 15 - E) << 23);  // |q * up| < 2^15
-    if (lane == 0) s_rowscale[r] = __uint_as_float(uint32_t(127 - 15 + E) << 23);
-    if (lane * 8 < hd) {
-      uint32_t hw[4], lw[4];
-#pragma unroll
-      for (int e2 = 0; e2 < 4; ++e2) {
-        const float x0 = v[2 * e2] * up, x1 = v[2 * e2 + 1] * up;
-        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-        hw[e2] = pack_half2(__half2float(h0), __half2float(h1));
-        lw[e2] = pack_half2(x0 - __half2float(h0), x1 - __half2float(h1));
+        for (int e = 0; e < 8; ++e) v[b][e] = 0.f;
       }
-      const uint32_t off = uint32_t((lane >> 3) * (FA_M * 128)) + sw128_off(r, lane & 7);
-      *reinterpret_cast<uint4 *>(sQ + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4 *>(sQ + FA_Q_BYTES + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+#pragma unroll
+    for (int b = 0; b < QB; ++b) {
+      const int r = r0 + b;
+      if (r >= FA_M) break;
+      float mx = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[b][e]));
+      mx = warp_max(mx);
+      int E = int((__float_as_uint(mx) >> 23) & 0xFF) - 126;  // mx < 2^E
+      if (E < -100) E = -100;
+      const float up = __uint_as_float(uint32_t(127 + 15 - E) << 23);  // |q * up| < 2^15
+      if (lane == 0) s_rowscale[r] = __uint_as_float(uint32_t(127 - 15 + E) << 23);
+      if (lane * 8 < hd) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const float x0 = v[b][2 * e2] * up, x1 = v[b][2 * e2 + 1] * up;
+          const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+          hw[e2] = pack_half2(__half2float(h0), __half2float(h1));
+          lw[e2] = pack_half2(x0 - __half2float(h0), x1 - __half2float(h1));
+        }
+        const uint32_t off = uint32_t((lane >> 3) * (FA_M * 128)) + sw128_off(r, lane & 7);
+        *reinterpret_cast<uint4 *>(sQ + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(sQ + FA_Q_BYTES + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
     }
   }
 
@@ -402,9 +410,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1) flash_attention_kernel(const __
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] = 0u;
       }
-      if (r_valid)
+      if (r_valid) {
+        if (a.n_split == 1) {  // output rows are 16-byte aligned (head_dim % 64 == 0)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) dst[c + e] = __uint_as_float(o[e]) * scale;
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4 *>(dst + c + e) =
+                make_float4(__uint_as_float(o[e]) * scale, __uint_as_float(o[e + 1]) * scale,
+                            __uint_as_float(o[e + 2]) * scale, __uint_as_float(o[e + 3]) * scale);
+        } else {  // partial rows of hd + 2 floats: 8-byte aligned
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            *reinterpret_cast<float2 *>(dst + c + e) = make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1]));
+        }
+      }
     }
   }
   __syncwarp();  // single-lane roles: lanes wait for their lane 0 before the block barrier
