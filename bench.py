@@ -521,13 +521,14 @@ def run_pipeline(args):
 
 
 # ---------------------------------------------------------------- fixed workloads for profilers
-def case_decode(steps: int, ctx: int, batch: int):
+def case_decode(steps: int, ctx: int, batch: int, layers: int = N_LAYERS):
     """`steps` eager decode steps of `batch` sequences after `ctx` seeded cached positions, through
-    the device-pointer stage calls (no CUDA graph, so every kernel is its own launch)."""
+    the device-pointer stage calls (no CUDA graph, so every kernel is its own launch); `layers` of
+    the model (fewer keep a profiler's capture small)."""
     import torch
     import stagefwd as sf
     dev = torch.device("cuda")
-    shape = sf.ModelShape()
+    shape = sf.ModelShape(n_layers=layers)
     be = sf.CudaStageBackend(synthetic=shape, rope_theta=10000.0, max_ctx=max(ctx + steps + 8, 64),
                              max_sessions=batch + 2, max_batch_tokens=max(batch, 8)).load_layout(
         "synthetic-gemma", "full", 0, shape.n_layers - 1, True, True)
@@ -602,6 +603,7 @@ def main():
                     help="run a fixed workload for a profiler instead of the benchmark")
     ap.add_argument("--ctx", type=int, default=512, help="--case decode: cached positions per sequence")
     ap.add_argument("--batch", type=int, default=1, help="--case decode: sequences per step")
+    ap.add_argument("--layers", type=int, default=N_LAYERS, help="--case decode: model layers")
     ap.add_argument("--tokens", type=int, default=64, help="--case gemm / prefill: tokens per launch / prompt")
     ap.add_argument("--launches", type=int, default=8, help="--case gemv/gemm: launches")
     args = ap.parse_args()
@@ -609,7 +611,7 @@ def main():
         import torch
         torch.cuda.set_device(0)
         if args.case == "decode":
-            case_decode(args.steps, args.ctx, args.batch)
+            case_decode(args.steps, args.ctx, args.batch, args.layers)
         elif args.case == "prefill":
             case_prefill(args.steps, args.tokens)
         else:
