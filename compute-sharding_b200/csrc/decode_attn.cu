@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace sfc {
 
@@ -68,11 +69,44 @@ __device__ __forceinline__ void load_row8(const uint8_t *p, bool kv32, float (&v
   }
 }
 
-template <int G, bool KV32>
+// ---- warp-level tensor-core helpers (fp16 cache path)
+// Eight 8x8 fp16 matrices' rows: lane L gives the shared-memory address of row L%8 of matrix L/8.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// D (16x8 f32) += A (16x16 fp16, row) * B (16x8 fp16, col).  Fragments (lane = 4g + t): a0/a1 = rows
+// g / g+8, k 2t..2t+1; a2/a3 = the same rows, k 2t+8..; b0/b1 = column g, k 2t.. / 2t+8..; d0,d1 =
+// row g, columns 2t, 2t+1; d2,d3 = row g+8.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Byte offset of (key, dim) (dim a multiple of 8) in a 32-key tile laid out by the cache's tensor
+// map: [64-dim chunk][key][64 dims], 16-byte pieces of a 128-byte row XOR-swizzled by key % 8.
+__device__ __forceinline__ uint32_t kv_tile_off(int key, int dim) {
+  return uint32_t((dim >> 6) * (32 * 128) + key * 128 + ((((dim & 63) >> 3) ^ (key & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+template <int G, bool KV32, bool TC>
 __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
     const float *__restrict__ qr, const float *__restrict__ kr, const float *__restrict__ vr, int q_ld, int kv_ld,
     float *__restrict__ out, KVLayer kv, const SeqInfo *__restrict__ seqs, AttnParams p, int n_split, int min_chunk,
-    float *__restrict__ part, unsigned *__restrict__ counters, unsigned *err) {
+    float *__restrict__ part, unsigned *__restrict__ counters, unsigned *err, const __grid_constant__ CUtensorMap kv_map,
+    int64_t kv_row0, int64_t slot_rows) {
   constexpr int ESZ = KV32 ? 4 : 2;
   constexpr int TK = DA_TILE_BYTES / (DA_MAX_HD * ESZ);  // keys per tile
   constexpr int KPW = TK / DA_WARPS;                      // keys per warp per tile
@@ -108,11 +142,21 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   const uint8_t *kbase = reinterpret_cast<const uint8_t *>(kv.base) + size_t(sq.slot) * kv.slot_stride * ESZ;
   const uint8_t *vbase = kbase + size_t(kv.slot_stride / 2) * ESZ;
   const size_t head_off = size_t(kvh) * p.max_ctx * row_bytes;
-  uint8_t *tiles = smem;  // [DA_STAGES][K tile | V tile]
+  // [DA_STAGES][K tile | V tile]; the tensor-copy layout (TC) needs 1024-byte alignment
+  uint8_t *tiles = TC ? smem + ((1024 - (smem_u32(smem) & 1023)) & 1023) : smem;
+  // TC: first cache rows of this (slot, kv head)'s keys and values in the arena's tensor map
+  const int64_t krow0 = kv_row0 + int64_t(sq.slot) * slot_rows + int64_t(kvh) * p.max_ctx;
+  const int64_t vrow0 = krow0 + int64_t(p.n_kv) * p.max_ctx;
 
   auto issue = [&](int i) {
     const int st = i % DA_STAGES;
     const int k0 = k_begin + i * TK;
+    if (TC) {  // whole 32-key boxes (rows past the sequence are finite: the arena starts zeroed)
+      mbar_arrive_expect_tx(&bars[st], uint32_t(2 * TK * row_bytes));
+      tma_load_3d(tiles + st * 2 * DA_TILE_BYTES, &kv_map, 0, int(krow0 + k0), 0, &bars[st]);
+      tma_load_3d(tiles + st * 2 * DA_TILE_BYTES + DA_TILE_BYTES, &kv_map, 0, int(vrow0 + k0), 0, &bars[st]);
+      return;
+    }
     const int nk = min(TK, k_old_end - k0);
     const uint32_t bytes = uint32_t(nk * row_bytes);
     mbar_arrive_expect_tx(&bars[st], 2 * bytes);
@@ -197,126 +241,311 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   }
   __syncthreads();
 
-  // ---- keys: lane l holds dims 8l..8l+7
-  const bool lane_on = lane * 8 < hd;
-  float qv[G][8];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qv[g][e] = lane_on ? s_vec[g][lane * 8 + e] : 0.f;
-  float m[G], l[G], acc[G][8];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
-  }
-  // one online-softmax update with KN keys (rows kf/vf; key k counts when bit k of `valid` is set)
-  auto update = [&](auto kn_tag, const float (*kf)[8], const float (*vf)[8], unsigned valid) {
-    constexpr int KN = decltype(kn_tag)::value;
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s[KN];
-      float mx = m[g];
-#pragma unroll
-      for (int k = 0; k < KN; ++k) {
-        float d = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d += qv[g][e] * kf[k][e];
-        d = warp_sum(d);
-        s[k] = (valid >> k) & 1u ? d : -INFINITY;
-        mx = fmaxf(mx, s[k]);
-      }
-      if (mx == -INFINITY) continue;  // no valid key yet
-      const float alpha = expf(m[g] - mx);  // exp(-inf) = 0 on the first keys
-      float psum = 0.f;
-      float pk[KN];
-#pragma unroll
-      for (int k = 0; k < KN; ++k) {
-        pk[k] = (valid >> k) & 1u ? expf(s[k] - mx) : 0.f;
-        psum += pk[k];
-      }
-      l[g] = l[g] * alpha + psum;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float a = acc[g][e] * alpha;
-#pragma unroll
-        for (int k = 0; k < KN; ++k) a += pk[k] * vf[k][e];
-        acc[g][e] = a;
-      }
-      m[g] = mx;
-    }
-  };
-
-  for (int i = 0; i < n_tiles; ++i) {
-    const int st = i % DA_STAGES;
-    mbar_wait_bounded(&bars[st], (i / DA_STAGES) & 1, err);
-    const int k0 = k_begin + i * TK;
-    const int nk = min(TK, k_old_end - k0);
-    const uint8_t *kt = tiles + st * 2 * DA_TILE_BYTES, *vt = kt + DA_TILE_BYTES;
-    float kf[KPW][8], vf[KPW][8];
-    unsigned valid = 0;
-#pragma unroll
-    for (int k = 0; k < KPW; ++k) {
-      const int kk = warp * KPW + k;
-      if (kk < nk) valid |= 1u << k;
-      if (kk < nk && lane_on) {
-        load_row8(kt + kk * row_bytes + lane * 8 * ESZ, KV32, kf[k]);
-        load_row8(vt + kk * row_bytes + lane * 8 * ESZ, KV32, vf[k]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) kf[k][e] = vf[k][e] = 0.f;
-      }
-    }
-    update(KeyCount<KPW>{}, kf, vf, valid);
-    __syncthreads();  // every warp is done with this stage
-    if (tid == 0 && i + DA_STAGES < n_tiles) issue(i + DA_STAGES);
-  }
-  if (owner && warp == 0) {  // the new key, from this CTA's own copy
-    float kf[1][8], vf[1][8];
-    const unsigned valid = 1u;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      kf[0][e] = lane_on ? s_vec[G][lane * 8 + e] : 0.f;
-      vf[0][e] = lane_on ? s_vec[G + 1][lane * 8 + e] : 0.f;
-    }
-    update(KeyCount<1>{}, kf, vf, valid);
-  }
-
-  // ---- merge the warps in a fixed order (tiles are free: every issued copy has been waited on)
-  if (lane == 0)
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      s_m[warp][g] = m[g];
-      s_l[warp][g] = l[g];
-    }
-  __syncthreads();
-  float *s_tmp = reinterpret_cast<float *>(tiles);  // [DA_WARPS][DA_MAX_HD]
-  float *s_acc = s_tmp + DA_WARPS * DA_MAX_HD;      // [DA_MAXG][DA_MAX_HD]
+  float *s_acc = reinterpret_cast<float *>(tiles) + DA_WARPS * DA_MAX_HD;  // [DA_MAXG][DA_MAX_HD] after the keys
   float M[G], L[G];
+  if constexpr (TC) {
+    // ---- fp16 cache on the tensor pipe (mma.sync m16n8k16, fp32 accumulate), per 32-key tile:
+    //  S^T = K Qc^T   warp 0: A = the key tile (16 keys x 16 dims per MMA, ldmatrix), B = the q
+    //                 columns in registers: column 2h = hi, 2h+1 = lo of q_h * 2^u_h (fp16 keys exact,
+    //                 q to ~22 bits), so lane (g, t) holds head t's scores at keys g, g+8, 16+g, 24+g
+    //  softmax        warp 0: tile maximum and sums by shuffles, p as fp16 hi + lo into P^T (shared)
+    //  O^T += V^T P^T every warp for its 32 dims: A = values transposed by ldmatrix, B = P^T;
+    //                 O stays in fragments (column 2h + 2h+1 = head h), rescaled when the maximum moves
+    const bool lane_on = lane * 8 < hd;
+    __shared__ uint32_t s_pt[8][TK / 2];  // P^T as fp16 pairs [column][key pair]
+    __shared__ float s_alpha[DA_MAXG], s_pnew[DA_MAXG], s_hm[DA_MAXG], s_hl[DA_MAXG];
+    const int g8 = lane >> 2, t4 = lane & 3;
+    for (int i = tid; i < 8 * (TK / 2); i += DA_THREADS) (&s_pt[0][0])[i] = 0u;
+    uint32_t qb[DA_MAX_HD / 16][2];
+    float rs = 1.f, m_run = -INFINITY, l_run = 0.f;  // warp 0: of head t4
+    if (warp == 0) {
+      float up[G];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float mm = -INFINITY;
-    for (int w = 0; w < DA_WARPS; ++w) mm = fmaxf(mm, s_m[w][g]);
-    float ll = 0.f;
-    for (int w = 0; w < DA_WARPS; ++w) ll += s_m[w][g] == -INFINITY ? 0.f : s_l[w][g] * expf(s_m[w][g] - mm);
-    M[g] = mm;
-    L[g] = ll;
-  }
+      for (int h = 0; h < G; ++h) {
+        float mx = 0.f;
+        if (lane_on)
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float scw = m[g] == -INFINITY ? 0.f : expf(m[g] - M[g]);
-    if (lane_on)
+          for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(s_vec[h][lane * 8 + e]));
+        mx = warp_max(mx);
+        int E = int((__float_as_uint(mx) >> 23) & 0xFF) - 126;  // mx < 2^E
+        if (E < -100) E = -100;
+        up[h] = __uint_as_float(uint32_t(127 + 15 - E) << 23);  // |q * up| < 2^15
+        if (t4 == h) rs = __uint_as_float(uint32_t(127 - 15 + E) << 23);
+      }
+      const int hh = g8 >> 1, part_lo = g8 & 1;  // this lane's B column: head hh, hi or lo
+      const float uph = hh < G ? lt_of(up, hh < G ? hh : 0) : 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s_tmp[warp * DA_MAX_HD + lane * 8 + e] = acc[g][e] * scw;
-    __syncthreads();
-    if (tid < hd) {
-      float a = 0.f;
-      for (int w = 0; w < DA_WARPS; ++w) a += s_tmp[w * DA_MAX_HD + tid];
-      s_acc[g * DA_MAX_HD + tid] = a;
+      for (int ks = 0; ks < DA_MAX_HD / 16; ++ks) {
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (hh < G && 16 * ks < hd) {
+          const float *qv = s_vec[hh] + 16 * ks + 2 * t4;
+          x[0] = qv[0] * uph;
+          x[1] = qv[1] * uph;
+          x[2] = qv[8] * uph;
+          x[3] = qv[9] * uph;
+          if (part_lo)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] -= __half2float(__float2half_rn(x[e]));
+        }
+        qb[ks][0] = pack_h2(x[0], x[1]);
+        qb[ks][1] = pack_h2(x[2], x[3]);
+      }
     }
+    float o[2][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    const int d0w = 32 * warp;  // this warp's dims for O
+    const bool pv = d0w < hd;
+    __syncthreads();  // P^T zeroed
+    for (int i = 0; i < n_tiles; ++i) {
+      const int st = i % DA_STAGES;
+      mbar_wait_bounded(&bars[st], (i / DA_STAGES) & 1, err);
+      const uint32_t kt = smem_u32(tiles + st * 2 * DA_TILE_BYTES), vt = kt + DA_TILE_BYTES;
+      const int nk = min(TK, k_old_end - (k_begin + i * TK));
+      if (warp == 0) {
+        float sc[2][4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+          const int key = 16 * mt + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+          for (int ks = 0; ks < DA_MAX_HD / 16; ++ks) {
+            if (16 * ks >= hd) break;
+            uint32_t a[4];
+            ldsm_x4(kt + kv_tile_off(key, 16 * ks + (lane >> 4) * 8), a);
+            mma_f16_16816(sc[mt], a, qb[ks][0], qb[ks][1]);
+          }
+        }
+        float s4[4] = {(sc[0][0] + sc[0][1]) * rs, (sc[0][2] + sc[0][3]) * rs, (sc[1][0] + sc[1][1]) * rs,
+                       (sc[1][2] + sc[1][3]) * rs};
+        const int key4[4] = {g8, g8 + 8, 16 + g8, 24 + g8};
+        float mt_ = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (key4[j] >= nk) s4[j] = -INFINITY;
+          mt_ = fmaxf(mt_, s4[j]);
+        }
+#pragma unroll
+        for (int sh = 4; sh < 32; sh <<= 1) mt_ = fmaxf(mt_, __shfl_xor_sync(0xFFFFFFFFu, mt_, sh));
+        const float m_new = fmaxf(m_run, mt_);
+        const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+        float p4[4], psum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          p4[j] = s4[j] == -INFINITY ? 0.f : expf(s4[j] - m_new);
+          psum += p4[j];
+        }
+#pragma unroll
+        for (int sh = 4; sh < 32; sh <<= 1) psum += __shfl_xor_sync(0xFFFFFFFFu, psum, sh);
+        l_run = l_run * alpha + psum;
+        m_run = m_new;
+        if (t4 < G) {
+          __half *ph = reinterpret_cast<__half *>(&s_pt[2 * t4][0]), *pl = reinterpret_cast<__half *>(&s_pt[2 * t4 + 1][0]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __half h = __float2half_rn(p4[j]);
+            ph[key4[j]] = h;
+            pl[key4[j]] = __float2half_rn(p4[j] - __half2float(h));
+          }
+          if (g8 == 0) s_alpha[t4] = alpha;
+        }
+      }
+      __syncthreads();  // P^T and the rescale factors of this tile
+      if (pv) {
+        const float a_t = t4 < G ? s_alpha[t4] : 1.f;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[mt][e] *= a_t;
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          const uint32_t b0 = s_pt[g8][8 * kk + t4], b1 = s_pt[g8][8 * kk + 4 + t4];
+          const int key = 16 * kk + (lane & 7) + (lane >> 4) * 8;
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            uint32_t a[4];
+            ldsm_x4_t(vt + kv_tile_off(key, d0w + 16 * mt + ((lane >> 3) & 1) * 8), a);
+            mma_f16_16816(o[mt], a, b0, b1);
+          }
+        }
+      }
+      __syncthreads();  // every warp is done with this stage and with P^T
+      if (tid == 0 && i + DA_STAGES < n_tiles) issue(i + DA_STAGES);
+    }
+    if (owner) {  // the new key and value, from this CTA's own (fp16-rounded) copy
+      if (warp == 0) {
+        float snew[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float d = 0.f;
+          if (lane_on)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d += s_vec[h][lane * 8 + e] * s_vec[G][lane * 8 + e];
+          snew[h] = warp_sum(d);
+        }
+        if (t4 < G) {
+          const float sn = lt_of(snew, t4 < G ? t4 : 0);
+          const float m_new = fmaxf(m_run, sn);
+          const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+          const float pn = expf(sn - m_new);
+          l_run = l_run * alpha + pn;
+          m_run = m_new;
+          if (g8 == 0) {
+            s_alpha[t4] = alpha;
+            s_pnew[t4] = pn;
+          }
+        }
+      }
+      __syncthreads();
+      if (pv && t4 < G) {
+        const float a_t = s_alpha[t4], pn = s_pnew[t4];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          const int d = d0w + 16 * mt + g8;
+          o[mt][0] = o[mt][0] * a_t + pn * s_vec[G + 1][d];
+          o[mt][1] *= a_t;
+          o[mt][2] = o[mt][2] * a_t + pn * s_vec[G + 1][d + 8];
+          o[mt][3] *= a_t;
+        }
+      }
+    }
+    if (warp == 0 && g8 == 0 && t4 < G) {
+      s_hm[t4] = m_run;
+      s_hl[t4] = l_run;
+    }
+    if (pv && t4 < G)  // every issued copy has been waited on: the tile area is free
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const int d = d0w + 16 * mt + g8;
+        s_acc[t4 * DA_MAX_HD + d] = o[mt][0] + o[mt][1];
+        s_acc[t4 * DA_MAX_HD + d + 8] = o[mt][2] + o[mt][3];
+      }
     __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      M[g] = s_hm[g];
+      L[g] = s_hl[g];
+    }
+  } else {
+    // ---- keys: lane l holds dims 8l..8l+7
+    const bool lane_on = lane * 8 < hd;
+    float qv[G][8];
+  #pragma unroll
+    for (int g = 0; g < G; ++g)
+  #pragma unroll
+      for (int e = 0; e < 8; ++e) qv[g][e] = lane_on ? s_vec[g][lane * 8 + e] : 0.f;
+    float m[G], l[G], acc[G][8];
+  #pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m[g] = -INFINITY;
+      l[g] = 0.f;
+  #pragma unroll
+      for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
+    }
+    // one online-softmax update with KN keys (rows kf/vf; key k counts when bit k of `valid` is set)
+    auto update = [&](auto kn_tag, const float (*kf)[8], const float (*vf)[8], unsigned valid) {
+      constexpr int KN = decltype(kn_tag)::value;
+  #pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float s[KN];
+        float mx = m[g];
+  #pragma unroll
+        for (int k = 0; k < KN; ++k) {
+          float d = 0.f;
+  #pragma unroll
+          for (int e = 0; e < 8; ++e) d += qv[g][e] * kf[k][e];
+          d = warp_sum(d);
+          s[k] = (valid >> k) & 1u ? d : -INFINITY;
+          mx = fmaxf(mx, s[k]);
+        }
+        if (mx == -INFINITY) continue;  // no valid key yet
+        const float alpha = expf(m[g] - mx);  // exp(-inf) = 0 on the first keys
+        float psum = 0.f;
+        float pk[KN];
+  #pragma unroll
+        for (int k = 0; k < KN; ++k) {
+          pk[k] = (valid >> k) & 1u ? expf(s[k] - mx) : 0.f;
+          psum += pk[k];
+        }
+        l[g] = l[g] * alpha + psum;
+  #pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float a = acc[g][e] * alpha;
+  #pragma unroll
+          for (int k = 0; k < KN; ++k) a += pk[k] * vf[k][e];
+          acc[g][e] = a;
+        }
+        m[g] = mx;
+      }
+    };
+
+    for (int i = 0; i < n_tiles; ++i) {
+      const int st = i % DA_STAGES;
+      mbar_wait_bounded(&bars[st], (i / DA_STAGES) & 1, err);
+      const int k0 = k_begin + i * TK;
+      const int nk = min(TK, k_old_end - k0);
+      const uint8_t *kt = tiles + st * 2 * DA_TILE_BYTES, *vt = kt + DA_TILE_BYTES;
+      float kf[KPW][8], vf[KPW][8];
+      unsigned valid = 0;
+  #pragma unroll
+      for (int k = 0; k < KPW; ++k) {
+        const int kk = warp * KPW + k;
+        if (kk < nk) valid |= 1u << k;
+        if (kk < nk && lane_on) {
+          load_row8(kt + kk * row_bytes + lane * 8 * ESZ, KV32, kf[k]);
+          load_row8(vt + kk * row_bytes + lane * 8 * ESZ, KV32, vf[k]);
+        } else {
+  #pragma unroll
+          for (int e = 0; e < 8; ++e) kf[k][e] = vf[k][e] = 0.f;
+        }
+      }
+      update(KeyCount<KPW>{}, kf, vf, valid);
+      __syncthreads();  // every warp is done with this stage
+      if (tid == 0 && i + DA_STAGES < n_tiles) issue(i + DA_STAGES);
+    }
+    if (owner && warp == 0) {  // the new key, from this CTA's own copy
+      float kf[1][8], vf[1][8];
+      const unsigned valid = 1u;
+  #pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        kf[0][e] = lane_on ? s_vec[G][lane * 8 + e] : 0.f;
+        vf[0][e] = lane_on ? s_vec[G + 1][lane * 8 + e] : 0.f;
+      }
+      update(KeyCount<1>{}, kf, vf, valid);
+    }
+
+    // ---- merge the warps in a fixed order (tiles are free: every issued copy has been waited on)
+    if (lane == 0)
+  #pragma unroll
+      for (int g = 0; g < G; ++g) {
+        s_m[warp][g] = m[g];
+        s_l[warp][g] = l[g];
+      }
+    __syncthreads();
+    float *s_tmp = reinterpret_cast<float *>(tiles);  // [DA_WARPS][DA_MAX_HD]
+  #pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mm = -INFINITY;
+      for (int w = 0; w < DA_WARPS; ++w) mm = fmaxf(mm, s_m[w][g]);
+      float ll = 0.f;
+      for (int w = 0; w < DA_WARPS; ++w) ll += s_m[w][g] == -INFINITY ? 0.f : s_l[w][g] * expf(s_m[w][g] - mm);
+      M[g] = mm;
+      L[g] = ll;
+    }
+  #pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float scw = m[g] == -INFINITY ? 0.f : expf(m[g] - M[g]);
+      if (lane_on)
+  #pragma unroll
+        for (int e = 0; e < 8; ++e) s_tmp[warp * DA_MAX_HD + lane * 8 + e] = acc[g][e] * scw;
+      __syncthreads();
+      if (tid < hd) {
+        float a = 0.f;
+        for (int w = 0; w < DA_WARPS; ++w) a += s_tmp[w * DA_MAX_HD + tid];
+        s_acc[g * DA_MAX_HD + tid] = a;
+      }
+      __syncthreads();
+    }
   }
   if (n_eff == 1) {
     for (int idx = tid; idx < G * hd; idx += DA_THREADS) {
@@ -421,27 +650,42 @@ bool decode_attention_supported(const AttnParams &p) {
 cudaError_t decode_attention(const float *q, const float *k, const float *v, int q_ld, int kv_ld, float *out,
                              KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, int64_t sum_keys,
                              const AttnParams &p, void *scratch, size_t scratch_bytes, unsigned *counters,
-                             cudaStream_t st) {
+                             cudaStream_t st, void *kv_arena, int64_t arena_rows) {
   if (n_seq <= 0) return cudaSuccess;
   if (!decode_attention_supported(p) || !counters) return cudaErrorInvalidValue;
   int ns = 1, min_chunk = DA_MIN_CHUNK;
   decode_attention_plan(n_seq, p, max_keys, sum_keys, &ns, &min_chunk);
   if (scratch_bytes < decode_attention_scratch_bytes(n_seq, p, max_keys)) return cudaErrorInvalidValue;
-  const size_t smem = size_t(DA_STAGES) * 2 * DA_TILE_BYTES;
+  // fp16 cache with whole 64-dim chunks: keys and values by tensor copies, products on the tensor pipe
+  CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  const bool tc = !p.kv_f32 && p.head_dim % 64 == 0 && kv_tensor_map(kv_arena, arena_rows, p.head_dim, &map);
+  const int64_t row0 = tc ? (static_cast<char *>(kv.base) - static_cast<char *>(kv_arena)) / 2 / p.head_dim : 0;
+  const int64_t slot_rows = 2 * int64_t(p.n_kv) * p.max_ctx;
+  const size_t smem = size_t(DA_STAGES) * 2 * DA_TILE_BYTES + (tc ? 1024 : 0);
   const dim3 grid(unsigned(n_seq), unsigned(p.n_kv), unsigned(ns));
   const int G = p.n_heads / p.n_kv;
   void (*kern)(const float *, const float *, const float *, int, int, float *, KVLayer, const SeqInfo *, AttnParams,
-               int, int, float *, unsigned *, unsigned *) = nullptr;
+               int, int, float *, unsigned *, unsigned *, const CUtensorMap, int64_t, int64_t) = nullptr;
   switch (G) {
-    case 1: kern = p.kv_f32 ? decode_attention_kernel<1, true> : decode_attention_kernel<1, false>; break;
-    case 2: kern = p.kv_f32 ? decode_attention_kernel<2, true> : decode_attention_kernel<2, false>; break;
-    case 4: kern = p.kv_f32 ? decode_attention_kernel<4, true> : decode_attention_kernel<4, false>; break;
+    case 1:
+      kern = tc ? decode_attention_kernel<1, false, true>
+                : p.kv_f32 ? decode_attention_kernel<1, true, false> : decode_attention_kernel<1, false, false>;
+      break;
+    case 2:
+      kern = tc ? decode_attention_kernel<2, false, true>
+                : p.kv_f32 ? decode_attention_kernel<2, true, false> : decode_attention_kernel<2, false, false>;
+      break;
+    case 4:
+      kern = tc ? decode_attention_kernel<4, false, true>
+                : p.kv_f32 ? decode_attention_kernel<4, true, false> : decode_attention_kernel<4, false, false>;
+      break;
     default: return cudaErrorInvalidValue;
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, grid, dim3(DA_THREADS), smem, st, q, k, v, q_ld, kv_ld, out, kv, seqs, p, ns, min_chunk,
-                    static_cast<float *>(scratch), counters, device_error_ptr());
+                    static_cast<float *>(scratch), counters, device_error_ptr(), map, row0, slot_rows);
 }
 
 }  // namespace sfc

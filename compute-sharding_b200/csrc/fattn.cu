@@ -72,15 +72,6 @@ struct FaArgs {
 };
 
 // ---------------------------------------------------------------- device helpers
-// One box of a 3-D tensor map into shared memory (no multicast).
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -481,6 +472,11 @@ bool flash_attention_supported(const AttnParams &p) {
 }
 
 int flash_attention_tile_tokens(const AttnParams &p) { return FA_M / (p.n_heads / p.n_kv); }
+
+bool kv_tensor_map(void *kv_arena, int64_t arena_rows, int head_dim, CUtensorMap *out) {
+  return kv_arena && arena_rows > 0 && arena_rows < (int64_t(1) << 30) && head_dim % 64 == 0 &&
+         head_dim <= FA_MAX_HD && kv_map_cached(kv_arena, arena_rows, head_dim, out);
+}
 
 bool flash_attention_prepare(void *kv_arena, int64_t arena_rows, int head_dim) {
   CUtensorMap m;

@@ -1,6 +1,7 @@
 // kernels.h — host-side launchers for the sm_100a stage-forward kernels (internal API).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -187,7 +188,7 @@ size_t decode_attention_scratch_bytes(int64_t n_seq, const AttnParams &p, int64_
 cudaError_t decode_attention(const float *q, const float *k, const float *v, int q_ld, int kv_ld, float *out,
                              KVLayer kv, const SeqInfo *seqs, int64_t n_seq, int64_t max_keys, int64_t sum_keys,
                              const AttnParams &p, void *scratch, size_t scratch_bytes, unsigned *counters,
-                             cudaStream_t st);
+                             cudaStream_t st, void *kv_arena = nullptr, int64_t arena_rows = 0);
 // causal GQA attention over the cache (real_math.rs:2697-2744); tree masks via parent links.
 size_t attention_scratch_bytes(int64_t n_tok, const AttnParams &p, int64_t max_keys);
 // tok_limit (nullable): per-token number of visible cache positions (default pos+1);
@@ -209,6 +210,9 @@ struct FaTileRef {
 };
 bool flash_attention_supported(const AttnParams &p);
 int flash_attention_tile_tokens(const AttnParams &p);
+// The cache's tensor map for 32-key tiles ([64-dim chunk][row][64 dims], 128-byte swizzle; built once
+// per arena and cached); false when the arena cannot be described.
+bool kv_tensor_map(void *kv_arena, int64_t arena_rows, int head_dim, CUtensorMap *out);
 // Builds (and caches) the cache's tensor map; false when the arena cannot be described.
 bool flash_attention_prepare(void *kv_arena, int64_t arena_rows, int head_dim);
 size_t flash_attention_scratch_bytes(int64_t n_tok, const AttnParams &p);

@@ -200,8 +200,10 @@ __global__ void logits_reduce_kernel(const float *__restrict__ part, int n_cta, 
 }
 
 // Softcap and argmax of precomputed raw scores [n][vocab] (the tensor-core path of the logits for
-// many rows): one CTA per row, thread j scans a contiguous vocabulary segment in index order with
-// strict '>', segments merge keeping the lowest index on ties; capped scores are written back.
+// many rows): one CTA per row; thread j scans indices j, j + 1024, ... (four at a time when the row
+// is 16-byte aligned) so each warp load is one contiguous piece of the row; every thread meets its
+// indices in increasing order with strict '>', and the merge keeps the lowest index on ties, so the
+// result is the lowest index of the maximum; capped scores are written back.
 constexpr int ARGMAX_THREADS = 1024;
 
 __global__ void __launch_bounds__(ARGMAX_THREADS) scores_argmax_kernel(float *__restrict__ scores, int64_t vocab,
@@ -212,16 +214,33 @@ __global__ void __launch_bounds__(ARGMAX_THREADS) scores_argmax_kernel(float *__
   pdl_wait();
   pdl_launch_dependents();
   float *row = scores + int64_t(blockIdx.x) * vocab;
-  const int64_t seg = (vocab + ARGMAX_THREADS - 1) / ARGMAX_THREADS;
-  const int64_t lo = int64_t(threadIdx.x) * seg, hi = lo + seg < vocab ? lo + seg : vocab;
   float b = -INFINITY;
   int64_t bi = INT64_MAX;
-  for (int64_t i = lo; i < hi; ++i) {
-    const float v = softcap_score(row[i], cap);
-    row[i] = v;
-    if (v > b) {
-      b = v;
-      bi = i;
+  if (vocab % 4 == 0) {
+    float4 *row4 = reinterpret_cast<float4 *>(row);
+    for (int64_t j = threadIdx.x; j < vocab / 4; j += ARGMAX_THREADS) {
+      float4 v = row4[j];
+      v.x = softcap_score(v.x, cap);
+      v.y = softcap_score(v.y, cap);
+      v.z = softcap_score(v.z, cap);
+      v.w = softcap_score(v.w, cap);
+      row4[j] = v;
+      const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (e[k] > b) {
+          b = e[k];
+          bi = 4 * j + k;
+        }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < vocab; i += ARGMAX_THREADS) {
+      const float v = softcap_score(row[i], cap);
+      row[i] = v;
+      if (v > b) {
+        b = v;
+        bi = i;
+      }
     }
   }
 #pragma unroll

@@ -794,7 +794,8 @@ cudaError_t layer_attention(sfc_stage *h, const AttnParams &ap, const KVLayer &k
                             bool decode, cudaStream_t st) {
   if (decode && !h->tree_active && decode_attention_supported(ap))
     return decode_attention(h->q, h->k, h->v, h->q_dim, h->k_dim, h->att, kv, h->seq_dev, T, max_keys,
-                            h->attn_sum_keys, ap, h->scratch, h->attn_scratch, h->attn_counters, st);
+                            h->attn_sum_keys, ap, h->scratch, h->attn_scratch, h->attn_counters, st, h->kv_arena,
+                            h->kv_rows);
   const bool tr = h->tree_active;
   cudaError_t e = qkv_post(h->q, h->k, h->v, h->q_dim, h->k_dim, kv, h->seq_dev, h->tok_seq_dev,
                            tr ? h->tree_rope_dev : nullptr, T, ap, st);
