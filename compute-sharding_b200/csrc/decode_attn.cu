@@ -35,7 +35,6 @@ constexpr int DA_MAXG = 4;  // query heads per kv head handled here (registers h
 constexpr int DA_MAX_HD = 256;
 constexpr int DA_MIN_CHUNK = 64;  // keys per split at least
 constexpr int DA_MAX_SPLIT = 32;  // key splits per (sequence, kv head) at most
-constexpr int DA_STAGES = 3;
 constexpr int DA_TILE_BYTES = 32 * DA_MAX_HD * 2;  // K or V of one tile: 32 fp16 keys (16 f32 keys)
 
 template <int N>
@@ -111,7 +110,8 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   constexpr int TK = DA_TILE_BYTES / (DA_MAX_HD * ESZ);  // keys per tile
   constexpr int KPW = TK / DA_WARPS;                      // keys per warp per tile
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bars[DA_STAGES];
+  constexpr int NST = TC ? 2 : 3;  // K/V ring stages
+  __shared__ uint64_t bars[NST];
   __shared__ float s_vec[DA_MAXG + 2][DA_MAX_HD];  // q heads, then the new k and v
   __shared__ float s_red[DA_MAXG + 2][DA_WARPS];
   __shared__ float s_m[DA_WARPS][DA_MAXG], s_l[DA_WARPS][DA_MAXG];
@@ -142,14 +142,14 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   const uint8_t *kbase = reinterpret_cast<const uint8_t *>(kv.base) + size_t(sq.slot) * kv.slot_stride * ESZ;
   const uint8_t *vbase = kbase + size_t(kv.slot_stride / 2) * ESZ;
   const size_t head_off = size_t(kvh) * p.max_ctx * row_bytes;
-  // [DA_STAGES][K tile | V tile]; the tensor-copy layout (TC) needs 1024-byte alignment
+  // [NST][K tile | V tile]; the tensor-copy layout (TC) needs 1024-byte alignment
   uint8_t *tiles = TC ? smem + ((1024 - (smem_u32(smem) & 1023)) & 1023) : smem;
   // TC: first cache rows of this (slot, kv head)'s keys and values in the arena's tensor map
   const int64_t krow0 = kv_row0 + int64_t(sq.slot) * slot_rows + int64_t(kvh) * p.max_ctx;
   const int64_t vrow0 = krow0 + int64_t(p.n_kv) * p.max_ctx;
 
   auto issue = [&](int i) {
-    const int st = i % DA_STAGES;
+    const int st = i % NST;
     const int k0 = k_begin + i * TK;
     if (TC) {  // whole 32-key boxes (rows past the sequence are finite: the arena starts zeroed)
       mbar_arrive_expect_tx(&bars[st], uint32_t(2 * TK * row_bytes));
@@ -165,10 +165,10 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
              &bars[st]);
   };
   if (tid == 0) {
-    for (int i = 0; i < DA_STAGES; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < NST; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
     // cached rows never depend on the previous kernel: request them before the dependency wait
-    for (int i = 0; i < n_tiles && i < DA_STAGES; ++i) issue(i);
+    for (int i = 0; i < n_tiles && i < NST; ++i) issue(i);
   }
   pdl_wait();
   pdl_launch_dependents();
@@ -298,8 +298,8 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
     const bool pv = d0w < hd;
     __syncthreads();  // P^T zeroed
     for (int i = 0; i < n_tiles; ++i) {
-      const int st = i % DA_STAGES;
-      mbar_wait_bounded(&bars[st], (i / DA_STAGES) & 1, err);
+      const int st = i % NST;
+      mbar_wait_bounded(&bars[st], (i / NST) & 1, err);
       const uint32_t kt = smem_u32(tiles + st * 2 * DA_TILE_BYTES), vt = kt + DA_TILE_BYTES;
       const int nk = min(TK, k_old_end - (k_begin + i * TK));
       if (warp == 0) {
@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
         }
       }
       __syncthreads();  // every warp is done with this stage and with P^T
-      if (tid == 0 && i + DA_STAGES < n_tiles) issue(i + DA_STAGES);
+      if (tid == 0 && i + NST < n_tiles) issue(i + NST);
     }
     if (owner) {  // the new key and value, from this CTA's own (fp16-rounded) copy
       if (warp == 0) {
@@ -480,8 +480,8 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
     };
 
     for (int i = 0; i < n_tiles; ++i) {
-      const int st = i % DA_STAGES;
-      mbar_wait_bounded(&bars[st], (i / DA_STAGES) & 1, err);
+      const int st = i % NST;
+      mbar_wait_bounded(&bars[st], (i / NST) & 1, err);
       const int k0 = k_begin + i * TK;
       const int nk = min(TK, k_old_end - k0);
       const uint8_t *kt = tiles + st * 2 * DA_TILE_BYTES, *vt = kt + DA_TILE_BYTES;
@@ -501,7 +501,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
       }
       update(KeyCount<KPW>{}, kf, vf, valid);
       __syncthreads();  // every warp is done with this stage
-      if (tid == 0 && i + DA_STAGES < n_tiles) issue(i + DA_STAGES);
+      if (tid == 0 && i + NST < n_tiles) issue(i + NST);
     }
     if (owner && warp == 0) {  // the new key, from this CTA's own copy
       float kf[1][8], vf[1][8];
@@ -662,7 +662,7 @@ cudaError_t decode_attention(const float *q, const float *k, const float *v, int
   const bool tc = !p.kv_f32 && p.head_dim % 64 == 0 && kv_tensor_map(kv_arena, arena_rows, p.head_dim, &map);
   const int64_t row0 = tc ? (static_cast<char *>(kv.base) - static_cast<char *>(kv_arena)) / 2 / p.head_dim : 0;
   const int64_t slot_rows = 2 * int64_t(p.n_kv) * p.max_ctx;
-  const size_t smem = size_t(DA_STAGES) * 2 * DA_TILE_BYTES + (tc ? 1024 : 0);
+  const size_t smem = size_t(tc ? 2 : 3) * 2 * DA_TILE_BYTES + (tc ? 1024 : 0);
   const dim3 grid(unsigned(n_seq), unsigned(p.n_kv), unsigned(ns));
   const int G = p.n_heads / p.n_kv;
   void (*kern)(const float *, const float *, const float *, int, int, float *, KVLayer, const SeqInfo *, AttnParams,
