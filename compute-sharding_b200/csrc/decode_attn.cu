@@ -303,19 +303,27 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
       const uint32_t kt = smem_u32(tiles + st * 2 * DA_TILE_BYTES), vt = kt + DA_TILE_BYTES;
       const int nk = min(TK, k_old_end - (k_begin + i * TK));
       if (warp == 0) {
-        float sc[2][4];
+        // two accumulators per 16-key group (even / odd k-steps): four independent MMA chains
+        float sc[2][4], sd[2][4];
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
-          const int key = 16 * mt + (lane & 7) + ((lane >> 3) & 1) * 8;
+        for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-          for (int ks = 0; ks < DA_MAX_HD / 16; ++ks) {
-            if (16 * ks >= hd) break;
+          for (int e = 0; e < 4; ++e) sc[mt][e] = sd[mt][e] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < DA_MAX_HD / 16; ++ks) {
+          if (16 * ks >= hd) break;
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            const int key = 16 * mt + (lane & 7) + ((lane >> 3) & 1) * 8;
             uint32_t a[4];
             ldsm_x4(kt + kv_tile_off(key, 16 * ks + (lane >> 4) * 8), a);
-            mma_f16_16816(sc[mt], a, qb[ks][0], qb[ks][1]);
+            mma_f16_16816((ks & 1) ? sd[mt] : sc[mt], a, qb[ks][0], qb[ks][1]);
           }
         }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[mt][e] += sd[mt][e];
         float s4[4] = {(sc[0][0] + sc[0][1]) * rs, (sc[0][2] + sc[0][3]) * rs, (sc[1][0] + sc[1][1]) * rs,
                        (sc[1][2] + sc[1][3]) * rs};
         const int key4[4] = {g8, g8 + 8, 16 + g8, 24 + g8};
