@@ -65,22 +65,32 @@ __global__ void __launch_bounds__(LOGIT_THREADS) logits_f16_kernel(const __half 
     float acc[T];
 #pragma unroll
     for (int t = 0; t < T; ++t) acc[t] = 0.f;
-    for (int c = 0; c < nchunk; ++c) {
-      const uint4 u = __ldcs(row + c * 32 + lane);  // streamed once: evict-first
-      const __half2 *hp = reinterpret_cast<const __half2 *>(&u);
-      float wf[8];
+    // eight 256-element chunks of the row per pass, their loads issued together (streamed once:
+    // evict-first); the sum runs over the chunks in order as before
+    for (int c0 = 0; c0 < nchunk; c0 += 8) {
+      uint4 u[8];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(hp[k]);
-        wf[2 * k] = f.x;
-        wf[2 * k + 1] = f.y;
-      }
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j < nchunk) u[j] = __ldcs(row + (c0 + j) * 32 + lane);
 #pragma unroll
-      for (int t = 0; t < T; ++t) {
-        const float4 x0 = *reinterpret_cast<const float4 *>(&hs[t * dim + c * 256 + lane * 8]);
-        const float4 x1 = *reinterpret_cast<const float4 *>(&hs[t * dim + c * 256 + lane * 8 + 4]);
-        acc[t] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w + wf[4] * x1.x + wf[5] * x1.y +
-                  wf[6] * x1.z + wf[7] * x1.w;
+      for (int j = 0; j < 8; ++j) {
+        if (c0 + j >= nchunk) break;
+        const int c = c0 + j;
+        const __half2 *hp = reinterpret_cast<const __half2 *>(&u[j]);
+        float wf[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(hp[k]);
+          wf[2 * k] = f.x;
+          wf[2 * k + 1] = f.y;
+        }
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float4 x0 = *reinterpret_cast<const float4 *>(&hs[t * dim + c * 256 + lane * 8]);
+          const float4 x1 = *reinterpret_cast<const float4 *>(&hs[t * dim + c * 256 + lane * 8 + 4]);
+          acc[t] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w + wf[4] * x1.x + wf[5] * x1.y +
+                    wf[6] * x1.z + wf[7] * x1.w;
+        }
       }
     }
 #pragma unroll
