@@ -131,4 +131,52 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------- residual-stream RMSNorm order
+// Every RMSNorm of the residual stream sums its squares in one order, whichever kernel computes
+// it (a GEMV or GEMM prologue, the residual add that closes a stage, the output norm): the row is
+// cut into 256-element blocks, lane l of a warp holds elements 8l..8l+7 of a block (zero past the
+// row's end) and sums their squares by fused multiply-add from zero in element order, the block
+// sum is the xor butterfly of warp_sum over the lanes, and the row total adds the block sums from
+// zero in block order.  The scale 1/sqrt(total/dim + eps) and everything computed from it are
+// then the same bits in every kernel, so a layer range split over several stages reproduces the
+// single-stage hidden states exactly.
+__device__ __forceinline__ float block_sumsq(const float (&v)[8]) {
+  float q = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) q = __fmaf_rn(v[e], v[e], q);
+  return warp_sum(q);
+}
+
+// The row total of that order computed by the NW warps of a block: warp w takes blocks w, w+NW, ..
+// and load8(b, v) fills the calling lane's 8 values of block b.  `red` holds 64 shared floats.
+// Every thread of the block must call it; all of them return the total.
+template <int NW, class Load8>
+__device__ __forceinline__ float row_sumsq(int nb, float *red, Load8 load8) {
+  const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
+  float tot = 0.f;
+  for (int c0 = 0; c0 < nb; c0 += 64) {
+    const int c1 = nb < c0 + 64 ? nb : c0 + 64;
+    for (int b = c0 + warp; b < c1; b += NW) {
+      float v[8];
+      load8(b, v);
+      const float s = block_sumsq(v);
+      if (lane == 0) red[b - c0] = s;
+    }
+    __syncthreads();
+    for (int b = c0; b < c1; ++b) tot = __fadd_rn(tot, red[b - c0]);
+    __syncthreads();
+  }
+  return tot;
+}
+
+// The residual add of a post-norm block: (a * s) * w + resid (w null: a + resid), then times the
+// layer scale when there is one, each operation rounded on its own (no contraction), in the order
+// of real_math.rs:30-47 followed by the residual add.
+__device__ __forceinline__ float resid_add(float a, float s, const float *w, float wv, float resid, const float *ls,
+                                           float lsv) {
+  float r = __fadd_rn(w ? __fmul_rn(__fmul_rn(a, s), wv) : a, resid);
+  if (ls) r = __fmul_rn(r, lsv);
+  return r;
+}
+
 }  // namespace sfc

@@ -619,11 +619,7 @@ __device__ __forceinline__ void build_x(const GemvPrologue &P, int nb, int cta, 
       load8(P.resid_in, off, rs);
       const float sc = P.scale ? P.scale[0] : 1.0f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float r = (P.w_post ? (v[e] * s1t) * wp[e] : v[e]) + rs[e];
-        if (P.scale) r = r * sc;
-        v[e] = r;
-      }
+      for (int e = 0; e < 8; ++e) v[e] = resid_add(v[e], s1t, P.w_post, wp[e], rs[e], P.scale, sc);
     }
     if (step == 1 || !P.w_next) return;
     const float s2t = (T == 1 || t == 0) ? s2[0] : s2[T - 1];
@@ -632,31 +628,24 @@ __device__ __forceinline__ void build_x(const GemvPrologue &P, int nb, int cta, 
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = (v[e] * s2t) * wn[e];
   };
-  // per-token sums over the CTA of sum(v^2) after `step` steps, in a fixed order
+  // per-token sums of v^2 after `step` steps in the residual-stream norm order (block_sumsq per
+  // unit, then the block sums in block order); the block sums pass through the start of X, which
+  // is written only after the norm passes
+  float *bsum = reinterpret_cast<float *>(X.frag);
   auto cta_sumsq = [&](int step, bool store_resid, float (&out)[T]) {
-    float part[T];
-#pragma unroll
-    for (int t = 0; t < T; ++t) part[t] = 0.f;
     for (int u = warp; u < units; u += CW) {
       const int t = u / nb, b = u % nb;
       float v[8];
       value8(t, b, step, v);
-      float q = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) q += v[e] * v[e];
-      if (T == 1 || t == 0) part[0] += q; else part[T - 1] += q;
+      const float s = block_sumsq(v);
+      if (lane == 0) bsum[u] = s;
       if (store_resid) store8(P.resid_out + int64_t(t) * K + b * QK_K + lane * 8, v);
-    }
-#pragma unroll
-    for (int t = 0; t < T; ++t) {
-      const float w = warp_sum(part[t]);
-      if (lane == 0) pro_red[t][warp] = w;
     }
     consumer_bar<CW>();
 #pragma unroll
     for (int t = 0; t < T; ++t) {
       float sum = 0.f;
-      for (int w = 0; w < CW; ++w) sum += pro_red[t][w];
+      for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, bsum[t * nb + b]);
       out[t] = sum;
     }
     consumer_bar<CW>();
@@ -679,27 +668,27 @@ __device__ __forceinline__ void build_x(const GemvPrologue &P, int nb, int cta, 
       }
       if (P.w_next) load8(P.w_next, col, wn);
     }
-    auto reduce = [&](float q, float (&out)[T]) {  // per-token CTA sum in a fixed order
+    // per-token CTA sum in the residual-stream norm order: warp = t * nb + b, so the warps of a
+    // token hold its block sums in block order (the other warps add zeros)
+    auto reduce = [&](const float (&vq)[8], float (&out)[T]) {
+      const float bs = block_sumsq(vq);
 #pragma unroll
       for (int tt = 0; tt < T; ++tt) {
-        const float w = warp_sum((T == 1 || tt == t) ? q : 0.f);
+        const float w = (T == 1 || tt == t) ? bs : 0.f;
         if (lane == 0) pro_red[tt][warp] = has ? w : 0.f;
       }
       consumer_bar<CW>();
 #pragma unroll
       for (int tt = 0; tt < T; ++tt) {
         float sum = 0.f;
-        for (int w = 0; w < CW; ++w) sum += pro_red[tt][w];
+        for (int w = 0; w < CW; ++w) sum = __fadd_rn(sum, pro_red[tt][w]);
         out[tt] = sum;
       }
       consumer_bar<CW>();
     };
     float tot[T];
     if (P.mode == 1 || P.w_post) {
-      float q = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) q += v[e] * v[e];
-      reduce(q, tot);
+      reduce(v, tot);
 #pragma unroll
       for (int tt = 0; tt < T; ++tt) s1[tt] = 1.0f / sqrtf(tot[tt] / float(K) + P.eps);
     }
@@ -710,17 +699,10 @@ __device__ __forceinline__ void build_x(const GemvPrologue &P, int nb, int cta, 
     } else {
       const float sc = P.scale ? P.scale[0] : 1.0f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float r = (P.w_post ? (v[e] * s1t) * wp[e] : v[e]) + rs[e];
-        if (P.scale) r = r * sc;
-        v[e] = r;
-      }
+      for (int e = 0; e < 8; ++e) v[e] = resid_add(v[e], s1t, P.w_post, wp[e], rs[e], P.scale, sc);
       if (P.w_next || (P.resid_out && cta == 0)) {
-        float q = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) q += v[e] * v[e];
         if (P.resid_out && cta == 0 && has) store8(P.resid_out + off, v);
-        reduce(q, tot);
+        reduce(v, tot);
 #pragma unroll
         for (int tt = 0; tt < T; ++tt) s2[tt] = 1.0f / sqrtf(tot[tt] / float(K) + P.eps);
       }

@@ -28,16 +28,22 @@ __device__ __forceinline__ float block_sum(float v, float *sh) {
 }
 
 // ---------------------------------------------------------------- rms norm
+// The lane's 8 values of 256-element block b of a row of `dim` floats (zero past the row's end).
+__device__ __forceinline__ void row_block8(const float *__restrict__ row, int dim, int b, float (&v)[8]) {
+  const int c = b * 256 + int(threadIdx.x & 31) * 8;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = c + e < dim ? row[c + e] : 0.f;
+}
+
+// out = (x * scale) * w per row, the sum of squares in the residual-stream norm order (row_sumsq).
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                                       int dim, float eps, float *__restrict__ out) {
-  __shared__ float sh[8];
+  __shared__ float red[64];
   pdl_wait();
   pdl_launch_dependents();
   const float *xr = x + int64_t(blockIdx.x) * dim;
   float *o = out + int64_t(blockIdx.x) * dim;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < dim; i += 256) ss += xr[i] * xr[i];
-  ss = block_sum<256>(ss, sh);
+  const float ss = row_sumsq<8>((dim + 255) / 256, red, [&](int b, float (&v)[8]) { row_block8(xr, dim, b, v); });
   const float scale = 1.0f / sqrtf(ss / float(dim) + eps);
   for (int i = threadIdx.x; i < dim; i += 256) o[i] = (xr[i] * scale) * w[i];
 }
@@ -48,42 +54,38 @@ cudaError_t rms_norm(const float *x, const float *w, int64_t n_tok, int dim, flo
 }
 
 // r = resid + (w_post ? rms_norm(a) * w_post : a); r *= layer_scale; resid = r;
-// if want_xn: xn = w_next ? rms_norm(r) * w_next : r.
+// if want_xn: xn = w_next ? rms_norm(r) * w_next : r.  Both norms sum in the residual-stream norm
+// order and r is formed as resid_add forms it, so a stage that ends here hands the next stage the
+// bits that the fused prologue of the following layer computes inside a single stage.
 __global__ void __launch_bounds__(256) add_norm_kernel(float *__restrict__ resid, const float *__restrict__ a,
                                                       const float *__restrict__ w_post,
                                                       const float *__restrict__ layer_scale, int want_xn,
                                                       const float *__restrict__ w_next, float *__restrict__ xn,
                                                       int dim, float eps) {
   extern __shared__ float buf[];
-  __shared__ float sh[8];
+  __shared__ float red[64];
   pdl_wait();
   pdl_launch_dependents();
   const int64_t base = int64_t(blockIdx.x) * dim;
+  const int nb = (dim + 255) / 256;
   float sc = 1.0f;
   if (w_post) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < dim; i += 256) {
-      const float v = a[base + i];
-      ss += v * v;
-    }
-    ss = block_sum<256>(ss, sh);
+    const float ss = row_sumsq<8>(nb, red, [&](int b, float (&v)[8]) { row_block8(a + base, dim, b, v); });
     sc = 1.0f / sqrtf(ss / float(dim) + eps);
   }
   const float ls = layer_scale ? layer_scale[0] : 1.0f;
-  float ss2 = 0.f;
   for (int i = threadIdx.x; i < dim; i += 256) {
-    float r = (w_post ? (a[base + i] * sc) * w_post[i] : a[base + i]) + resid[base + i];
-    if (layer_scale) r = r * ls;
+    const float r = resid_add(a[base + i], sc, w_post, w_post ? w_post[i] : 0.f, resid[base + i], layer_scale, ls);
     resid[base + i] = r;
     buf[i] = r;
-    ss2 += r * r;
   }
   if (!want_xn) return;
+  __syncthreads();
   if (!w_next) {
     for (int i = threadIdx.x; i < dim; i += 256) xn[base + i] = buf[i];
     return;
   }
-  ss2 = block_sum<256>(ss2, sh);
+  const float ss2 = row_sumsq<8>(nb, red, [&](int b, float (&v)[8]) { row_block8(buf, dim, b, v); });
   const float sc2 = 1.0f / sqrtf(ss2 / float(dim) + eps);
   for (int i = threadIdx.x; i < dim; i += 256) xn[base + i] = (buf[i] * sc2) * w_next[i];
 }

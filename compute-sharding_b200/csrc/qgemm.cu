@@ -657,7 +657,7 @@ __device__ __forceinline__ float gelu_tanh_mul_b(float v, float u) {
 __global__ void __launch_bounds__(BP_WARPS * 32) gemm_bprep_kernel(GemmPrologue P, int64_t K, int n_tok, int TN,
                                                                   uint8_t *__restrict__ img,
                                                                   float *__restrict__ meta) {
-  __shared__ float red[BP_WARPS];
+  __shared__ float red[64];
   pdl_wait();
   pdl_launch_dependents();
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -687,11 +687,7 @@ __global__ void __launch_bounds__(BP_WARPS * 32) gemm_bprep_kernel(GemmPrologue 
       ld8(P.resid_in + roff + col, rs);
       const float sc = P.scale ? P.scale[0] : 1.0f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float r = (P.w_post ? (v[e] * s1) * wp[e] : v[e]) + rs[e];
-        if (P.scale) r = r * sc;
-        v[e] = r;
-      }
+      for (int e = 0; e < 8; ++e) v[e] = resid_add(v[e], s1, P.w_post, wp[e], rs[e], P.scale, sc);
     }
     if (step == 1 || !P.w_next) return;
     float wn[8];
@@ -699,26 +695,16 @@ __global__ void __launch_bounds__(BP_WARPS * 32) gemm_bprep_kernel(GemmPrologue 
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = (v[e] * s2) * wn[e];
   };
+  // the token's sum of v^2 after `step` steps, in the residual-stream norm order (row_sumsq)
   auto cta_sumsq = [&](int step, bool store_resid) {
-    float part = 0.f;
-    for (int b = warp; b < nb; b += BP_WARPS) {
-      float v[8];
+    return row_sumsq<BP_WARPS>(nb, red, [&](int b, float (&v)[8]) {
       value8(b, step, v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) part += v[e] * v[e];
       if (store_resid) {
         float *o = P.resid_out + roff + b * QK_K + lane * 8;
         *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
         *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
       }
-    }
-    part = warp_sum(part);
-    if (lane == 0) red[warp] = part;
-    __syncthreads();
-    float sum = 0.f;
-    for (int w = 0; w < BP_WARPS; ++w) sum += red[w];
-    __syncthreads();
-    return sum;
+    });
   };
   if (valid && !P.gate && P.mode != 0) {
     if (P.mode == 1 || P.w_post) s1 = 1.0f / sqrtf(cta_sumsq(0, false) / float(K) + P.eps);
