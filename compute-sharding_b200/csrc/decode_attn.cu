@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int NST = TC ? 2 : 3;  // K/V ring stages
   __shared__ uint64_t bars[NST];
-  __shared__ float s_vec[DA_MAXG + 2][DA_MAX_HD];  // q heads, then the new k and v
+  __shared__ __align__(16) float s_vec[DA_MAXG + 2][DA_MAX_HD];  // q heads, then the new k and v
   __shared__ float s_red[DA_MAXG + 2][DA_WARPS];
   __shared__ float s_m[DA_WARPS][DA_MAXG], s_l[DA_WARPS][DA_MAXG];
   __shared__ unsigned s_last;
@@ -245,20 +245,33 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   float M[G], L[G];
   if constexpr (TC) {
     // ---- fp16 cache on the tensor pipe (mma.sync m16n8k16, fp32 accumulate), per 32-key tile:
-    //  S^T = K Qc^T   warp 0: A = the key tile (16 keys x 16 dims per MMA, ldmatrix), B = the q
-    //                 columns in registers: column 2h = hi, 2h+1 = lo of q_h * 2^u_h (fp16 keys exact,
-    //                 q to ~22 bits), so lane (g, t) holds head t's scores at keys g, g+8, 16+g, 24+g
-    //  softmax        warp 0: tile maximum and sums by shuffles, p as fp16 hi + lo into P^T (shared)
+    //  S^T = K Qc^T   every warp for its own 32 dims (two 16-dim k-steps): A = the key tile
+    //                 (ldmatrix), B = the q columns in registers: column 2h = hi, 2h+1 = lo of
+    //                 q_h * 2^u_h (fp16 keys exact, q to ~22 bits), so lane (g, t) holds head t's
+    //                 partial scores at keys g, g+8, 16+g, 24+g; the partials go to shared memory
+    //  softmax        warp 0: adds the warps' partials in warp order, running maximum and sum by
+    //                 shuffles, p as fp16 hi + lo into P^T (shared)
     //  O^T += V^T P^T every warp for its 32 dims: A = values transposed by ldmatrix, B = P^T;
     //                 O stays in fragments (column 2h + 2h+1 = head h), rescaled when the maximum moves
+    // The partial scores reuse the q rows of s_vec and its rows past the new value (four rows of
+    // 256 floats whatever G): every warp holds its q fragments and the new key's score is known
+    // before the first tile.
     const bool lane_on = lane * 8 < hd;
     __shared__ uint32_t s_pt[8][TK / 2];  // P^T as fp16 pairs [column][key pair]
     __shared__ float s_alpha[DA_MAXG], s_pnew[DA_MAXG], s_hm[DA_MAXG], s_hl[DA_MAXG];
     const int g8 = lane >> 2, t4 = lane & 3;
     for (int i = tid; i < 8 * (TK / 2); i += DA_THREADS) (&s_pt[0][0])[i] = 0u;
-    uint32_t qb[DA_MAX_HD / 16][2];
+    const int d0w = 32 * warp;  // this warp's dims for S and O
+    const bool pv = d0w < hd;   // hd is a multiple of 64
+    const int nqk = hd / 32;    // warps holding partial scores
+    auto part_slot = [&](int w) {  // warp w's 32 x float4 partials
+      const int j = w >> 1;
+      return reinterpret_cast<float4 *>(&s_vec[j < G ? j : j + 2][(w & 1) * 128]);
+    };
+    uint32_t qb[2][2];
     float rs = 1.f, m_run = -INFINITY, l_run = 0.f;  // warp 0: of head t4
-    if (warp == 0) {
+    float snew[G];
+    {
       float up[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
@@ -275,7 +288,8 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
       const int hh = g8 >> 1, part_lo = g8 & 1;  // this lane's B column: head hh, hi or lo
       const float uph = hh < G ? lt_of(up, hh < G ? hh : 0) : 0.f;
 #pragma unroll
-      for (int ks = 0; ks < DA_MAX_HD / 16; ++ks) {
+      for (int j = 0; j < 2; ++j) {
+        const int ks = 2 * warp + j;
         float x[4] = {0.f, 0.f, 0.f, 0.f};
         if (hh < G && 16 * ks < hd) {
           const float *qv = s_vec[hh] + 16 * ks + 2 * t4;
@@ -287,45 +301,59 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
 #pragma unroll
             for (int e = 0; e < 4; ++e) x[e] -= __half2float(__float2half_rn(x[e]));
         }
-        qb[ks][0] = pack_h2(x[0], x[1]);
-        qb[ks][1] = pack_h2(x[2], x[3]);
+        qb[j][0] = pack_h2(x[0], x[1]);
+        qb[j][1] = pack_h2(x[2], x[3]);
+      }
+      // the new key's score per head (owner), from the fp16-rounded key, before the q rows are reused
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float d = 0.f;
+        if (owner && warp == 0 && lane_on)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) d += s_vec[h][lane * 8 + e] * s_vec[G][lane * 8 + e];
+        snew[h] = warp_sum(d);
       }
     }
     float o[2][4];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-    const int d0w = 32 * warp;  // this warp's dims for O
-    const bool pv = d0w < hd;
-    __syncthreads();  // P^T zeroed
+    __syncthreads();  // P^T zeroed; every warp is done reading the q rows
     for (int i = 0; i < n_tiles; ++i) {
       const int st = i % NST;
       mbar_wait_bounded(&bars[st], (i / NST) & 1, err);
       const uint32_t kt = smem_u32(tiles + st * 2 * DA_TILE_BYTES), vt = kt + DA_TILE_BYTES;
       const int nk = min(TK, k_old_end - (k_begin + i * TK));
-      if (warp == 0) {
-        // two accumulators per 16-key group (even / odd k-steps): four independent MMA chains
-        float sc[2][4], sd[2][4];
+      if (pv) {
+        float sc[2][4];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) sc[mt][e] = sd[mt][e] = 0.f;
+          for (int e = 0; e < 4; ++e) sc[mt][e] = 0.f;
 #pragma unroll
-        for (int ks = 0; ks < DA_MAX_HD / 16; ++ks) {
-          if (16 * ks >= hd) break;
+        for (int j = 0; j < 2; ++j) {
+          const int ks = 2 * warp + j;
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt) {
             const int key = 16 * mt + (lane & 7) + ((lane >> 3) & 1) * 8;
             uint32_t a[4];
             ldsm_x4(kt + kv_tile_off(key, 16 * ks + (lane >> 4) * 8), a);
-            mma_f16_16816((ks & 1) ? sd[mt] : sc[mt], a, qb[ks][0], qb[ks][1]);
+            mma_f16_16816(sc[mt], a, qb[j][0], qb[j][1]);
           }
         }
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sc[mt][e] += sd[mt][e];
-        float s4[4] = {(sc[0][0] + sc[0][1]) * rs, (sc[0][2] + sc[0][3]) * rs, (sc[1][0] + sc[1][1]) * rs,
-                       (sc[1][2] + sc[1][3]) * rs};
+        part_slot(warp)[lane] =
+            make_float4(sc[0][0] + sc[0][1], sc[0][2] + sc[0][3], sc[1][0] + sc[1][1], sc[1][2] + sc[1][3]);
+      }
+      __syncthreads();  // this tile's partial scores
+      if (warp == 0) {
+        float4 acc = part_slot(0)[lane];
+        for (int w = 1; w < nqk; ++w) {
+          const float4 v = part_slot(w)[lane];
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        float s4[4] = {acc.x * rs, acc.y * rs, acc.z * rs, acc.w * rs};
         const int key4[4] = {g8, g8 + 8, 16 + g8, 24 + g8};
         float mt_ = -INFINITY;
 #pragma unroll
@@ -377,31 +405,20 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
           }
         }
       }
-      __syncthreads();  // every warp is done with this stage and with P^T
+      __syncthreads();  // every warp is done with this stage, P^T and the rescale factors
       if (tid == 0 && i + NST < n_tiles) issue(i + NST);
     }
     if (owner) {  // the new key and value, from this CTA's own (fp16-rounded) copy
-      if (warp == 0) {
-        float snew[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          float d = 0.f;
-          if (lane_on)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) d += s_vec[h][lane * 8 + e] * s_vec[G][lane * 8 + e];
-          snew[h] = warp_sum(d);
-        }
-        if (t4 < G) {
-          const float sn = lt_of(snew, t4 < G ? t4 : 0);
-          const float m_new = fmaxf(m_run, sn);
-          const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
-          const float pn = expf(sn - m_new);
-          l_run = l_run * alpha + pn;
-          m_run = m_new;
-          if (g8 == 0) {
-            s_alpha[t4] = alpha;
-            s_pnew[t4] = pn;
-          }
+      if (warp == 0 && t4 < G) {
+        const float sn = lt_of(snew, t4 < G ? t4 : 0);
+        const float m_new = fmaxf(m_run, sn);
+        const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+        const float pn = expf(sn - m_new);
+        l_run = l_run * alpha + pn;
+        m_run = m_new;
+        if (g8 == 0) {
+          s_alpha[t4] = alpha;
+          s_pnew[t4] = pn;
         }
       }
       __syncthreads();
