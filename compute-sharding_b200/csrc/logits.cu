@@ -285,11 +285,13 @@ cudaError_t scores_argmax(float *scores, int64_t n, int64_t vocab, float cap, in
                     score);
 }
 
-static int logits_ctas() { return 2 * num_sms(); }
+// CTAs of a pass over the table with T rows: four per SM for one row (63 registers a thread, so
+// 32 warps per SM keep their loads in flight), two per SM for more rows (more registers a thread).
+static int logits_ctas(int T) { return (T == 1 ? 4 : 2) * num_sms(); }
 
 size_t logits_scratch_bytes(int64_t n_tok) {
-  const int64_t T = n_tok < LOGIT_MAX_T ? n_tok : LOGIT_MAX_T;
-  return size_t(logits_ctas()) * T * 4 * sizeof(float);
+  const int T = int(n_tok < LOGIT_MAX_T ? n_tok : LOGIT_MAX_T);  // the first (widest) pass; a later
+  return size_t(logits_ctas(T)) * T * 4 * sizeof(float);         // one-row pass needs no more
 }
 
 cudaError_t logits_argmax(int type, const void *w, int64_t vocab, int dim, const float *h, int64_t n_tok, float cap,
@@ -299,9 +301,9 @@ cudaError_t logits_argmax(int type, const void *w, int64_t vocab, int dim, const
   if (vocab <= 0 || dim <= 0) return cudaErrorInvalidValue;
   if (scratch_bytes < logits_scratch_bytes(n_tok)) return cudaErrorInvalidValue;
   float *part = static_cast<float *>(scratch);
-  const int ctas = logits_ctas();
   for (int64_t t0 = 0; t0 < n_tok; t0 += LOGIT_MAX_T) {
     const int T = int(n_tok - t0 < LOGIT_MAX_T ? n_tok - t0 : LOGIT_MAX_T);
+    const int ctas = logits_ctas(T);
     const float *hx = h + t0 * dim;
     float *as = all_scores ? all_scores + t0 * vocab : nullptr;
     cudaError_t e;

@@ -18,7 +18,8 @@
 namespace sfc {
 
 // Scratch for the per-CTA (score, index) partials of the no-alloc logits path.  64 KiB covers
-// 2 CTAs per SM x 4 tokens per pass x 16 bytes on GPUs with up to 512 SMs.  Every GPU that loads
+// 2 CTAs per SM x 4 tokens per pass (or 4 CTAs per SM x 1 token) x 16 bytes on GPUs with up to
+// 512 SMs.  Every GPU that loads
 // the library holds this array until the process exits.
 constexpr size_t NOALLOC_SCRATCH_BYTES = 64 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
