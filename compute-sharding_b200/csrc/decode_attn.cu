@@ -647,7 +647,9 @@ int decode_attention_splits(int64_t n_seq, const AttnParams &p, int64_t max_keys
 // tiles does not amortise, so large batches spread their keys over about DA_CTAS_PER_SM CTAs per
 // SM instead of giving every sequence the split count of the longest one.  A sequence then takes
 // max(ceil(span / n_split), min_chunk) keys per split; n_split bounds the grid and the partials.
-constexpr int DA_CTAS_PER_SM = 4;  // measured at 64 sequences: 2 and 8 were slower
+// Measured at 64 sequences (contexts 512-3584, tensor-pipe kernel, three resident CTAs per SM):
+// 11.36 ms per step at 2, 12.06 at 3, 11.79 at 4, 11.88 at 6, 11.64 at 8.
+constexpr int DA_CTAS_PER_SM = 2;
 static void decode_attention_plan(int64_t n_seq, const AttnParams &p, int64_t max_keys, int64_t sum_keys, int *ns,
                                   int *min_chunk) {
   *ns = decode_attention_splits(n_seq, p, max_keys);
